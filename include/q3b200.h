@@ -1,0 +1,234 @@
+/*
+ * q3b200.h -- C ABI of libq3b200.so, a B200 (sm_100a) implementation of the
+ * Qwen3-0.6B Q8_0 decode hot path of abourramouss/qwen3-iree.
+ *
+ * Conventions
+ *   - Every function returns a q3 status (0 = Q3_OK).  On failure
+ *     q3_last_error() gives a one-line reason (thread-local).
+ *   - "device" pointers are CUDA device pointers owned by the caller unless a
+ *     q3_model owns them; "host" pointers are ordinary (or pinned) host memory.
+ *   - f16 tensors are IEEE binary16; Q8_0 tensors are the reference's 34-byte
+ *     blocks [f16 scale | 32 x int8] in [N, K] row-major block order
+ *     (tools/create_q8_irpa.py:103-129, :185-224), rows starting 16-byte aligned.
+ *   - `stream` is a cudaStream_t (NULL = the default stream).  Kernel entry
+ *     points only enqueue work; they never allocate and never synchronize.
+ *   - Shape or alignment violations return Q3_ERR_INVALID before any launch.
+ *
+ * The reference has no host C API: its path is an IREE module (.vmfb) driven
+ * from Python through iree.runtime (scripts/benchmark.py:34-81,
+ * scripts/chat.py:84-126), with six hand-written kernels substituted into
+ * the executable (compile.sh:34-65).  This header provides both halves:
+ *   (1) the six IREE-ABI kernels themselves (same names, same parameters,
+ *       same fixed launch grid), plus host launchers for them;
+ *   (2) a host API mirroring the module's public functions
+ *       (@run, @decode, @generate, @prefill_all, @init_chat, @chat_turn).
+ */
+#ifndef Q3B200_H
+#define Q3B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q3B200_ABI_VERSION 1
+
+/* ---------------------------------------------------------------- status */
+#define Q3_OK 0
+#define Q3_ERR_INVALID 1     /* bad argument: shape, alignment, null pointer */
+#define Q3_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define Q3_ERR_DEVICE 3      /* a kernel raised its error word (wait limit, bad token/position) */
+#define Q3_ERR_NOMEM 4       /* device or host allocation failed (model set-up only) */
+#define Q3_ERR_STATE 5       /* call out of sequence (e.g. chat turn before init) */
+#define Q3_ERR_UNSUPPORTED 6 /* no sm_100 device, or a shape this build does not cover */
+
+const char* q3_strerror(int status);
+const char* q3_last_error(void);
+int q3_abi_version(void);
+
+/* ------------------------------------------------------ device plumbing
+ * For hosts without a CUDA binding (the ctypes twins of scripts/benchmark.py
+ * and scripts/chat.py).  Thin wrappers over the CUDA runtime. */
+int q3_device_count(int* n);
+int q3_set_device(int device);
+int q3_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, size_t* total_mem);
+int q3_device_malloc(void** dptr, size_t bytes);
+int q3_device_free(void* dptr);
+int q3_host_malloc(void** hptr, size_t bytes); /* page-locked */
+int q3_host_free(void* hptr);
+int q3_memcpy_htod(void* dst, const void* src, size_t bytes, void* stream);
+int q3_memcpy_dtoh(void* dst, const void* src, size_t bytes, void* stream);
+int q3_memcpy_dtod(void* dst, const void* src, size_t bytes, void* stream);
+int q3_memset(void* dst, int value, size_t bytes, void* stream);
+int q3_stream_create(void** stream);
+int q3_stream_destroy(void* stream);
+int q3_stream_synchronize(void* stream);
+int q3_event_create(void** event);
+int q3_event_destroy(void* event);
+int q3_event_record(void* event, void* stream);
+int q3_event_elapsed_ms(void* start, void* end, float* ms);
+
+/* ------------------------------------------------------------ host math
+ * RoPE angle tables of rope_decode_q/k (model/qwen3_full.mlir:324-454):
+ * cos/sin of f32(pos) * powf(1e6, -(2i/128)), i < 64, for pos < n_pos.
+ * cos_out/sin_out: host float[n_pos * 64]. */
+int q3_rope_table(int64_t n_pos, float* cos_out, float* sin_out);
+/* Q8_0 quantizer of tools/create_q8_irpa.py:103-118 on host memory
+ * (n multiple of 32; out: n/32*34 bytes).  Used to build weights. */
+int q3_quantize_q8_0(const float* w, int64_t n, uint8_t* out);
+
+/* --------------------------------------------------- stateless kernels */
+
+/* Q8_0 fused dequant + GEMV, y[N] = W[N,K] . x[K] (f32 accumulate, f16 out),
+ * in the summation order of the reference's GPU-dialect kernels
+ * (kernels/mlir/dispatch_{3,4,12,18,20}_gpu.mlir; per block sum, then scale).
+ * Replaces q8_fused_gemv (model/qwen3_full.mlir:536-589).
+ * K multiple of 256, K <= 3072; N multiple of 8; w, x 16-byte aligned. */
+int q3_gemv_q8(const void* w, const void* x, void* y, int N, int K, void* stream);
+
+/* Same, in the CUDA kernels' order (kernels/cuda/dispatch_3.cu:33-47;
+ * per element acc += (scale*q)*x). */
+int q3_gemv_q8_cuda_order(const void* w, const void* x, void* y, int N, int K, void* stream);
+
+/* L independent GEMVs in one launch: y[l] = W_l . x[l], W_l = w + l*w_stride
+ * bytes, x: [L, K] f16, y: [L, N] f16.  The stacked-weights form of
+ * model/qwen3_full.mlir:561-566; used to measure streaming bandwidth. L <= 32. */
+int q3_gemv_q8_layers(const void* w, int64_t w_stride, const void* x, void* y, int N, int K,
+                      int L, void* stream);
+
+/* Fused variants used by the decode step (also exposed for tests):
+ *   q3_gemv_q8_norm:   y = W . rmsnorm(x, gamma)        (:779, :620-638)
+ *   q3_gemv_q8_resid:  y = r + f16(W . x)               (:739, :801-805 / :852, :858-862)
+ *   q3_gemv_q8_swiglu: y[n] = swiglu(gate_n, up_n), gate/up = rows n and
+ *                      n + N of W (2N rows), input rmsnorm(x, gamma)  (:807-839)
+ * x, r, y are f16; gamma f16[K]. */
+int q3_gemv_q8_norm(const void* w, const void* x, const void* gamma, void* y, int N, int K,
+                    void* stream);
+int q3_gemv_q8_resid(const void* w, const void* x, const void* r, void* y, int N, int K,
+                     void* stream);
+int q3_gemv_q8_swiglu(const void* w, const void* x, const void* gamma, void* y, int N, int K,
+                      void* stream);
+
+/* f16 vocab GEMV fused with the tiled argmax (model/qwen3_full.mlir:1456-1509;
+ * kernels/cuda/dispatch_24.cu): logits = W[N,1024] . rmsnorm(x, gamma)
+ * (gamma may be NULL: no norm), token = first index of the largest logit
+ * (-1 if none is above -inf).  logits (f16[N]) may be NULL.  token is a
+ * DEVICE int64.  workspace: q3_vocab_argmax_workspace_bytes() bytes of device
+ * memory, zero-filled once before first use (the kernel leaves it re-armed).
+ * N multiple of 8, K == 1024. */
+size_t q3_vocab_argmax_workspace_bytes(void);
+int q3_vocab_argmax(const void* w, const void* x, const void* gamma, void* logits,
+                    int64_t* token, void* workspace, int N, int K, void* stream);
+
+/* Decode attention for one layer (model/qwen3_full.mlir:591-748 minus the
+ * projections): QK-RMSNorm + RoPE of the raw q/k, K/V written at slot
+ * slot0 + pos of the flat caches ([slots, 8, 128] f16), then GQA attention
+ * of the 16 q heads over slots slot0 .. slot0 + pos.
+ *   qkv:    device f16 [2048 q | 1024 k | 1024 v] (raw projections)
+ *   pos:    DEVICE int64 position (pos < S and pos < rope rows)
+ *   rope_cos/rope_sin: device f32 [rope_rows, 64] (q3_rope_table)
+ *   out:    device f16 [2048]
+ *   workspace: q3_attention_workspace_bytes(S) bytes, zero-filled once. */
+size_t q3_attention_workspace_bytes(int64_t S);
+int q3_decode_attention(const void* qkv, const void* q_norm, const void* k_norm,
+                        const float* rope_cos, const float* rope_sin, int64_t rope_rows,
+                        void* k_cache, void* v_cache, int64_t slot0, int64_t S,
+                        const int64_t* pos, void* out, void* workspace, void* stream);
+
+/* ------------------------------------------------- IREE-ABI kernels
+ * The six substituted executables of compile.sh:36-42 / :58-65, compiled for
+ * sm_100a with the same export names and parameter lists
+ * (kernels/cuda/dispatch_{3,4,12,18,20,24}.cu) and the same fixed launch
+ * (grid N/8 x 256 threads, cuda/dispatch_N.mlir count()).  Numerics follow
+ * the kernels/cuda order, bit for bit.  Declared here for linkers that want
+ * the device symbols; the q3_iree_dispatch_* launchers run them on a stream:
+ *   q8_stacked / weight  binding 0, b1 binding 1 (input at a fixed offset),
+ *   b2 binding 2 (output at a fixed or pushed offset), c* push constants.
+ * Replaces: decode_dispatch_3 (attn_q), _4 (attn_k / attn_v), _12 (attn_o),
+ * _18 (ffn gate|up), _20 (ffn_down), _24 (vocab, f16 weights). */
+int q3_iree_dispatch_3(const void* q8_stacked, const void* b1, void* b2, uint32_t c0,
+                       uint32_t c1, void* stream);
+int q3_iree_dispatch_4(const void* q8_stacked, const void* b1, void* b2, uint32_t c0,
+                       uint32_t c1, uint32_t c2, void* stream);
+int q3_iree_dispatch_12(const void* q8_stacked, const void* b1, void* b2, uint32_t c0,
+                        uint32_t c1, void* stream);
+int q3_iree_dispatch_18(const void* q8_stacked, const void* b1, void* b2, uint32_t c0,
+                        uint32_t c1, void* stream);
+int q3_iree_dispatch_20(const void* q8_stacked, const void* b1, void* b2, uint32_t c0,
+                        uint32_t c1, void* stream);
+int q3_iree_dispatch_24(const void* weight, const void* b1, void* b2, uint32_t c0,
+                        void* stream);
+
+/* ------------------------------------------------------------- model
+ * Weights: device pointers in the reference's parameter layout
+ * (tools/create_q8_irpa.py:146-224, model/qwen3_full.mlir:65-79, :772-777).
+ * token_embd and output_T may be the same buffer (tied embedding). */
+typedef struct q3_weights {
+  const void* token_embd;     /* f16 [151936, 1024] */
+  const void* output_norm;    /* f16 [1024] */
+  const void* output_T;       /* f16 [151936, 1024] */
+  const void* attn_norm;      /* f16 [28, 1024]  stacked.attn_norm.weight */
+  const void* ffn_norm;       /* f16 [28, 1024]  stacked.ffn_norm.weight */
+  const void* attn_q_norm;    /* f16 [28, 128]   stacked.attn_q_norm.weight */
+  const void* attn_k_norm;    /* f16 [28, 128]   stacked.attn_k_norm.weight */
+  const void* q8_attn_q;      /* Q8_0 [28, 2228224]  stacked.q8.attn_q.weight */
+  const void* q8_attn_k;      /* Q8_0 [28, 1114112] */
+  const void* q8_attn_v;      /* Q8_0 [28, 1114112] */
+  const void* q8_attn_output; /* Q8_0 [28, 2228224] */
+  const void* q8_ffn_gate_up; /* Q8_0 [28, 6684672]  gate rows then up rows */
+  const void* q8_ffn_down;    /* Q8_0 [28, 3342336] */
+} q3_weights;
+
+typedef struct q3_model q3_model;
+
+/* Creates a decoder bound to the current device and to `stream` (NULL: the
+ * model creates its own).  Owns the KV cache for max_seq_len positions
+ * (the flat [28*S, 8, 128] layout of model/qwen3_full.mlir:212-230), the
+ * RoPE tables, activations and workspaces; the weights stay caller-owned. */
+int q3_model_create(const q3_weights* w, int64_t max_seq_len, void* stream, q3_model** out);
+int q3_model_destroy(q3_model* m);
+void* q3_model_stream(q3_model* m);
+
+/* @run (model/qwen3_full.mlir:2113-2167): ingest the prompt through the
+ * decode path (the @prefill_all route, :1541-1570), take the argmax of its
+ * last logits as the first token, then @generate (:1396-1534): tokens in
+ * groups of 4, stopping after a group whose last token is eos, or after
+ * max_gen tokens.  Like the reference, the first token is fed but not
+ * returned.  prompt/out_tokens are HOST int64 buffers (out: max_gen slots);
+ * *n_out receives the count.  n_prompt + max_gen + 1 <= max_seq_len. */
+int q3_run(q3_model* m, const int64_t* prompt, int64_t n_prompt, int64_t max_gen, int64_t eos,
+           int64_t* out_tokens, int64_t* n_out);
+
+/* @decode (model/qwen3_full.mlir:1340-1394): one step for `token` at `pos`
+ * (attending to cached positions 0..pos-1), logits f16[151936] written to
+ * the DEVICE buffer `logits` (may be NULL), argmax to *next_token (host). */
+int q3_decode(q3_model* m, int64_t token, int64_t pos, void* logits, int64_t* next_token);
+
+/* @init_chat / @chat_turn (model/qwen3_full.mlir:2172-2222): a persistent,
+ * zero-initialised cache of max_ctx positions; each turn ingests new_tokens
+ * at the current position, generates as @run does, and advances the
+ * position by n_tokens + n_out + 1, as the reference does. */
+int q3_init_chat(q3_model* m, int64_t max_ctx);
+int q3_chat_turn(q3_model* m, const int64_t* new_tokens, int64_t n_tokens, int64_t max_gen,
+                 int64_t eos, int64_t* out_tokens, int64_t* n_out);
+
+/* Step-level access for harnesses: enqueue `steps` decode steps of the
+ * generation graph without synchronising (state must have been set by
+ * q3_run or q3_generate_begin).  q3_generate_begin sets up a generation
+ * like q3_run but returns after uploading the prompt. */
+int q3_generate_begin(q3_model* m, const int64_t* prompt, int64_t n_prompt, int64_t max_gen,
+                      int64_t eos);
+int q3_generate_steps(q3_model* m, int64_t steps);
+int q3_generate_end(q3_model* m, int64_t* out_tokens, int64_t* n_out);
+
+/* Kernel launches of one generation step (for reporting). */
+int q3_model_launches_per_step(q3_model* m, int64_t* n);
+/* Device error word of the last run (0: none; see q3_strerror(Q3_ERR_DEVICE)). */
+int q3_model_device_error(q3_model* m, int* code);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q3B200_H */

@@ -1,0 +1,958 @@
+// q3_api.cu -- the C ABI of libq3b200.so (include/q3b200.h): launchers for
+// the sm_100a kernels, the IREE-ABI dispatch launchers, and the decoder
+// object that runs the reference's @run / @decode / @chat_turn semantics as
+// CUDA graphs of the fused kernels.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "q3_attn.cuh"
+#include "q3_common.cuh"
+#include "q3_gemv.cuh"
+#include "q3_iree.cuh"
+#include "q3b200.h"
+
+using namespace q3;
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+static thread_local char g_err[512] = "";
+
+static int set_err(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define Q3_CUDA(call)                                                                     \
+  do {                                                                                    \
+    cudaError_t e_ = (call);                                                              \
+    if (e_ != cudaSuccess)                                                                \
+      return set_err(Q3_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                     __FILE__, __LINE__);                                                 \
+  } while (0)
+
+#define Q3_LAUNCHED()                                                                    \
+  do {                                                                                   \
+    cudaError_t e_ = cudaGetLastError();                                                 \
+    if (e_ != cudaSuccess)                                                               \
+      return set_err(Q3_ERR_CUDA, "kernel launch failed: %s (%s:%d)",                    \
+                     cudaGetErrorString(e_), __FILE__, __LINE__);                        \
+  } while (0)
+
+#define Q3_REQUIRE(cond, ...)                              \
+  do {                                                     \
+    if (!(cond)) return set_err(Q3_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+static inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+extern "C" const char* q3_strerror(int s) {
+  switch (s) {
+    case Q3_OK: return "ok";
+    case Q3_ERR_INVALID: return "invalid argument";
+    case Q3_ERR_CUDA: return "CUDA runtime error";
+    case Q3_ERR_DEVICE: return "kernel reported an error (wait limit, bad token or position)";
+    case Q3_ERR_NOMEM: return "out of memory";
+    case Q3_ERR_STATE: return "call out of sequence";
+    case Q3_ERR_UNSUPPORTED: return "unsupported device or shape";
+    default: return "unknown status";
+  }
+}
+extern "C" const char* q3_last_error(void) { return g_err; }
+extern "C" int q3_abi_version(void) { return Q3B200_ABI_VERSION; }
+
+// ---------------------------------------------------------------------------
+// device plumbing
+// ---------------------------------------------------------------------------
+extern "C" int q3_device_count(int* n) {
+  Q3_REQUIRE(n, "n is null");
+  *n = 0;
+  cudaError_t e = cudaGetDeviceCount(n);
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) {
+    *n = 0;
+    cudaGetLastError();
+    return Q3_OK;
+  }
+  Q3_CUDA(e);
+  return Q3_OK;
+}
+extern "C" int q3_set_device(int d) {
+  Q3_CUDA(cudaSetDevice(d));
+  return Q3_OK;
+}
+extern "C" int q3_device_info(int d, int* sms, int* ccmaj, int* ccmin, size_t* mem) {
+  cudaDeviceProp p;
+  Q3_CUDA(cudaGetDeviceProperties(&p, d));
+  if (sms) *sms = p.multiProcessorCount;
+  if (ccmaj) *ccmaj = p.major;
+  if (ccmin) *ccmin = p.minor;
+  if (mem) *mem = p.totalGlobalMem;
+  return Q3_OK;
+}
+extern "C" int q3_device_malloc(void** p, size_t n) {
+  Q3_REQUIRE(p, "null out pointer");
+  cudaError_t e = cudaMalloc(p, n);
+  if (e == cudaErrorMemoryAllocation) {
+    cudaGetLastError();
+    return set_err(Q3_ERR_NOMEM, "cudaMalloc(%zu) failed", n);
+  }
+  Q3_CUDA(e);
+  return Q3_OK;
+}
+extern "C" int q3_device_free(void* p) {
+  Q3_CUDA(cudaFree(p));
+  return Q3_OK;
+}
+extern "C" int q3_host_malloc(void** p, size_t n) {
+  Q3_REQUIRE(p, "null out pointer");
+  Q3_CUDA(cudaMallocHost(p, n));
+  return Q3_OK;
+}
+extern "C" int q3_host_free(void* p) {
+  Q3_CUDA(cudaFreeHost(p));
+  return Q3_OK;
+}
+extern "C" int q3_memcpy_htod(void* d, const void* s, size_t n, void* st) {
+  Q3_CUDA(cudaMemcpyAsync(d, s, n, cudaMemcpyHostToDevice, (cudaStream_t)st));
+  return Q3_OK;
+}
+extern "C" int q3_memcpy_dtoh(void* d, const void* s, size_t n, void* st) {
+  Q3_CUDA(cudaMemcpyAsync(d, s, n, cudaMemcpyDeviceToHost, (cudaStream_t)st));
+  return Q3_OK;
+}
+extern "C" int q3_memcpy_dtod(void* d, const void* s, size_t n, void* st) {
+  Q3_CUDA(cudaMemcpyAsync(d, s, n, cudaMemcpyDeviceToDevice, (cudaStream_t)st));
+  return Q3_OK;
+}
+extern "C" int q3_memset(void* d, int v, size_t n, void* st) {
+  Q3_CUDA(cudaMemsetAsync(d, v, n, (cudaStream_t)st));
+  return Q3_OK;
+}
+extern "C" int q3_stream_create(void** s) {
+  Q3_REQUIRE(s, "null out pointer");
+  cudaStream_t t;
+  Q3_CUDA(cudaStreamCreateWithFlags(&t, cudaStreamNonBlocking));
+  *s = t;
+  return Q3_OK;
+}
+extern "C" int q3_stream_destroy(void* s) {
+  Q3_CUDA(cudaStreamDestroy((cudaStream_t)s));
+  return Q3_OK;
+}
+extern "C" int q3_stream_synchronize(void* s) {
+  Q3_CUDA(cudaStreamSynchronize((cudaStream_t)s));
+  return Q3_OK;
+}
+extern "C" int q3_event_create(void** e) {
+  Q3_REQUIRE(e, "null out pointer");
+  cudaEvent_t t;
+  Q3_CUDA(cudaEventCreate(&t));
+  *e = t;
+  return Q3_OK;
+}
+extern "C" int q3_event_destroy(void* e) {
+  Q3_CUDA(cudaEventDestroy((cudaEvent_t)e));
+  return Q3_OK;
+}
+extern "C" int q3_event_record(void* e, void* s) {
+  Q3_CUDA(cudaEventRecord((cudaEvent_t)e, (cudaStream_t)s));
+  return Q3_OK;
+}
+extern "C" int q3_event_elapsed_ms(void* a, void* b, float* ms) {
+  Q3_REQUIRE(ms, "null out pointer");
+  Q3_CUDA(cudaEventElapsedTime(ms, (cudaEvent_t)a, (cudaEvent_t)b));
+  return Q3_OK;
+}
+
+// ---------------------------------------------------------------------------
+// host math
+// ---------------------------------------------------------------------------
+extern "C" int q3_rope_table(int64_t n_pos, float* c, float* s) {
+  Q3_REQUIRE(n_pos >= 0 && c && s, "bad rope table arguments");
+  for (int64_t p = 0; p < n_pos; ++p) {
+    const float pf = (float)(int32_t)p;
+    for (int i = 0; i < 64; ++i) {
+      const float e = -((2.0f * (float)i) / 128.0f);
+      const float th = powf(1.0e6f, e) * 1.0f;
+      const float a = pf * th;
+      c[p * 64 + i] = cosf(a);
+      s[p * 64 + i] = sinf(a);
+    }
+  }
+  return Q3_OK;
+}
+
+static void quantize_range(const float* w, uint8_t* out, int64_t b0, int64_t b1) {
+  for (int64_t b = b0; b < b1; ++b) {
+    const float* blk = w + b * kQBlk;
+    float amax = 0.0f;
+    for (int j = 0; j < kQBlk; ++j) amax = std::fmax(amax, std::fabs(blk[j]));
+    float scale = amax / 127.0f;
+    if (scale == 0.0f) scale = 1.0f;
+    const __half hs = __float2half_rn(scale);
+    uint16_t sh;
+    memcpy(&sh, &hs, 2);
+    uint8_t* o = out + b * kQBytes;
+    o[0] = (uint8_t)(sh & 0xff);
+    o[1] = (uint8_t)(sh >> 8);
+    for (int j = 0; j < kQBlk; ++j) {
+      float q = std::nearbyint(blk[j] / scale);
+      q = q < -128.0f ? -128.0f : (q > 127.0f ? 127.0f : q);
+      o[2 + j] = (uint8_t)(int8_t)q;
+    }
+  }
+}
+
+extern "C" int q3_quantize_q8_0(const float* w, int64_t n, uint8_t* out) {
+  Q3_REQUIRE(w && out && n >= 0 && n % kQBlk == 0, "quantize: n must be a multiple of 32");
+  const int64_t nb = n / kQBlk;
+  unsigned nt = std::thread::hardware_concurrency();
+  if (nt == 0) nt = 1;
+  if (nb < 65536) nt = 1;
+  std::vector<std::thread> th;
+  for (unsigned t = 0; t < nt; ++t)
+    th.emplace_back(quantize_range, w, out, nb * t / nt, nb * (t + 1) / nt);
+  for (auto& t : th) t.join();
+  return Q3_OK;
+}
+
+// ---------------------------------------------------------------------------
+// launch helpers
+// ---------------------------------------------------------------------------
+static int current_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = v > 0 ? v : 148;
+  }
+  return cache[dev];
+}
+
+constexpr size_t kMaxDynSmem = 200 * 1024;
+static std::mutex g_attr_mu;
+
+template <typename F>
+static int ensure_smem_attr(F* fn, size_t bytes) {
+  // cudaFuncSetAttribute is per device; set the cap once per (function, device).
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  if (dev >= 0 && dev < 64 && done[dev]) return Q3_OK;
+  (void)bytes;
+  Q3_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDynSmem));
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return Q3_OK;
+}
+
+struct LaunchShape {
+  int grid, nstages;
+  size_t smem;
+};
+
+static LaunchShape stream_shape(int ntiles, uint32_t tile_bytes, int ctas_per_sm_stream) {
+  const int sms = current_sms();
+  LaunchShape s;
+  if (ntiles <= 4 * sms) {
+    s.grid = ntiles > 0 ? ntiles : 1;
+    s.nstages = 1;
+  } else {
+    s.grid = ctas_per_sm_stream * sms;
+    const int tpc = (ntiles + s.grid - 1) / s.grid;
+    const size_t budget = (size_t)(kMaxDynSmem / ctas_per_sm_stream) - 1024;
+    int ns = (int)(budget / tile_bytes);
+    if (ns < 1) ns = 1;
+    if (ns > 16) ns = 16;
+    if (ns > tpc) ns = tpc;
+    s.nstages = ns;
+  }
+  s.smem = ring_smem_bytes(s.nstages, tile_bytes);
+  return s;
+}
+
+template <int G, int ORDER, int MODE>
+static int launch_q8_t(Q8GemvArgs a, cudaStream_t st, int* launches) {
+  const uint32_t rowbytes = (uint32_t)(a.K / kQBlk) * kQBytes;
+  const uint32_t tile_bytes = rowbytes * kTileRows * (MODE == kModeSwiglu ? 2u : 1u);
+  const int ntiles = a.nseg * (a.seg_rows / kTileRows);
+  LaunchShape ls = stream_shape(ntiles, tile_bytes, 2);
+  a.nstages = ls.nstages;
+  int rc = ensure_smem_attr(k_gemv_q8<G, ORDER, MODE>, ls.smem);
+  if (rc) return rc;
+  k_gemv_q8<G, ORDER, MODE><<<ls.grid, kGemvThreads, ls.smem, st>>>(a);
+  Q3_LAUNCHED();
+  if (launches) ++*launches;
+  return Q3_OK;
+}
+
+template <int ORDER, int MODE>
+static int launch_q8(const Q8GemvArgs& a, cudaStream_t st, int* launches) {
+  switch ((a.K + 1023) / 1024) {
+    case 1: return launch_q8_t<1, ORDER, MODE>(a, st, launches);
+    case 2: return launch_q8_t<2, ORDER, MODE>(a, st, launches);
+    case 3: return launch_q8_t<3, ORDER, MODE>(a, st, launches);
+    default: return set_err(Q3_ERR_UNSUPPORTED, "K=%d above 3072", a.K);
+  }
+}
+
+static int check_q8_shape(const void* w, const void* x, const void* y, int N, int K) {
+  Q3_REQUIRE(w && x && y, "null pointer");
+  Q3_REQUIRE(K > 0 && K % 256 == 0 && K <= 3072, "K=%d must be a multiple of 256, <= 3072", K);
+  Q3_REQUIRE(N > 0 && N % 8 == 0, "N=%d must be a positive multiple of 8", N);
+  Q3_REQUIRE(aligned16(w) && aligned16(x), "w and x must be 16-byte aligned");
+  return Q3_OK;
+}
+
+static Q8GemvArgs q8_args_single(const void* w, const void* x, void* y, const void* r, int N,
+                                 int K) {
+  Q8GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.seg[0].w = (const uint8_t*)w;
+  a.seg[0].x = (const uint16_t*)x;
+  a.seg[0].y = (uint16_t*)y;
+  a.seg[0].r = (const uint16_t*)r;
+  a.nseg = 1;
+  a.seg_rows = N;
+  a.K = K;
+  return a;
+}
+
+extern "C" int q3_gemv_q8(const void* w, const void* x, void* y, int N, int K, void* stream) {
+  int rc = check_q8_shape(w, x, y, N, K);
+  if (rc) return rc;
+  return launch_q8<kOrderMlir, kModePlain>(q8_args_single(w, x, y, nullptr, N, K),
+                                          (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int q3_gemv_q8_cuda_order(const void* w, const void* x, void* y, int N, int K,
+                                     void* stream) {
+  int rc = check_q8_shape(w, x, y, N, K);
+  if (rc) return rc;
+  return launch_q8<kOrderCuda, kModePlain>(q8_args_single(w, x, y, nullptr, N, K),
+                                          (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int q3_gemv_q8_layers(const void* w, int64_t w_stride, const void* x, void* y, int N,
+                                 int K, int L, void* stream) {
+  int rc = check_q8_shape(w, x, y, N, K);
+  if (rc) return rc;
+  Q3_REQUIRE(L >= 1 && L <= kMaxSeg, "L=%d must be in [1, %d]", L, kMaxSeg);
+  Q3_REQUIRE(w_stride % 16 == 0, "w_stride must be a multiple of 16");
+  Q8GemvArgs a = q8_args_single(w, x, y, nullptr, N, K);
+  a.nseg = L;
+  for (int l = 0; l < L; ++l) {
+    a.seg[l].w = (const uint8_t*)w + (int64_t)l * w_stride;
+    a.seg[l].x = (const uint16_t*)x + (int64_t)l * K;
+    a.seg[l].y = (uint16_t*)y + (int64_t)l * N;
+  }
+  return launch_q8<kOrderMlir, kModePlain>(a, (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int q3_gemv_q8_norm(const void* w, const void* x, const void* gamma, void* y, int N,
+                               int K, void* stream) {
+  int rc = check_q8_shape(w, x, y, N, K);
+  if (rc) return rc;
+  Q3_REQUIRE(gamma, "gamma is null");
+  Q8GemvArgs a = q8_args_single(w, x, y, nullptr, N, K);
+  a.norm_g = (const uint16_t*)gamma;
+  return launch_q8<kOrderMlir, kModeNormIn>(a, (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int q3_gemv_q8_resid(const void* w, const void* x, const void* r, void* y, int N,
+                                int K, void* stream) {
+  int rc = check_q8_shape(w, x, y, N, K);
+  if (rc) return rc;
+  Q3_REQUIRE(r, "r is null");
+  return launch_q8<kOrderMlir, kModeResid>(q8_args_single(w, x, y, r, N, K),
+                                          (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int q3_gemv_q8_swiglu(const void* w, const void* x, const void* gamma, void* y, int N,
+                                 int K, void* stream) {
+  int rc = check_q8_shape(w, x, y, N, K);
+  if (rc) return rc;
+  Q3_REQUIRE(gamma, "gamma is null");
+  Q8GemvArgs a = q8_args_single(w, x, y, nullptr, N, K);
+  a.norm_g = (const uint16_t*)gamma;
+  a.up_off_bytes = (int64_t)N * (K / kQBlk) * kQBytes;
+  return launch_q8<kOrderMlir, kModeSwiglu>(a, (cudaStream_t)stream, nullptr);
+}
+
+// vocab + argmax ------------------------------------------------------------
+constexpr int kArgmaxMaxGrid = 4096;
+extern "C" size_t q3_vocab_argmax_workspace_bytes(void) {
+  return sizeof(ArgmaxPartial) * kArgmaxMaxGrid + 256;
+}
+
+static int launch_vocab(VocabArgs a, cudaStream_t st, int* launches) {
+  const uint32_t tile_bytes = (uint32_t)a.K * 2u * kTileRows;
+  LaunchShape ls = stream_shape(a.N / kTileRows, tile_bytes, 2);
+  if (ls.grid > kArgmaxMaxGrid) ls.grid = kArgmaxMaxGrid;
+  a.nstages = ls.nstages;
+  int rc = ensure_smem_attr(k_vocab_argmax, ls.smem);
+  if (rc) return rc;
+  k_vocab_argmax<<<ls.grid, kGemvThreads, ls.smem, st>>>(a);
+  Q3_LAUNCHED();
+  if (launches) ++*launches;
+  return Q3_OK;
+}
+
+extern "C" int q3_vocab_argmax(const void* w, const void* x, const void* gamma, void* logits,
+                               int64_t* token, void* ws, int N, int K, void* stream) {
+  Q3_REQUIRE(w && x && token && ws, "null pointer");
+  Q3_REQUIRE(K == kVocabK, "K=%d: this build covers K == 1024", K);
+  Q3_REQUIRE(N > 0 && N % 8 == 0, "N=%d must be a positive multiple of 8", N);
+  Q3_REQUIRE(aligned16(w) && aligned16(ws), "w and workspace must be 16-byte aligned");
+  VocabArgs a;
+  memset(&a, 0, sizeof(a));
+  a.w = (const uint16_t*)w;
+  a.x = (const uint16_t*)x;
+  a.norm_g = (const uint16_t*)gamma;
+  a.logits = (uint16_t*)logits;
+  a.N = N;
+  a.K = K;
+  a.partial = (ArgmaxPartial*)ws;
+  a.counter = (unsigned int*)((uint8_t*)ws + sizeof(ArgmaxPartial) * kArgmaxMaxGrid);
+  a.token_out = token;
+  return launch_vocab(a, (cudaStream_t)stream, nullptr);
+}
+
+// attention -----------------------------------------------------------------
+static int max_splits_for(int64_t S) { return (int)((S + kAttSplit - 1) / kAttSplit); }
+
+extern "C" size_t q3_attention_workspace_bytes(int64_t S) {
+  const int ms = max_splits_for(S < 1 ? 1 : S);
+  return sizeof(AttnPartial) * (size_t)kNKV * ms * 2 + 256;
+}
+
+static int launch_attn(const AttnArgs& a, int batch, cudaStream_t st, int* launches) {
+  dim3 grid(kNKV, a.max_splits, batch);
+  k_attn_decode<<<grid, 256, 0, st>>>(a);
+  Q3_LAUNCHED();
+  if (launches) ++*launches;
+  return Q3_OK;
+}
+
+extern "C" int q3_decode_attention(const void* qkv, const void* q_norm, const void* k_norm,
+                                   const float* rope_cos, const float* rope_sin, int64_t rope_rows,
+                                   void* kc, void* vc, int64_t slot0, int64_t S, const int64_t* pos,
+                                   void* out, void* ws, void* stream) {
+  Q3_REQUIRE(qkv && q_norm && k_norm && rope_cos && rope_sin && kc && vc && pos && out && ws,
+             "null pointer");
+  Q3_REQUIRE(S >= 1 && slot0 >= 0 && rope_rows >= 1, "bad S / slot0 / rope_rows");
+  Q3_REQUIRE(aligned16(qkv) && aligned16(kc) && aligned16(vc) && aligned16(ws),
+             "qkv, caches and workspace must be 16-byte aligned");
+  AttnArgs a;
+  memset(&a, 0, sizeof(a));
+  a.qkv = (const uint16_t*)qkv;
+  a.q_norm = (const uint16_t*)q_norm;
+  a.k_norm = (const uint16_t*)k_norm;
+  a.rope_cos = rope_cos;
+  a.rope_sin = rope_sin;
+  a.rope_pos = rope_rows;
+  a.kc = (uint16_t*)kc;
+  a.vc = (uint16_t*)vc;
+  a.slot0 = slot0;
+  a.S = S;
+  a.pos = pos;
+  a.pos_stride = 1;
+  a.out = (uint16_t*)out;
+  a.max_splits = max_splits_for(S);
+  a.part = (AttnPartial*)ws;
+  a.counters = (unsigned int*)((uint8_t*)ws + sizeof(AttnPartial) * (size_t)kNKV * a.max_splits * 2);
+  return launch_attn(a, 1, (cudaStream_t)stream, nullptr);
+}
+
+// IREE-ABI dispatch launchers --------------------------------------------------
+#define Q3_IREE_CHECK(w, b1, b2)                                                  \
+  Q3_REQUIRE((w) && (b1) && (b2), "null binding");                                \
+  Q3_REQUIRE(aligned16(w) && aligned16(b1), "bindings 0 and 1 must be 16-byte aligned")
+
+extern "C" int q3_iree_dispatch_3(const void* q8, const void* b1, void* b2, uint32_t c0,
+                                  uint32_t c1, void* stream) {
+  Q3_IREE_CHECK(q8, b1, b2);
+  decode_dispatch_3_matmul_2048x1x1024_f16<<<256, 256, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)q8, (const char*)b1, (char*)b2, c0, c1);
+  Q3_LAUNCHED();
+  return Q3_OK;
+}
+extern "C" int q3_iree_dispatch_4(const void* q8, const void* b1, void* b2, uint32_t c0,
+                                  uint32_t c1, uint32_t c2, void* stream) {
+  Q3_IREE_CHECK(q8, b1, b2);
+  decode_dispatch_4_matmul_1024x1x1024_f16<<<128, 256, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)q8, (const char*)b1, (char*)b2, c0, c1, c2);
+  Q3_LAUNCHED();
+  return Q3_OK;
+}
+extern "C" int q3_iree_dispatch_12(const void* q8, const void* b1, void* b2, uint32_t c0,
+                                   uint32_t c1, void* stream) {
+  Q3_IREE_CHECK(q8, b1, b2);
+  decode_dispatch_12_matmul_1024x1x2048_f16<<<128, 256, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)q8, (const char*)b1, (char*)b2, c0, c1);
+  Q3_LAUNCHED();
+  return Q3_OK;
+}
+extern "C" int q3_iree_dispatch_18(const void* q8, const void* b1, void* b2, uint32_t c0,
+                                   uint32_t c1, void* stream) {
+  Q3_IREE_CHECK(q8, b1, b2);
+  decode_dispatch_18_matmul_6144x1x1024_f16<<<768, 256, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)q8, (const char*)b1, (char*)b2, c0, c1);
+  Q3_LAUNCHED();
+  return Q3_OK;
+}
+extern "C" int q3_iree_dispatch_20(const void* q8, const void* b1, void* b2, uint32_t c0,
+                                   uint32_t c1, void* stream) {
+  Q3_IREE_CHECK(q8, b1, b2);
+  decode_dispatch_20_matmul_1024x1x3072_f16<<<128, 256, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)q8, (const char*)b1, (char*)b2, c0, c1);
+  Q3_LAUNCHED();
+  return Q3_OK;
+}
+extern "C" int q3_iree_dispatch_24(const void* w, const void* b1, void* b2, uint32_t c0,
+                                   void* stream) {
+  Q3_IREE_CHECK(w, b1, b2);
+  decode_dispatch_24_matmul_151936x1x1024_f16<<<18992, 256, 0, (cudaStream_t)stream>>>(
+      (const __half*)w, (const char*)b1, (char*)b2, c0);
+  Q3_LAUNCHED();
+  return Q3_OK;
+}
+
+// ---------------------------------------------------------------------------
+// decoder object
+// ---------------------------------------------------------------------------
+struct q3_model {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  q3_weights w{};
+  int64_t S = 0;
+  // owned device memory
+  uint16_t *kc = nullptr, *vc = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  uint16_t *x = nullptr, *qkv = nullptr, *attn = nullptr, *h1 = nullptr, *act = nullptr,
+           *logits = nullptr;
+  int64_t* tokens = nullptr;  // [S + 1]: token at each position
+  SeqState* st = nullptr;
+  ArgmaxPartial* am_part = nullptr;
+  unsigned int* am_counter = nullptr;
+  AttnPartial* att_part = nullptr;
+  unsigned int* att_counters = nullptr;
+  int* err = nullptr;
+  // pinned host staging
+  SeqState* h_st = nullptr;
+  int64_t* h_tokens = nullptr;
+  // graphs
+  cudaGraphExec_t g_ingest = nullptr, g_gen = nullptr;
+  int launches_gen = 0, launches_ingest = 0;
+  // generation bookkeeping
+  int64_t gen_n_prompt = 0, gen_pos0 = 0, gen_max = 0;
+  bool gen_active = false;
+  // chat
+  bool chat_ready = false;
+  int64_t chat_pos = 0, chat_max = 0;
+};
+
+static int enqueue_layers(q3_model* m, bool ingest, int* launches) {
+  cudaStream_t st = m->stream;
+  const int32_t* stop = &m->st->stop;
+  for (int l = 0; l < kLayers; ++l) {
+    // 1) RMSNorm + Q|K|V projections (layer 0 also gathers the embedding)
+    Q8GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    const uint8_t* wq = (const uint8_t*)m->w.q8_attn_q + l * kBplQ;
+    const uint8_t* wk = (const uint8_t*)m->w.q8_attn_k + l * kBplKV;
+    const uint8_t* wv = (const uint8_t*)m->w.q8_attn_v + l * kBplKV;
+    const int64_t rb = 1088;
+    a.seg[0] = {wq, m->x, m->qkv, nullptr};
+    a.seg[1] = {wq + 1024 * rb, m->x, m->qkv + 1024, nullptr};
+    a.seg[2] = {wk, m->x, m->qkv + 2048, nullptr};
+    a.seg[3] = {wv, m->x, m->qkv + 3072, nullptr};
+    a.nseg = 4;
+    a.seg_rows = 1024;
+    a.K = 1024;
+    a.norm_g = (const uint16_t*)m->w.attn_norm + l * kDim;
+    a.seq = m->st;
+    a.err = m->err;
+    if (l == 0) {
+      a.tokens = m->tokens;
+      a.embd = (const uint16_t*)m->w.token_embd;
+      a.embed_out = m->x;
+    }
+    int rc = launch_q8<kOrderMlir, kModeNormIn>(a, st, launches);
+    if (rc) return rc;
+    // 2) QK-norm + RoPE + KV write + attention
+    AttnArgs t;
+    memset(&t, 0, sizeof(t));
+    t.qkv = m->qkv;
+    t.q_norm = (const uint16_t*)m->w.attn_q_norm + l * kHD;
+    t.k_norm = (const uint16_t*)m->w.attn_k_norm + l * kHD;
+    t.rope_cos = m->rope_cos;
+    t.rope_sin = m->rope_sin;
+    t.rope_pos = m->S;
+    t.kc = m->kc;
+    t.vc = m->vc;
+    t.slot0 = (int64_t)l * m->S;
+    t.S = m->S;
+    t.pos = &m->st->pos;
+    t.pos_stride = 1;
+    t.stop = stop;
+    t.out = m->attn;
+    t.max_splits = max_splits_for(m->S);
+    t.part = m->att_part;
+    t.counters = m->att_counters;
+    t.err = m->err;
+    rc = launch_attn(t, 1, st, launches);
+    if (rc) return rc;
+    // 3) O projection + residual: h1 = x + W_o . attn
+    a = q8_args_single((const uint8_t*)m->w.q8_attn_output + l * kBplO, m->attn, m->h1, m->x,
+                       1024, 2048);
+    a.seq = m->st;
+    a.err = m->err;
+    rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches);
+    if (rc) return rc;
+    // 4) RMSNorm + gate|up + SwiGLU: act = swiglu(W_gu . rmsnorm(h1))
+    a = q8_args_single((const uint8_t*)m->w.q8_ffn_gate_up + l * kBplGU, m->h1, m->act, nullptr,
+                       3072, 1024);
+    a.norm_g = (const uint16_t*)m->w.ffn_norm + l * kDim;
+    a.up_off_bytes = 3072 * rb;
+    a.seq = m->st;
+    a.err = m->err;
+    rc = launch_q8<kOrderMlir, kModeSwiglu>(a, st, launches);
+    if (rc) return rc;
+    // 5) down projection + residual: x = h1 + W_d . act
+    a = q8_args_single((const uint8_t*)m->w.q8_ffn_down + l * kBplD, m->act, m->x, m->h1, 1024,
+                       3072);
+    a.seq = m->st;
+    a.err = m->err;
+    if (ingest && l == kLayers - 1) a.advance = m->st;
+    rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches);
+    if (rc) return rc;
+  }
+  return Q3_OK;
+}
+
+static int enqueue_vocab(q3_model* m, int* launches) {
+  VocabArgs v;
+  memset(&v, 0, sizeof(v));
+  v.w = (const uint16_t*)m->w.output_T;
+  v.x = m->x;
+  v.norm_g = (const uint16_t*)m->w.output_norm;
+  v.logits = m->logits;
+  v.N = kVocab;
+  v.K = kDim;
+  v.partial = m->am_part;
+  v.counter = m->am_counter;
+  v.seq = m->st;
+  v.tokens = m->tokens;
+  v.err = m->err;
+  return launch_vocab(v, m->stream, launches);
+}
+
+static int capture(q3_model* m, bool ingest, cudaGraphExec_t* out, int* launches) {
+  cudaGraph_t g = nullptr;
+  Q3_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  int n = 0;
+  int rc = enqueue_layers(m, ingest, &n);
+  if (rc == Q3_OK && !ingest) rc = enqueue_vocab(m, &n);
+  cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  Q3_CUDA(e);
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  Q3_CUDA(e);
+  *launches = n;
+  return Q3_OK;
+}
+
+static void model_free(q3_model* m) {
+  if (!m) return;
+  if (m->g_ingest) cudaGraphExecDestroy(m->g_ingest);
+  if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
+  void* dev[] = {m->kc, m->vc, m->rope_cos, m->rope_sin, m->x, m->qkv, m->attn, m->h1, m->act,
+                 m->logits, m->tokens, m->st, m->am_part, m->att_part, m->err};
+  for (void* p : dev)
+    if (p) cudaFree(p);
+  if (m->h_st) cudaFreeHost(m->h_st);
+  if (m->h_tokens) cudaFreeHost(m->h_tokens);
+  if (m->own_stream && m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+#define Q3_MALLOC(ptr, bytes)                                                        \
+  do {                                                                               \
+    cudaError_t e_ = cudaMalloc((void**)&(ptr), (bytes));                            \
+    if (e_ != cudaSuccess) {                                                         \
+      cudaGetLastError();                                                            \
+      model_free(m);                                                                 \
+      return set_err(Q3_ERR_NOMEM, "cudaMalloc(%zu) for %s failed: %s", (size_t)(bytes), \
+                     #ptr, cudaGetErrorString(e_));                                  \
+    }                                                                                \
+  } while (0)
+
+extern "C" int q3_model_create(const q3_weights* w, int64_t S, void* stream, q3_model** out) {
+  Q3_REQUIRE(w && out, "null pointer");
+  Q3_REQUIRE(S >= 2 && S <= (1 << 20), "max_seq_len=%lld out of range", (long long)S);
+  const void* req[] = {w->token_embd, w->output_norm, w->output_T, w->attn_norm, w->ffn_norm,
+                       w->attn_q_norm, w->attn_k_norm, w->q8_attn_q, w->q8_attn_k, w->q8_attn_v,
+                       w->q8_attn_output, w->q8_ffn_gate_up, w->q8_ffn_down};
+  for (const void* p : req) {
+    Q3_REQUIRE(p != nullptr, "a weight pointer is null");
+    Q3_REQUIRE(aligned16(p), "weight pointers must be 16-byte aligned");
+  }
+  int dev = 0;
+  Q3_CUDA(cudaGetDevice(&dev));
+  int major = 0;
+  Q3_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+  if (major != 10) return set_err(Q3_ERR_UNSUPPORTED, "device %d is sm_%d0; this build is sm_100a", dev, major);
+  q3_model* m = new q3_model();
+  m->device = dev;
+  m->w = *w;
+  m->S = S;
+  if (stream) {
+    m->stream = (cudaStream_t)stream;
+  } else {
+    cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+      model_free(m);
+      return set_err(Q3_ERR_CUDA, "stream create: %s", cudaGetErrorString(e));
+    }
+    m->own_stream = true;
+  }
+  const size_t cache = (size_t)kLayers * S * kNKV * kHD * sizeof(uint16_t);
+  Q3_MALLOC(m->kc, cache);
+  Q3_MALLOC(m->vc, cache);
+  Q3_MALLOC(m->rope_cos, (size_t)S * 64 * sizeof(float));
+  Q3_MALLOC(m->rope_sin, (size_t)S * 64 * sizeof(float));
+  Q3_MALLOC(m->x, kDim * 2);
+  Q3_MALLOC(m->qkv, 4096 * 2);
+  Q3_MALLOC(m->attn, 2048 * 2);
+  Q3_MALLOC(m->h1, kDim * 2);
+  Q3_MALLOC(m->act, kFFN * 2);
+  Q3_MALLOC(m->logits, (size_t)kVocab * 2);
+  Q3_MALLOC(m->tokens, (size_t)(S + 1) * sizeof(int64_t));
+  Q3_MALLOC(m->st, sizeof(SeqState));
+  Q3_MALLOC(m->am_part, q3_vocab_argmax_workspace_bytes());
+  m->am_counter = (unsigned int*)((uint8_t*)m->am_part + sizeof(ArgmaxPartial) * kArgmaxMaxGrid);
+  Q3_MALLOC(m->att_part, q3_attention_workspace_bytes(S));
+  m->att_counters = (unsigned int*)((uint8_t*)m->att_part +
+                                    sizeof(AttnPartial) * (size_t)kNKV * max_splits_for(S) * 2);
+  Q3_MALLOC(m->err, sizeof(int));
+  if (cudaMallocHost((void**)&m->h_st, sizeof(SeqState)) != cudaSuccess ||
+      cudaMallocHost((void**)&m->h_tokens, (size_t)(S + 1) * sizeof(int64_t)) != cudaSuccess) {
+    cudaGetLastError();
+    model_free(m);
+    return set_err(Q3_ERR_NOMEM, "pinned host allocation failed");
+  }
+  std::vector<float> c((size_t)S * 64), s((size_t)S * 64);
+  q3_rope_table(S, c.data(), s.data());
+  int rc = Q3_OK;
+  auto chk = [&](cudaError_t e) {
+    if (e != cudaSuccess && rc == Q3_OK)
+      rc = set_err(Q3_ERR_CUDA, "model init: %s", cudaGetErrorString(e));
+  };
+  chk(cudaMemcpyAsync(m->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice, m->stream));
+  chk(cudaMemcpyAsync(m->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice, m->stream));
+  chk(cudaMemsetAsync(m->am_part, 0, q3_vocab_argmax_workspace_bytes(), m->stream));
+  chk(cudaMemsetAsync(m->att_part, 0, q3_attention_workspace_bytes(S), m->stream));
+  chk(cudaMemsetAsync(m->err, 0, sizeof(int), m->stream));
+  chk(cudaMemsetAsync(m->st, 0, sizeof(SeqState), m->stream));
+  chk(cudaMemsetAsync(m->tokens, 0, (size_t)(S + 1) * sizeof(int64_t), m->stream));
+  chk(cudaStreamSynchronize(m->stream));
+  if (rc == Q3_OK) rc = capture(m, true, &m->g_ingest, &m->launches_ingest);
+  if (rc == Q3_OK) rc = capture(m, false, &m->g_gen, &m->launches_gen);
+  if (rc != Q3_OK) {
+    model_free(m);
+    return rc;
+  }
+  *out = m;
+  return Q3_OK;
+}
+
+extern "C" int q3_model_destroy(q3_model* m) {
+  if (m) {
+    cudaStreamSynchronize(m->stream);
+    model_free(m);
+  }
+  return Q3_OK;
+}
+
+extern "C" void* q3_model_stream(q3_model* m) { return m ? (void*)m->stream : nullptr; }
+
+extern "C" int q3_model_launches_per_step(q3_model* m, int64_t* n) {
+  Q3_REQUIRE(m && n, "null pointer");
+  *n = m->launches_gen;
+  return Q3_OK;
+}
+
+extern "C" int q3_model_device_error(q3_model* m, int* code) {
+  Q3_REQUIRE(m && code, "null pointer");
+  Q3_CUDA(cudaMemcpyAsync(code, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+  Q3_CUDA(cudaStreamSynchronize(m->stream));
+  return Q3_OK;
+}
+
+// Upload tokens at positions [pos0, pos0+n) and a fresh sequence state.
+static int seq_begin(q3_model* m, const int64_t* toks, int64_t pos0, int64_t n, int64_t n_prompt,
+                     int64_t max_gen, int64_t eos) {
+  memcpy(m->h_tokens, toks, (size_t)n * sizeof(int64_t));
+  Q3_CUDA(cudaMemcpyAsync(m->tokens + pos0, m->h_tokens, (size_t)n * sizeof(int64_t),
+                          cudaMemcpyHostToDevice, m->stream));
+  SeqState s;
+  memset(&s, 0, sizeof(s));
+  s.pos = pos0;
+  s.n_prompt = n_prompt;
+  s.max_gen = max_gen;
+  s.eos = eos;
+  s.stop = 0;
+  *m->h_st = s;
+  Q3_CUDA(cudaMemcpyAsync(m->st, m->h_st, sizeof(SeqState), cudaMemcpyHostToDevice, m->stream));
+  Q3_CUDA(cudaMemsetAsync(m->err, 0, sizeof(int), m->stream));
+  return Q3_OK;
+}
+
+static int launch_graphs(q3_model* m, int64_t n_ingest, int64_t n_gen) {
+  for (int64_t i = 0; i < n_ingest; ++i) Q3_CUDA(cudaGraphLaunch(m->g_ingest, m->stream));
+  for (int64_t i = 0; i < n_gen; ++i) Q3_CUDA(cudaGraphLaunch(m->g_gen, m->stream));
+  return Q3_OK;
+}
+
+static int check_device_err(q3_model* m) {
+  int code = 0;
+  Q3_CUDA(cudaMemcpyAsync(&code, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+  Q3_CUDA(cudaStreamSynchronize(m->stream));
+  if (code != 0) return set_err(Q3_ERR_DEVICE, "kernel error word %d", code);
+  return Q3_OK;
+}
+
+extern "C" int q3_generate_begin(q3_model* m, const int64_t* prompt, int64_t n_prompt,
+                                 int64_t max_gen, int64_t eos) {
+  Q3_REQUIRE(m && prompt, "null pointer");
+  Q3_REQUIRE(n_prompt >= 1, "the prompt must hold at least one token");
+  Q3_REQUIRE(max_gen >= 0, "max_gen must be >= 0");
+  Q3_REQUIRE(n_prompt + max_gen <= m->S, "n_prompt + max_gen = %lld exceeds max_seq_len %lld",
+             (long long)(n_prompt + max_gen), (long long)m->S);
+  for (int64_t i = 0; i < n_prompt; ++i)
+    Q3_REQUIRE(prompt[i] >= 0 && prompt[i] < kVocab, "prompt token %lld out of range",
+               (long long)prompt[i]);
+  int rc = seq_begin(m, prompt, 0, n_prompt, n_prompt, max_gen, eos);
+  if (rc) return rc;
+  m->gen_n_prompt = n_prompt;
+  m->gen_pos0 = 0;
+  m->gen_max = max_gen;
+  m->gen_active = true;
+  // ingest all but the last prompt token; the last one runs the vocab head
+  return launch_graphs(m, n_prompt - 1, 1);
+}
+
+extern "C" int q3_generate_steps(q3_model* m, int64_t steps) {
+  Q3_REQUIRE(m, "null model");
+  if (!m->gen_active) return set_err(Q3_ERR_STATE, "no generation in progress");
+  return launch_graphs(m, 0, steps);
+}
+
+static int read_generated(q3_model* m, int64_t first_pos, int64_t max_gen, int64_t* out,
+                          int64_t* n_out) {
+  if (max_gen > 0)
+    Q3_CUDA(cudaMemcpyAsync(m->h_tokens, m->tokens + first_pos, (size_t)max_gen * sizeof(int64_t),
+                            cudaMemcpyDeviceToHost, m->stream));
+  Q3_CUDA(cudaMemcpyAsync(m->h_st, m->st, sizeof(SeqState), cudaMemcpyDeviceToHost, m->stream));
+  int rc = check_device_err(m);
+  if (rc) return rc;
+  const int64_t n = m->h_st->n_gen;
+  if (out && n > 0) memcpy(out, m->h_tokens, (size_t)n * sizeof(int64_t));
+  if (n_out) *n_out = n;
+  return Q3_OK;
+}
+
+extern "C" int q3_generate_end(q3_model* m, int64_t* out, int64_t* n_out) {
+  Q3_REQUIRE(m, "null model");
+  if (!m->gen_active) return set_err(Q3_ERR_STATE, "no generation in progress");
+  m->gen_active = false;
+  // generated tokens sit at positions n_prompt+1 .. (the first token, at n_prompt, is fed only)
+  return read_generated(m, m->gen_pos0 + m->gen_n_prompt + 1, m->gen_max, out, n_out);
+}
+
+extern "C" int q3_run(q3_model* m, const int64_t* prompt, int64_t n_prompt, int64_t max_gen,
+                      int64_t eos, int64_t* out, int64_t* n_out) {
+  Q3_REQUIRE(out || max_gen == 0, "out_tokens is null");
+  int rc = q3_generate_begin(m, prompt, n_prompt, max_gen, eos);
+  if (rc) return rc;
+  rc = q3_generate_steps(m, max_gen);
+  if (rc) return rc;
+  return q3_generate_end(m, out, n_out);
+}
+
+extern "C" int q3_decode(q3_model* m, int64_t token, int64_t pos, void* logits, int64_t* next) {
+  Q3_REQUIRE(m, "null model");
+  Q3_REQUIRE(token >= 0 && token < kVocab, "token out of range");
+  Q3_REQUIRE(pos >= 0 && pos < m->S, "pos out of range");
+  m->gen_active = false;
+  int rc = seq_begin(m, &token, pos, 1, INT64_MAX / 2, INT64_MAX / 2, -1);
+  if (rc) return rc;
+  rc = launch_graphs(m, 0, 1);
+  if (rc) return rc;
+  if (logits)
+    Q3_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)kVocab * 2, cudaMemcpyDeviceToDevice,
+                            m->stream));
+  Q3_CUDA(cudaMemcpyAsync(m->h_tokens, m->tokens + pos + 1, sizeof(int64_t),
+                          cudaMemcpyDeviceToHost, m->stream));
+  rc = check_device_err(m);
+  if (rc) return rc;
+  if (next) *next = m->h_tokens[0];
+  return Q3_OK;
+}
+
+extern "C" int q3_init_chat(q3_model* m, int64_t max_ctx) {
+  Q3_REQUIRE(m, "null model");
+  Q3_REQUIRE(max_ctx >= 2 && max_ctx <= m->S, "max_ctx must be in [2, max_seq_len]");
+  const size_t cache = (size_t)kLayers * m->S * kNKV * kHD * sizeof(uint16_t);
+  Q3_CUDA(cudaMemsetAsync(m->kc, 0, cache, m->stream));
+  Q3_CUDA(cudaMemsetAsync(m->vc, 0, cache, m->stream));
+  Q3_CUDA(cudaStreamSynchronize(m->stream));
+  m->chat_ready = true;
+  m->chat_pos = 0;
+  m->chat_max = max_ctx;
+  m->gen_active = false;
+  return Q3_OK;
+}
+
+extern "C" int q3_chat_turn(q3_model* m, const int64_t* toks, int64_t n, int64_t max_gen,
+                            int64_t eos, int64_t* out, int64_t* n_out) {
+  Q3_REQUIRE(m && toks, "null pointer");
+  if (!m->chat_ready) return set_err(Q3_ERR_STATE, "q3_init_chat was not called");
+  Q3_REQUIRE(n >= 1 && max_gen >= 0, "need n_tokens >= 1 and max_gen >= 0");
+  Q3_REQUIRE(m->chat_pos + n + max_gen <= m->chat_max, "turn exceeds the chat context");
+  Q3_REQUIRE(out || max_gen == 0, "out_tokens is null");
+  for (int64_t i = 0; i < n; ++i)
+    Q3_REQUIRE(toks[i] >= 0 && toks[i] < kVocab, "token out of range");
+  const int64_t p0 = m->chat_pos;
+  int rc = seq_begin(m, toks, p0, n, p0 + n, max_gen, eos);
+  if (rc) return rc;
+  rc = launch_graphs(m, n - 1, 1 + max_gen);
+  if (rc) return rc;
+  int64_t got = 0;
+  rc = read_generated(m, p0 + n + 1, max_gen, out, &got);
+  if (rc) return rc;
+  if (n_out) *n_out = got;
+  // model/qwen3_full.mlir:2216-2218: current_pos = new_pos + (count + 1)
+  m->chat_pos = p0 + n + got + 1;
+  return Q3_OK;
+}

@@ -1,0 +1,480 @@
+// q3_gemv.cuh -- batch-1 GEMV kernels for sm_100a.
+//
+//   * Q8_0 fused dequant + GEMV (replaces kernels/cuda/dispatch_{3,4,12,18,20}.cu
+//     and their GPU-dialect twins), with optional fused RMSNorm prologue,
+//     residual-add epilogue, or SwiGLU epilogue over gate/up row pairs;
+//   * f16 vocab GEMV (replaces kernels/cuda/dispatch_24.cu) fused with the
+//     tiled argmax of model/qwen3_full.mlir:1469-1509.
+//
+// Data path: a producer warp streams tiles of 8 weight rows from HBM into a
+// ring of shared-memory stages with 1-D bulk copies (cp.async.bulk, TMA
+// engine, completion on mbarriers); eight consumer warps compute from shared
+// memory.  Weight rows are used in the reference's native layout (Q8_0 rows
+// of K/32 34-byte blocks, f16 rows), 16-byte aligned row starts.
+//
+// Lane mapping = the reference's: warp per row; for Q8_0 lane l owns blocks
+// l, l+32, ... (the input slice for those blocks lives in registers); for f16
+// lane l owns k = l, l+32, ....  Summation orders therefore match the
+// reference kernels exactly (see q3_common.cuh).
+#pragma once
+
+#include "q3_common.cuh"
+
+namespace q3 {
+
+constexpr int kGemvConsumerWarps = 8;
+constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kTileRows = 8;
+constexpr int kMaxSeg = 32;
+
+enum GemvOrder : int { kOrderMlir = 0, kOrderCuda = 1 };
+enum GemvMode : int { kModePlain = 0, kModeNormIn = 1, kModeResid = 2, kModeSwiglu = 3 };
+
+// Device-resident decode state of one sequence (read by the step kernels).
+struct SeqState {
+  int64_t pos;       // position of the token fed in the current step
+  int64_t n_prompt;  // prompt length; steps at pos >= n_prompt produce output
+  int64_t n_gen;     // generated tokens so far
+  int64_t max_gen;
+  int64_t eos;
+  int32_t stop;      // set once the reference's end rule fired
+  int32_t pad;
+};
+
+struct Q8Seg {
+  const uint8_t* w;   // first row of this segment
+  const uint16_t* x;  // input (f16 bits); with kModeNormIn, the un-normalised input
+  uint16_t* y;        // output rows of this segment
+  const uint16_t* r;  // residual rows (kModeResid) aligned with y
+};
+
+struct Q8GemvArgs {
+  Q8Seg seg[kMaxSeg];
+  int nseg;
+  int seg_rows;          // rows per segment (multiple of 8)
+  int K;                 // multiple of 256, <= 3072
+  int64_t up_off_bytes;  // kModeSwiglu: byte offset from a gate row to its up row
+  const uint16_t* norm_g;  // kModeNormIn: RMSNorm gamma [K]
+  // Layer-0 embedding gather (kModeNormIn only): when tokens != nullptr the
+  // input is row tokens[seq->pos] of embd, and CTA 0 also stores it to embed_out.
+  const int64_t* tokens;
+  const SeqState* seq;
+  const uint16_t* embd;
+  uint16_t* embed_out;
+  SeqState* advance;     // if set, pos += 1 (the step's last kernel, prompt ingestion)
+  int* err;
+  int nstages;
+};
+
+// --------------------------------------------------------------------------
+// Input slices in registers
+// --------------------------------------------------------------------------
+template <int G>
+__device__ __forceinline__ void load_x_blocks(const uint16_t* x, int nb, int lane,
+                                              uint32_t (&xr)[G][16]) {
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int b = lane + 32 * g;
+    if (b < nb) {
+      const uint4* p = reinterpret_cast<const uint4*>(x + 32 * b);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const uint4 t = p[v];
+        xr[g][4 * v + 0] = t.x;
+        xr[g][4 * v + 1] = t.y;
+        xr[g][4 * v + 2] = t.z;
+        xr[g][4 * v + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) xr[g][i] = 0u;
+    }
+  }
+}
+
+// RMSNorm of model/qwen3_full.mlir:134-165 evaluated per warp:
+// ss in lane-strided fma order + butterfly; r = sqrt(ss/K + eps).
+__device__ __forceinline__ float rms_denominator(const uint16_t* x, int K, int lane) {
+  float ss = 0.0f;
+  for (int k = lane; k < K; k += 32) {
+    const float v = h2f(x[k]);
+    ss = __fmaf_rn(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  return __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), kEps));
+}
+
+__device__ __forceinline__ uint16_t rms_apply(uint16_t x, uint16_t g, float r) {
+  return f2h(__fmul_rn(__fdiv_rn(h2f(x), r), h2f(g)));
+}
+
+template <int G>
+__device__ __forceinline__ void load_x_blocks_norm(const uint16_t* x, const uint16_t* gamma,
+                                                   int K, int lane, uint32_t (&xr)[G][16]) {
+  const float r = rms_denominator(x, K, lane);
+  const int nb = K / kQBlk;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int b = lane + 32 * g;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      uint32_t v = 0u;
+      if (b < nb) {
+        const int k = 32 * b + 2 * i;
+        v = (uint32_t)rms_apply(x[k], gamma[k], r) |
+            ((uint32_t)rms_apply(x[k + 1], gamma[k + 1], r) << 16);
+      }
+      xr[g][i] = v;
+    }
+  }
+}
+
+template <int G>
+__device__ __forceinline__ void h2_to_f32(const uint32_t (&xr)[G][16], float (&xf)[G][32]) {
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      xf[g][2 * i] = h2f((uint16_t)(xr[g][i] & 0xffffu));
+      xf[g][2 * i + 1] = h2f((uint16_t)(xr[g][i] >> 16));
+    }
+}
+
+// Dot of one Q8_0 row held in shared memory at byte address `row`.
+template <int G, int ORDER>
+__device__ __forceinline__ float q8_row_dot(uint32_t row, int nb, int lane,
+                                            const uint32_t (&xr)[G][16]) {
+  float acc = 0.0f;
+  if constexpr (ORDER == kOrderMlir) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int b = lane + 32 * g;
+      if (b < nb) {
+        const Q8BlockWords bw = q8_load_block(row + (uint32_t)(kQBytes * b));
+        acc = q8_block_dot_mlir(bw, xr[g], acc);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int b = lane + 32 * g;
+      if (b < nb) {
+        float xf[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          xf[2 * i] = h2f((uint16_t)(xr[g][i] & 0xffffu));
+          xf[2 * i + 1] = h2f((uint16_t)(xr[g][i] >> 16));
+        }
+        const Q8BlockWords bw = q8_load_block(row + (uint32_t)(kQBytes * b));
+        acc = q8_block_dot_cuda(bw, xf, acc);
+      }
+    }
+  }
+  return warp_sum(acc);
+}
+
+// --------------------------------------------------------------------------
+// Ring of shared-memory stages fed by the producer warp
+// --------------------------------------------------------------------------
+struct Ring {
+  uint8_t* buf;
+  uint64_t* full;
+  uint64_t* empty;
+  uint32_t stage_bytes;
+  int ns;
+};
+
+__device__ __forceinline__ Ring ring_setup(uint8_t* smem, int ns, uint32_t stage_bytes,
+                                           int consumers) {
+  Ring r;
+  r.full = reinterpret_cast<uint64_t*>(smem);
+  r.empty = r.full + ns;
+  r.buf = smem + 128 * ((16 * ns + 127) / 128);
+  r.stage_bytes = stage_bytes;
+  r.ns = ns;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&r.full[s], 1);
+      mbar_init(&r.empty[s], consumers);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  return r;
+}
+
+__host__ __device__ inline size_t ring_smem_bytes(int ns, uint32_t stage_bytes) {
+  return 128 * ((16 * (size_t)ns + 127) / 128) + (size_t)ns * stage_bytes;
+}
+
+// Producer side: acquire stage for the i-th tile (waits for consumers to free it).
+__device__ __forceinline__ bool ring_acquire(const Ring& r, int i, int* err) {
+  if (i >= r.ns) {
+    const int s = i % r.ns;
+    return mbar_wait(&r.empty[s], (uint32_t)(((i / r.ns) - 1) & 1), err, kErrTimeoutEmpty);
+  }
+  return true;
+}
+
+// Producer drain: wait (bounded) until the copies of the last issued tiles landed.
+__device__ __forceinline__ void ring_drain(const Ring& r, int issued) {
+  const int first = issued > r.ns ? issued - r.ns : 0;
+  for (int i = first; i < issued; ++i)
+    mbar_wait(&r.full[i % r.ns], (uint32_t)((i / r.ns) & 1), nullptr, 0);
+}
+
+// --------------------------------------------------------------------------
+// Q8_0 GEMV kernel
+// --------------------------------------------------------------------------
+template <int G, int ORDER, int MODE>
+__global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant__ Q8GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = a.K / kQBlk;
+  const uint32_t rowbytes = (uint32_t)(nb * kQBytes);
+  const uint32_t tile_bytes = rowbytes * kTileRows * (MODE == kModeSwiglu ? 2u : 1u);
+  const int tiles_per_seg = a.seg_rows / kTileRows;
+  const int ntiles = a.nseg * tiles_per_seg;
+  Ring ring = ring_setup(smem, a.nstages, tile_bytes, kGemvConsumerWarps);
+
+  if (a.seq != nullptr && a.seq->stop) return;
+
+  if (warp == kGemvConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      int i = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+        if (!ring_acquire(ring, i, a.err)) break;
+        const int s = i % ring.ns;
+        const int seg = t / tiles_per_seg;
+        const int r0 = (t % tiles_per_seg) * kTileRows;
+        const uint8_t* src = a.seg[seg].w + (int64_t)r0 * rowbytes;
+        uint8_t* dst = ring.buf + (size_t)s * ring.stage_bytes;
+        mbar_expect_tx(&ring.full[s], tile_bytes);
+        bulk_g2s(dst, src, rowbytes * kTileRows, &ring.full[s], pol);
+        if (MODE == kModeSwiglu)
+          bulk_g2s(dst + rowbytes * kTileRows, src + a.up_off_bytes, rowbytes * kTileRows,
+                   &ring.full[s], pol);
+      }
+      ring_drain(ring, i);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  uint32_t xr[G][16];
+  const uint16_t* xcur = nullptr;
+  if (MODE == kModeNormIn || MODE == kModeSwiglu) {
+    const uint16_t* x = a.seg[0].x;
+    if (a.tokens != nullptr) {
+      int64_t tok = a.tokens[a.seq->pos];
+      if (tok < 0 || tok >= kVocab) {
+        if (lane == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
+        tok = 0;
+      }
+      x = a.embd + tok * (int64_t)kDim;
+      if (blockIdx.x == 0 && warp == 0 && a.embed_out != nullptr)
+        for (int k = lane; k < a.K; k += 32) a.embed_out[k] = x[k];
+    }
+    load_x_blocks_norm<G>(x, a.norm_g, a.K, lane, xr);
+  }
+
+  int i = 0;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+    const int seg = t / tiles_per_seg;
+    const int r0 = (t % tiles_per_seg) * kTileRows;
+    if (MODE == kModePlain || MODE == kModeResid) {
+      if (a.seg[seg].x != xcur) {
+        xcur = a.seg[seg].x;
+        load_x_blocks<G>(xcur, nb, lane, xr);
+      }
+    }
+    const int s = i % ring.ns;
+    if (!mbar_wait(&ring.full[s], (uint32_t)((i / ring.ns) & 1), a.err, kErrTimeoutFull)) break;
+    const uint32_t base = smem_u32(ring.buf + (size_t)s * ring.stage_bytes);
+    const int row = r0 + warp;
+    const float d = q8_row_dot<G, ORDER>(base + rowbytes * warp, nb, lane, xr);
+    if (MODE == kModeSwiglu) {
+      const float u = q8_row_dot<G, ORDER>(base + rowbytes * (kTileRows + warp), nb, lane, xr);
+      if (lane == 0) a.seg[seg].y[row] = swiglu_h(f2h(d), f2h(u));
+    } else if (MODE == kModeResid) {
+      if (lane == 0)
+        a.seg[seg].y[row] = f2h(__fadd_rn(h2f(a.seg[seg].r[row]), h2f(f2h(d))));
+    } else {
+      if (lane == 0) a.seg[seg].y[row] = f2h(d);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ring.empty[s]);
+  }
+  if (a.advance != nullptr && blockIdx.x == 0 && threadIdx.x == 0) a.advance->pos += 1;
+}
+
+// --------------------------------------------------------------------------
+// f16 vocab GEMV + argmax
+// --------------------------------------------------------------------------
+struct ArgmaxPartial {
+  float v;
+  int32_t pad;
+  int64_t i;
+};
+
+// "a is a better argmax candidate than b": larger value, then lower index;
+// only values above -inf qualify (NaN never does) -- the strict ogt scan of
+// model/qwen3_full.mlir:1482-1507.
+__device__ __forceinline__ bool am_better(float av, int64_t ai, float bv, int64_t bi) {
+  if (!(av > -__int_as_float(0x7f800000))) return false;
+  if (bi < 0) return true;
+  return av > bv || (av == bv && ai < bi);
+}
+
+struct VocabArgs {
+  const uint16_t* w;       // [N, K] f16 rows
+  const uint16_t* x;       // input (f16); normalised with norm_g if non-null
+  const uint16_t* norm_g;
+  uint16_t* logits;        // optional [N] f16
+  int N, K;                // N multiple of 8, K == 1024 (lane holds K/32 inputs)
+  ArgmaxPartial* partial;  // [gridDim.x]
+  unsigned int* counter;   // zero before the first launch; the last CTA re-zeroes it
+  int64_t* token_out;      // optional: the argmax
+  // Decode-state update done by the last CTA (optional):
+  SeqState* seq;           // pos += 1; tokens[pos] = argmax; n_gen / stop bookkeeping
+  int64_t* tokens;
+  int* err;
+  int nstages;
+};
+
+constexpr int kVocabK = 1024;
+
+__global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_constant__ VocabArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ ArgmaxPartial warp_best[kGemvThreads / 32];
+  __shared__ int is_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rowbytes = (uint32_t)a.K * 2u;
+  const uint32_t tile_bytes = rowbytes * kTileRows;
+  const int ntiles = a.N / kTileRows;
+  Ring ring = ring_setup(smem, a.nstages, tile_bytes, kGemvConsumerWarps);
+  if (a.seq != nullptr && a.seq->stop) return;
+
+  if (warp == kGemvConsumerWarps) {
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      int i = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+        if (!ring_acquire(ring, i, a.err)) break;
+        const int s = i % ring.ns;
+        mbar_expect_tx(&ring.full[s], tile_bytes);
+        bulk_g2s(ring.buf + (size_t)s * ring.stage_bytes,
+                 reinterpret_cast<const uint8_t*>(a.w) + (int64_t)t * tile_bytes, tile_bytes,
+                 &ring.full[s], pol);
+      }
+      ring_drain(ring, i);
+    }
+  } else {
+    // lane-strided inputs x[l + 32 i], normalised in f32 and rounded to f16
+    uint16_t xh[kVocabK / 32];
+    if (a.norm_g != nullptr) {
+      const float r = rms_denominator(a.x, a.K, lane);
+#pragma unroll
+      for (int i = 0; i < kVocabK / 32; ++i)
+        xh[i] = rms_apply(a.x[lane + 32 * i], a.norm_g[lane + 32 * i], r);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kVocabK / 32; ++i) xh[i] = a.x[lane + 32 * i];
+    }
+    float best_v = -__int_as_float(0x7f800000);
+    int64_t best_i = -1;
+    int i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      const int s = i % ring.ns;
+      if (!mbar_wait(&ring.full[s], (uint32_t)((i / ring.ns) & 1), a.err, kErrTimeoutFull)) break;
+      const uint32_t row = smem_u32(ring.buf + (size_t)s * ring.stage_bytes) + rowbytes * warp;
+      float acc = 0.0f;
+#pragma unroll
+      for (int k = 0; k < kVocabK / 32; ++k) acc = fma_h(lds16(row + 2u * (lane + 32 * k)), xh[k], acc);
+      acc = warp_sum(acc);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ring.empty[s]);
+      const uint16_t lh = f2h(acc);
+      const int64_t n = (int64_t)t * kTileRows + warp;
+      if (lane == 0 && a.logits != nullptr) a.logits[n] = lh;
+      const float lv = h2f(lh);
+      if (am_better(lv, n, best_v, best_i)) {
+        best_v = lv;
+        best_i = n;
+      }
+    }
+    if (lane == 0) {
+      warp_best[warp].v = best_v;
+      warp_best[warp].i = best_i;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float bv = -__int_as_float(0x7f800000);
+    int64_t bi = -1;
+    for (int w = 0; w < kGemvConsumerWarps; ++w)
+      if (am_better(warp_best[w].v, warp_best[w].i, bv, bi)) {
+        bv = warp_best[w].v;
+        bi = warp_best[w].i;
+      }
+    a.partial[blockIdx.x].v = bv;
+    a.partial[blockIdx.x].i = bi;
+    __threadfence();
+    const unsigned prev = atomicAdd(a.counter, 1u);
+    is_last = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // last CTA: reduce the per-CTA partials (any order: the rule is a total order)
+  float bv = -__int_as_float(0x7f800000);
+  int64_t bi = -1;
+  for (int c = threadIdx.x; c < (int)gridDim.x; c += blockDim.x) {
+    const volatile ArgmaxPartial* p = a.partial + c;
+    const float v = p->v;
+    const int64_t ii = p->i;
+    if (am_better(v, ii, bv, bi)) {
+      bv = v;
+      bi = ii;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (am_better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    warp_best[warp].v = bv;
+    warp_best[warp].i = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w)
+      if (am_better(warp_best[w].v, warp_best[w].i, bv, bi)) {
+        bv = warp_best[w].v;
+        bi = warp_best[w].i;
+      }
+    if (a.token_out != nullptr) *a.token_out = bi;
+    if (a.seq != nullptr) {
+      SeqState* st = a.seq;
+      const int64_t pos = st->pos;
+      a.tokens[pos + 1] = bi;
+      if (pos >= st->n_prompt) {
+        st->n_gen += 1;
+        // @generate (model/qwen3_full.mlir:1412-1530): groups of 4; the loop
+        // ends when the last token of a group is eos, or max_gen is reached.
+        if (st->n_gen >= st->max_gen || ((st->n_gen % 4) == 0 && bi == st->eos)) st->stop = 1;
+      }
+      st->pos = pos + 1;
+    }
+    *a.counter = 0u;
+  }
+}
+
+}  // namespace q3

@@ -1,0 +1,131 @@
+"""Host mirror of the reference module's public functions, over libq3b200.so.
+
+The reference drives model/qwen3_full.mlir through iree.runtime:
+``ctx.invoke(run, [tokens, n_tokens, max_tokens, eos])`` returns
+``(tokens_out, n)`` (scripts/benchmark.py:52-81, scripts/chat.py:112-126).
+``Qwen3Decoder`` offers the same calls -- run, decode, prefill_all,
+init_chat, chat_turn -- backed by the sm_100a kernels and CUDA graphs of the
+library, with numpy arrays in and out and no PyTorch.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from ._lib import Weights, call, lib
+from .device import DeviceArray
+from .weights import VOCAB
+
+WEIGHT_FIELDS = [
+    ("token_embd", "token_embd.weight"), ("output_norm", "output_norm.weight"),
+    ("output_T", "output_T.weight"), ("attn_norm", "stacked.attn_norm.weight"),
+    ("ffn_norm", "stacked.ffn_norm.weight"), ("attn_q_norm", "stacked.attn_q_norm.weight"),
+    ("attn_k_norm", "stacked.attn_k_norm.weight"), ("q8_attn_q", "stacked.q8.attn_q.weight"),
+    ("q8_attn_k", "stacked.q8.attn_k.weight"), ("q8_attn_v", "stacked.q8.attn_v.weight"),
+    ("q8_attn_output", "stacked.q8.attn_output.weight"),
+    ("q8_ffn_gate_up", "stacked.q8.ffn_gate_up.weight"),
+    ("q8_ffn_down", "stacked.q8.ffn_down.weight"),
+]
+
+
+class DeviceWeights:
+    """Uploads a parameter dict once (tied tensors share one buffer)."""
+
+    def __init__(self, host: dict[str, np.ndarray]):
+        self.buffers: dict[str, DeviceArray] = {}
+        by_id: dict[int, DeviceArray] = {}
+        for _, name in WEIGHT_FIELDS:
+            a = host[name]
+            if id(a) not in by_id:
+                by_id[id(a)] = DeviceArray.from_host(a)
+            self.buffers[name] = by_id[id(a)]
+        self.nbytes = sum(d.nbytes for d in by_id.values())
+        self.struct = Weights(**{f: self.buffers[n].ptr for f, n in WEIGHT_FIELDS})
+
+
+class Qwen3Decoder:
+    """One decoder (KV cache, activations, graphs) on the current device."""
+
+    def __init__(self, weights: DeviceWeights | dict, max_seq_len: int = 1024, stream=None):
+        self.weights = weights if isinstance(weights, DeviceWeights) else DeviceWeights(weights)
+        self.max_seq_len = int(max_seq_len)
+        h = ctypes.c_void_p()
+        call("q3_model_create", ctypes.byref(self.weights.struct), self.max_seq_len, stream,
+             ctypes.byref(h))
+        self.handle = h.value
+        self.stream = lib().q3_model_stream(self.handle)
+
+    # -- @run (model/qwen3_full.mlir:2113-2167)
+    def run(self, tokens, max_tokens: int, eos: int) -> tuple[np.ndarray, int]:
+        t = np.ascontiguousarray(tokens, dtype=np.int64)
+        out = np.zeros(max(int(max_tokens), 1), dtype=np.int64)
+        n = ctypes.c_int64(0)
+        call("q3_run", self.handle, t.ctypes.data, t.size, int(max_tokens), int(eos),
+             out.ctypes.data, ctypes.byref(n))
+        return out[:max(int(max_tokens), 0)], n.value
+
+    # -- @decode (model/qwen3_full.mlir:1340-1394)
+    def decode(self, token: int, pos: int, want_logits: bool = True):
+        nxt = ctypes.c_int64(-1)
+        logits = DeviceArray((VOCAB,), np.float16) if want_logits else None
+        call("q3_decode", self.handle, int(token), int(pos), logits.ptr if logits else None,
+             ctypes.byref(nxt))
+        return (logits.download() if logits else None), nxt.value
+
+    # -- @prefill_all (model/qwen3_full.mlir:1541-1570): token by token through @decode
+    def prefill_all(self, tokens) -> np.ndarray:
+        logits = None
+        for i, t in enumerate(np.asarray(tokens, dtype=np.int64)):
+            logits, _ = self.decode(int(t), i, want_logits=(i == len(tokens) - 1))
+        return logits
+
+    # -- @init_chat / @chat_turn (model/qwen3_full.mlir:2172-2222)
+    def init_chat(self, max_ctx: int) -> None:
+        call("q3_init_chat", self.handle, int(max_ctx))
+
+    def chat_turn(self, tokens, max_gen: int, eos: int) -> tuple[np.ndarray, int]:
+        t = np.ascontiguousarray(tokens, dtype=np.int64)
+        out = np.zeros(max(int(max_gen), 1), dtype=np.int64)
+        n = ctypes.c_int64(0)
+        call("q3_chat_turn", self.handle, t.ctypes.data, t.size, int(max_gen), int(eos),
+             out.ctypes.data, ctypes.byref(n))
+        return out[:max(int(max_gen), 0)], n.value
+
+    # -- step-level access for harnesses
+    def generate_begin(self, tokens, max_gen: int, eos: int) -> None:
+        t = np.ascontiguousarray(tokens, dtype=np.int64)
+        call("q3_generate_begin", self.handle, t.ctypes.data, t.size, int(max_gen), int(eos))
+
+    def generate_steps(self, steps: int) -> None:
+        call("q3_generate_steps", self.handle, int(steps))
+
+    def generate_end(self, max_gen: int) -> tuple[np.ndarray, int]:
+        out = np.zeros(max(int(max_gen), 1), dtype=np.int64)
+        n = ctypes.c_int64(0)
+        call("q3_generate_end", self.handle, out.ctypes.data, ctypes.byref(n))
+        return out[:n.value], n.value
+
+    def launches_per_step(self) -> int:
+        n = ctypes.c_int64(0)
+        call("q3_model_launches_per_step", self.handle, ctypes.byref(n))
+        return n.value
+
+    def device_error(self) -> int:
+        c = ctypes.c_int(0)
+        call("q3_model_device_error", self.handle, ctypes.byref(c))
+        return c.value
+
+    def synchronize(self) -> None:
+        call("q3_stream_synchronize", self.stream)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib().q3_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,265 @@
+"""GPU kernels through the C ABI vs the CPU oracle, bit for bit.
+
+Each kernel states a summation order (q3_common.cuh); the oracle states the
+same one, so outputs are compared as f16 bit patterns, not with a tolerance.
+The reference's own CUDA kernels (oracle/_ref) pin the oracle itself."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+from conftest import ROOT, bits, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+Q8_SHAPES = [(2048, 1024), (1024, 1024), (1024, 2048), (6144, 1024), (1024, 3072),
+             (8, 256), (24, 512), (40, 1280), (16, 2816)]
+
+
+def _up(q3, a):
+    return q3.DeviceArray.from_host(np.ascontiguousarray(a))
+
+
+def _q8(O, rng, N, K, std=0.02):
+    return O.quantize_q8_0((rng.standard_normal((N, K)) * std).astype(np.float32))
+
+
+def _sync(q3):
+    q3.synchronize(None)
+
+
+@pytest.mark.parametrize("N,K", Q8_SHAPES)
+def test_gemv_q8_bit_exact(gpu, O, N, K):
+    rng = np.random.default_rng(N * 7 + K)
+    w, x = _q8(O, rng, N, K), rng.standard_normal(K).astype(np.float16)
+    dw, dx, dy = _up(gpu, w), _up(gpu, x), gpu.DeviceArray((N,), np.float16)
+    dy.fill_bytes(0xFF)
+    assert gpu.lib().q3_gemv_q8(dw.ptr, dx.ptr, dy.ptr, N, K, None) == 0
+    y = dy.download()
+    assert np.array_equal(bits(y), bits(O.gemv_q8(w, x, N, K, "mlir")))
+
+
+@pytest.mark.parametrize("N,K", Q8_SHAPES[:5])
+def test_gemv_q8_cuda_order_bit_exact(gpu, O, N, K):
+    rng = np.random.default_rng(N + K)
+    w, x = _q8(O, rng, N, K), rng.standard_normal(K).astype(np.float16)
+    dw, dx, dy = _up(gpu, w), _up(gpu, x), gpu.DeviceArray((N,), np.float16)
+    assert gpu.lib().q3_gemv_q8_cuda_order(dw.ptr, dx.ptr, dy.ptr, N, K, None) == 0
+    assert np.array_equal(bits(dy.download()), bits(O.gemv_q8(w, x, N, K, "cuda")))
+
+
+def test_gemv_q8_extreme_values(gpu, O):
+    """Blocks at int8 limits, zero blocks, large and tiny scales, inf input."""
+    rng = np.random.default_rng(11)
+    N, K = 16, 1024
+    wf = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    wf[0, :32] = 0
+    wf[1] = np.where(np.arange(K) % 2 == 0, 1000.0, -1000.0)
+    wf[2] = 1e-7
+    w = O.quantize_q8_0(wf)
+    x = rng.standard_normal(K).astype(np.float16)
+    x[5] = 65504
+    dw, dx, dy = _up(gpu, w), _up(gpu, x), gpu.DeviceArray((N,), np.float16)
+    assert gpu.lib().q3_gemv_q8(dw.ptr, dx.ptr, dy.ptr, N, K, None) == 0
+    assert np.array_equal(bits(dy.download()), bits(O.gemv_q8(w, x, N, K, "mlir")))
+
+
+@pytest.mark.parametrize("N,K,L", [(2048, 1024, 28), (1024, 3072, 6)])
+def test_gemv_q8_layers_bit_exact(gpu, O, N, K, L):
+    rng = np.random.default_rng(L)
+    bpl = N * (K // 32) * 34
+    w = np.stack([_q8(O, rng, N, K) for _ in range(L)])
+    x = rng.standard_normal((L, K)).astype(np.float16)
+    dw, dx, dy = _up(gpu, w), _up(gpu, x), gpu.DeviceArray((L, N), np.float16)
+    assert gpu.lib().q3_gemv_q8_layers(dw.ptr, bpl, dx.ptr, dy.ptr, N, K, L, None) == 0
+    y = dy.download()
+    for l in range(L):
+        assert np.array_equal(bits(y[l]), bits(O.gemv_q8(w[l], x[l], N, K, "mlir"))), l
+
+
+def test_gemv_q8_norm_resid_swiglu_bit_exact(gpu, O):
+    rng = np.random.default_rng(21)
+    L = gpu.lib()
+    x = rng.standard_normal(1024).astype(np.float16)
+    g = (1 + 0.1 * rng.standard_normal(1024)).astype(np.float16)
+    # norm prologue (attention input, model/qwen3_full.mlir:779)
+    w = _q8(O, rng, 2048, 1024)
+    dw, dx, dg, dy = _up(gpu, w), _up(gpu, x), _up(gpu, g), gpu.DeviceArray((2048,), np.float16)
+    assert L.q3_gemv_q8_norm(dw.ptr, dx.ptr, dg.ptr, dy.ptr, 2048, 1024, None) == 0
+    assert np.array_equal(bits(dy.download()), bits(O.gemv_q8(w, O.rmsnorm(x, g), 2048, 1024)))
+    # residual epilogue (O projection, :739 + :801-805)
+    a = rng.standard_normal(2048).astype(np.float16)
+    w = _q8(O, rng, 1024, 2048)
+    dw, da, dy = _up(gpu, w), _up(gpu, a), gpu.DeviceArray((1024,), np.float16)
+    assert L.q3_gemv_q8_resid(dw.ptr, da.ptr, dx.ptr, dy.ptr, 1024, 2048, None) == 0
+    want = O.add_f16(x, O.gemv_q8(w, a, 1024, 2048))
+    assert np.array_equal(bits(dy.download()), bits(want))
+    # SwiGLU epilogue over gate/up rows (:807-839)
+    w = _q8(O, rng, 6144, 1024)
+    dw, dy = _up(gpu, w), gpu.DeviceArray((3072,), np.float16)
+    assert L.q3_gemv_q8_swiglu(dw.ptr, dx.ptr, dg.ptr, dy.ptr, 3072, 1024, None) == 0
+    want = O.swiglu(O.gemv_q8(w, O.rmsnorm(x, g), 6144, 1024))
+    assert np.array_equal(bits(dy.download()), bits(want))
+
+
+# ---------------------------------------------------------------- vocab + argmax
+def _vocab_case(gpu, O, N, rng, norm=True, w=None, x=None):
+    L = gpu.lib()
+    if w is None:
+        w = (rng.standard_normal((N, 1024)) * 0.02).astype(np.float16)
+    if x is None:
+        x = rng.standard_normal(1024).astype(np.float16)
+    g = (1 + 0.1 * rng.standard_normal(1024)).astype(np.float16)
+    ws = gpu.DeviceArray((L.q3_vocab_argmax_workspace_bytes(),), np.uint8, zero=True)
+    dw, dx, dg = _up(gpu, w), _up(gpu, x), _up(gpu, g)
+    dl, dt = gpu.DeviceArray((N,), np.float16), gpu.DeviceArray((1,), np.int64)
+    assert L.q3_vocab_argmax(dw.ptr, dx.ptr, dg.ptr if norm else None, dl.ptr, dt.ptr, ws.ptr, N,
+                             1024, None) == 0
+    xin = O.rmsnorm(x, g) if norm else x
+    want = O.gemv_f16(w, xin)
+    return dl.download(), int(dt.download()[0]), want, O.argmax_f16(want), (L, dw, dx, dg, dl, dt, ws)
+
+
+def test_vocab_argmax_bit_exact(gpu, O):
+    rng = np.random.default_rng(31)
+    logits, tok, want, wtok, h = _vocab_case(gpu, O, 151936, rng)
+    assert np.array_equal(bits(logits), bits(want))
+    assert tok == wtok
+    # a second launch on the same workspace (the counter re-arms itself)
+    L, dw, dx, dg, dl, dt, ws = h
+    dt.fill_bytes(0xFF)
+    assert L.q3_vocab_argmax(dw.ptr, dx.ptr, dg.ptr, None, dt.ptr, ws.ptr, 151936, 1024, None) == 0
+    assert int(dt.download()[0]) == wtok
+
+
+def test_vocab_argmax_ties_take_lowest_index(gpu, O):
+    rng = np.random.default_rng(32)
+    N = 4096
+    w = (rng.standard_normal((N, 1024)) * 0.02).astype(np.float16)
+    x = rng.standard_normal(1024).astype(np.float16)
+    w[3000] = w[700] = w[2999] = (x.astype(np.float32) * 0.01).astype(np.float16)  # equal maxima
+    logits, tok, want, wtok, _ = _vocab_case(gpu, O, N, rng, norm=False, w=w, x=x)
+    assert np.array_equal(bits(logits), bits(want))
+    assert tok == wtok == 700
+
+
+def test_vocab_argmax_small_and_no_norm(gpu, O):
+    rng = np.random.default_rng(33)
+    logits, tok, want, wtok, _ = _vocab_case(gpu, O, 64, rng, norm=False)
+    assert np.array_equal(bits(logits), bits(want)) and tok == wtok
+
+
+# ---------------------------------------------------------------- attention
+@pytest.mark.parametrize("T", [1, 2, 31, 32, 33, 255, 256, 257, 513, 1024, 2049])
+def test_decode_attention_bit_exact(gpu, O, T):
+    rng = np.random.default_rng(T)
+    L = gpu.lib()
+    S, layer = 2100, 2
+    slot0, pos = layer * S, T - 1
+    kc = rng.standard_normal((3 * S, 8, 128)).astype(np.float16)
+    vc = rng.standard_normal((3 * S, 8, 128)).astype(np.float16)
+    qkv = rng.standard_normal(4096).astype(np.float16)
+    gq = (1 + 0.1 * rng.standard_normal(128)).astype(np.float16)
+    gk = (1 + 0.1 * rng.standard_normal(128)).astype(np.float16)
+    c = np.empty((S, 64), np.float32)
+    s = np.empty((S, 64), np.float32)
+    assert L.q3_rope_table(S, c.ctypes.data, s.ctypes.data) == 0
+    d = {k: _up(gpu, v) for k, v in dict(qkv=qkv, gq=gq, gk=gk, c=c, s=s, kc=kc, vc=vc,
+                                         pos=np.array([pos], np.int64)).items()}
+    out = gpu.DeviceArray((2048,), np.float16)
+    ws = gpu.DeviceArray((L.q3_attention_workspace_bytes(S),), np.uint8, zero=True)
+    for rep in range(2):  # twice: the split counters must re-arm
+        assert L.q3_decode_attention(d["qkv"].ptr, d["gq"].ptr, d["gk"].ptr, d["c"].ptr,
+                                     d["s"].ptr, S, d["kc"].ptr, d["vc"].ptr, slot0, S,
+                                     d["pos"].ptr, out.ptr, ws.ptr, None) == 0
+    qn = O.qk_norm_rope(qkv[:2048], gq, pos)
+    kn = O.qk_norm_rope(qkv[2048:3072], gk, pos)
+    kc2, vc2 = kc.copy(), vc.copy()
+    kc2[slot0 + pos] = kn.reshape(8, 128)
+    vc2[slot0 + pos] = qkv[3072:].reshape(8, 128)
+    want = O.attention(qn, kc2, vc2, slot0, T)
+    got = out.download()
+    assert np.array_equal(bits(got), bits(want)), rel_l2(got, want)
+    gk_cache, gv_cache = d["kc"].download(), d["vc"].download()
+    assert np.array_equal(bits(gk_cache), bits(kc2)) and np.array_equal(bits(gv_cache), bits(vc2))
+
+
+# ---------------------------------------------------------------- IREE-ABI kernels
+IREE = [  # (dispatch, N, K, in_off, out_off, bpl)
+    (3, 2048, 1024, 2112, 4160, 2228224),
+    (4, 1024, 1024, 2112, None, 1114112),
+    (12, 1024, 2048, 12352, 2048, 2228224),
+    (18, 6144, 1024, 64, 6144, 6684672),
+    (20, 1024, 3072, 18432, 0, 3342336),
+]
+
+
+def _iree_setup(gpu, O, N, K, in_off, out_off, seed):
+    rng = np.random.default_rng(seed)
+    w = np.stack([_q8(O, rng, N, K) for _ in range(3)])  # 3 stacked layers
+    x = rng.standard_normal(K).astype(np.float16)
+    b1 = np.zeros(in_off + 2 * K + 64, np.uint8)
+    b1[in_off:in_off + 2 * K] = x.view(np.uint8)
+    oo = out_off if out_off is not None else 8192
+    b2 = np.full(oo + 2 * N + 64, 0xAB, np.uint8)
+    return w, x, _up(gpu, w), _up(gpu, b1), _up(gpu, b2), oo, b2
+
+
+def _launch(L, prefix, d, dw, db1, db2, oo, layer):
+    fn = getattr(L, f"{prefix}_dispatch_{d}")
+    if d == 4:
+        return fn(dw.ptr, db1.ptr, db2.ptr, oo, layer, 0, None)
+    return fn(dw.ptr, db1.ptr, db2.ptr, layer, 0, None)
+
+
+@pytest.mark.parametrize("d,N,K,in_off,out_off,bpl", IREE)
+def test_iree_dispatch_bit_exact(gpu, O, d, N, K, in_off, out_off, bpl):
+    w, x, dw, db1, db2, oo, b2 = _iree_setup(gpu, O, N, K, in_off, out_off, d)
+    assert _launch(gpu.lib(), "q3_iree", d, dw, db1, db2, oo, 2) == 0
+    got = db2.download()
+    y = got[oo:oo + 2 * N].view(np.float16)
+    assert np.array_equal(bits(y), bits(O.gemv_q8(w[2], x, N, K, "cuda")))
+    assert np.all(got[:oo] == 0xAB) and np.all(got[oo + 2 * N:] == 0xAB)
+
+
+REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libref_dispatch.so")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not os.path.exists(REF_LIB):
+        pytest.skip("oracle/_ref not built (the reference tree was absent at build time)")
+    L = ctypes.CDLL(REF_LIB)
+    P, U = ctypes.c_void_p, ctypes.c_uint32
+    for d in (3, 12, 18, 20):
+        getattr(L, f"ref_dispatch_{d}").argtypes = [P, P, P, U, U, P]
+    L.ref_dispatch_4.argtypes = [P, P, P, U, U, U, P]
+    L.ref_dispatch_24.argtypes = [P, P, P, U, P]
+    return L
+
+
+@pytest.mark.parametrize("d,N,K,in_off,out_off,bpl", IREE)
+def test_reference_kernels_pin_the_oracle(gpu, O, ref, d, N, K, in_off, out_off, bpl):
+    """The reference's own dispatch_N.cu, run on this GPU, equals the oracle's
+    CUDA-order GEMV bit for bit -- and therefore our q3_iree_dispatch_N."""
+    w, x, dw, db1, db2, oo, _ = _iree_setup(gpu, O, N, K, in_off, out_off, 100 + d)
+    assert _launch(ref, "ref", d, dw, db1, db2, oo, 1) == 0
+    _sync(gpu)
+    y = db2.download()[oo:oo + 2 * N].view(np.float16)
+    assert np.array_equal(bits(y), bits(O.gemv_q8(w[1], x, N, K, "cuda")))
+
+
+def test_reference_vocab_kernel_pins_the_oracle(gpu, O, ref):
+    rng = np.random.default_rng(24)
+    N = 151936
+    w = (rng.standard_normal((N, 1024)) * 0.02).astype(np.float16)
+    x = rng.standard_normal(1024).astype(np.float16)
+    b1 = np.zeros(64 + 2048, np.uint8)
+    b1[64:] = x.view(np.uint8)
+    dw, db1 = _up(gpu, w), _up(gpu, b1)
+    want = bits(O.gemv_f16(w, x))
+    for lib_, fn in ((ref, "ref_dispatch_24"), (gpu.lib(), "q3_iree_dispatch_24")):
+        db2 = gpu.DeviceArray((256 + 2 * N,), np.uint8, zero=True)
+        assert getattr(lib_, fn)(dw.ptr, db1.ptr, db2.ptr, 256, None) == 0
+        _sync(gpu)
+        assert np.array_equal(bits(db2.download()[256:].view(np.float16)), want), fn
