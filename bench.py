@@ -1,0 +1,472 @@
+#!/usr/bin/env python3
+"""Qwen3-0.6B Q8_0 batch-1 greedy decode on B200 -- the BASELINE metric.
+
+Workload: 28 layers of Q8_0 projections + GQA
+attention over the flat KV cache + tied f16 vocab GEMV + argmax, seeded
+random-init weights (N(0,0.02) quantised Q8_0, gammas 1+N(0,0.1)), a 32-token
+prompt of ids U[0,151936), 256 generated tokens per sequence, KV cache of
+1024 positions.  A "step" is one decode step (one token through all 28 layers
+and the vocab head).  Timed steps are grouped in sequences of up to 256
+generated tokens; every sequence restarts from the same prompt.
+
+  python bench.py [--gpus N --steps K --warmup W]      our sm_100a path
+  python bench.py --impl reference [...]               the CPU oracle (reference arm)
+
+value: tokens/s over all ranks, device time (CUDA events on the decoder's
+stream) of the K timed steps, max over ranks.  e2e: q3_run (the public call
+mirroring the reference's @run) with host prompt in / host tokens out, wall
+clock, as scripts/benchmark.py measures it.  N>1 (torchrun): independent
+replicas, one per GPU, no collective on the data path (replicas only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qwen3-iree_b200"))
+
+METRIC = "Qwen3-0.6B Q8_0 decode tok/s (B=1, B=32) and GEMV HBM GB/s vs 8 TB/s peak"
+UNIT = "tok/s"
+PROMPT_LEN, GEN_PER_SEQ, CACHE = 32, 256, 1024
+EOS = 151645
+NOMINAL_HBM_GBS = 8000.0
+KIND_NAMES = ["qkv", "attn", "o", "gate_up", "down", "vocab"]
+# Algorithmic bytes per launch (weights + activations read and written).
+Q8_BYTES = {"qkv": 2228224 + 2 * 1114112, "o": 2228224, "gate_up": 6684672, "down": 3342336}
+ACT_BYTES = {"qkv": 2048 + 2048 + 8192, "o": 4096 + 2048 + 2048, "gate_up": 2048 + 2048 + 6144,
+             "down": 6144 + 2048 + 2048}
+VOCAB_BYTES = 151936 * 1024 * 2 + 2048 + 2048 + 151936 * 2
+NORM_BYTES = 28 * (1024 + 1024 + 128 + 128) * 2 + 1024 * 2
+KV_ROW = 8 * 128 * 2  # one position of K (or V) for one layer
+
+
+def step_bytes(pos: int) -> int:
+    """Algorithmic HBM bytes of one decode step at position pos (attends pos+1 keys)."""
+    w = sum(Q8_BYTES.values()) * 28 + VOCAB_BYTES + NORM_BYTES
+    kv = 28 * (2 * KV_ROW * (pos + 1) + 2 * KV_ROW)
+    return w + kv
+
+
+def attn_bytes(pos: int) -> int:
+    return 2 * KV_ROW * (pos + 1) + 2 * KV_ROW + 8192 + 4096 + 512
+
+
+def load_peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic() -> dict:
+    """ncu DRAM bytes per launch, from profiles/ncu_traffic.txt ("kind bytes" lines)."""
+    out = {}
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    if os.path.exists(p):
+        for line in open(p):
+            parts = line.split()
+            if len(parts) >= 2 and not line.startswith("#"):
+                try:
+                    out[parts[0]] = float(parts[1])
+                except ValueError:
+                    pass
+    return out
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device, self.lines, self.proc = device, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------- distributed plumbing
+class Dist:
+    """torch.distributed over NCCL for the barrier and the max-over-ranks of the
+    timings only; the decode itself has no collective (replicas)."""
+
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.torch = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.torch, self.dist = torch, dist
+
+    def barrier(self):
+        if self.torch:
+            self.dist.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.torch:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v: float) -> float:
+        if not self.torch:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.torch:
+            self.dist.destroy_process_group()
+
+
+def aggregate(units_per_rank: list[float], times_ms: list[float]) -> tuple[float, float]:
+    """Whole-job throughput: all units over the slowest rank's time."""
+    t = max(times_ms)
+    return sum(units_per_rank) / (t / 1e3), t
+
+
+# ---------------------------------------------------------------- CPU oracle legs
+def cpu_oracle_decode(steps: int, warmup: int, seed: int, budget_s: float) -> dict:
+    """The CPU oracle (oracle/q3_oracle.c, all host threads) on the same
+    workload: prompt ingestion (timed separately) then up to `steps` decode
+    steps, stopping early once `budget_s` of decode time is spent."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from q3b200.weights import synthetic_weights, to_oracle_dict
+
+    w = synthetic_weights(seed=seed)
+    m = O.Model(to_oracle_dict(w))
+    prompt = np.random.default_rng(seed).integers(0, 151936, PROMPT_LEN, dtype=np.int64)
+    kc, vc = m.new_cache(CACHE)
+    t0 = time.perf_counter()
+    tok = None
+    for i, t in enumerate(prompt):
+        tok, _ = m.decode_step(int(t), i, kc, vc, CACHE)
+    t_prompt = time.perf_counter() - t0
+    pos = PROMPT_LEN
+    for _ in range(warmup):
+        tok, _ = m.decode_step(tok, pos, kc, vc, CACHE)
+        pos += 1
+    n, t_dec = 0, 0.0
+    steps = min(steps, GEN_PER_SEQ - warmup)
+    while n < steps and pos < CACHE - 1:
+        t1 = time.perf_counter()
+        tok, _ = m.decode_step(tok, pos, kc, vc, CACHE)
+        t_dec += time.perf_counter() - t1
+        n += 1
+        pos += 1
+        if t_dec > budget_s:
+            break
+    # @run throughput of the configuration (32-token prompt + 256 generated),
+    # from the measured prompt time and the sampled per-step time
+    e2e = GEN_PER_SEQ / (t_prompt + GEN_PER_SEQ * t_dec / n)
+    return {"tok_s": n / t_dec, "steps": n, "decode_s": t_dec, "prompt_s": t_prompt,
+            "e2e_tok_s": e2e, "threads": O.num_threads(),
+            "first_pos": PROMPT_LEN + warmup}
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def run_reference(args, d: Dist) -> None:
+    """Reference arm: the reference's decode path on host cores.  IREE (the
+    reference's runtime, needed for its llvm-cpu build) is not installed here,
+    so this times the oracle port of that path, all host threads."""
+    if d.rank != 0:
+        return
+    r = cpu_oracle_decode(args.steps, args.warmup, args.seed, budget_s=args.ref_budget)
+    line = {
+        "metric": METRIC, "impl": "reference", "value": r["tok_s"], "unit": UNIT,
+        "n_gpus": args.gpus, "steps": r["steps"], "warmup": args.warmup,
+        "ms_per_step": 1e3 / r["tok_s"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args),
+        "cpu_baseline": {"value": r["tok_s"], "unit": UNIT, "cores": r["threads"], "kind": "port",
+                         "sample": f"{r['steps']} decode steps from position {r['first_pos']} "
+                                   f"after a {PROMPT_LEN}-token prompt, oracle/q3_oracle.c, "
+                                   f"{r['threads']} threads on {cpu_model()}"},
+        "e2e": {"value": r["e2e_tok_s"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args) -> dict:
+    return {"workload": "configs[2]: Qwen3-0.6B Q8_0 greedy decode, batch 1 per GPU, "
+                        f"{PROMPT_LEN}-token prompt, {GEN_PER_SEQ} generated tokens per sequence, "
+                        f"KV cache {CACHE}",
+            "model": "Qwen3-0.6B (random init, Q8_0)", "global_batch": args.gpus,
+            "seq_len": PROMPT_LEN + GEN_PER_SEQ, "parallelism": f"replicas x{args.gpus}",
+            "l2": "inputs larger than L2: all 779 MB of weights are streamed every step"}
+
+
+# ---------------------------------------------------------------- our path
+def run_ours(args, d: Dist) -> None:
+    import q3b200
+    from q3b200.weights import synthetic_weights
+
+    q3b200.set_device(d.local)
+    host = synthetic_weights(seed=args.seed)
+    dw = q3b200.DeviceWeights(host)
+    del host
+    prompt = np.random.default_rng(args.seed).integers(0, 151936, PROMPT_LEN, dtype=np.int64)
+    dec = q3b200.Qwen3Decoder(dw, max_seq_len=CACHE, engine=args.engine)
+    ev = q3b200.Events()
+
+    # warm-up: one short sequence
+    dec.generate_begin(prompt, args.warmup, -1)
+    dec.generate_steps(args.warmup)
+    _, n = dec.generate_end(args.warmup)
+    assert n == args.warmup
+
+    chunks = [min(GEN_PER_SEQ, args.steps - i) for i in range(0, args.steps, GEN_PER_SEQ)]
+    clocks = ClockSampler(d.local)
+    d.barrier()
+    dec.synchronize()
+    clocks.start()
+    launches0 = dec.kernel_launches()
+    total_ms, done, bytes_total = 0.0, 0, 0
+    for c in chunks:
+        dec.generate_begin(prompt, c, -1)           # prompt ingestion: untimed
+        ev.record_start(dec.stream)
+        dec.generate_steps(c)
+        ev.record_end(dec.stream)
+        total_ms += ev.elapsed_ms()
+        _, n = dec.generate_end(c)
+        assert n == c, (n, c)
+        done += c
+        bytes_total += sum(step_bytes(PROMPT_LEN + i) for i in range(c))
+    dec.synchronize()
+    launches = dec.kernel_launches() - launches0
+    clk = clocks.stop()
+    d.barrier()
+    t_max = d.max(total_ms)
+    value = d.sum(done) / (t_max / 1e3)
+
+    # per-kernel device times from an event-instrumented step graph
+    prof_steps = 8
+    prof = q3b200.Qwen3Decoder(dw, max_seq_len=CACHE, engine="graph")
+    prof.generate_begin(prompt, prof_steps + 64, -1)
+    prof.generate_steps(64)
+    times_us, kinds = prof.profile_steps(prof_steps)
+    prof.generate_end(prof_steps + 64)
+    prof.close()
+    ppos = PROMPT_LEN + 64 + prof_steps // 2
+    kern = {}
+    for name_i, name in enumerate(KIND_NAMES):
+        sel = times_us[kinds == name_i]
+        if sel.size == 0:
+            continue
+        if name in Q8_BYTES:
+            b = Q8_BYTES[name] + ACT_BYTES[name]
+        elif name == "vocab":
+            b = VOCAB_BYTES
+        else:
+            b = attn_bytes(ppos)
+        avg = float(sel.mean())
+        kern[name] = {"launches_per_step": int(sel.size), "avg_us": avg,
+                      "total_us_per_step": float(sel.sum()), "alg_bytes_per_launch": b,
+                      "achieved_gbs": b / (avg * 1e-6) / 1e9}
+    step_us = float(times_us.sum())
+    for k in kern.values():
+        k["share"] = k["total_us_per_step"] / step_us
+    peak, peak_kind = load_peaks()
+    peak_src = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s")
+    if dec.engine == "persistent":
+        # one kernel runs every timed step: its launch covers a whole chunk of steps
+        per_step = bytes_total / done
+        ach = per_step / (t_max / done * 1e-3) / 1e9
+        tr = load_traffic().get("persistent_per_step")
+        roof = {"bound": "hbm", "kernel": "k_decode_persistent", "achieved": ach, "peak": peak,
+                "unit": "GB/s", "frac": ach / peak, "traffic": tr,
+                "alg_bytes_per_launch": bytes_total / len(chunks), "traffic_unit": "bytes per step",
+                "peak_source": peak_src}
+    else:
+        dom = max(kern, key=lambda k: kern[k]["total_us_per_step"])
+        roof = {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["achieved_gbs"],
+                "peak": peak, "unit": "GB/s", "frac": kern[dom]["achieved_gbs"] / peak,
+                "traffic": load_traffic().get(dom), "peak_source": peak_src}
+
+    # streaming GEMV bandwidth: 28 layers of one projection in one launch
+    gemv_stream = measure_gemv_stream(q3b200, dw, peak) if not args.quick else {}
+
+    # end to end through the public call (host prompt in, host tokens out)
+    e2e_vals = []
+    for _ in range(3):
+        dec.synchronize()
+        d.barrier()
+        t0 = time.perf_counter()
+        out, n = dec.run(prompt, GEN_PER_SEQ, EOS)
+        dt = time.perf_counter() - t0
+        e2e_vals.append(n / dt)
+    e2e_local = statistics.median(e2e_vals)
+    e2e = d.sum(e2e_local) if d.world > 1 else e2e_local
+    h2d = PROMPT_LEN * 8 + 48
+    d2h = GEN_PER_SEQ * 8 + 48 + 4
+    err = dec.device_error()
+
+    cpu = None
+    if d.world == 1 and not args.no_cpu_baseline:
+        r = cpu_oracle_decode(args.steps, 0, args.seed, budget_s=args.cpu_budget)
+        cpu = {"value": r["tok_s"], "unit": UNIT, "cores": r["threads"], "kind": "port",
+               "sample": f"{r['steps']} decode steps from position {r['first_pos']} after a "
+                         f"{PROMPT_LEN}-token prompt, oracle/q3_oracle.c, {r['threads']} threads "
+                         f"on {cpu_model()}"}
+
+    if d.rank == 0:
+        ms = t_max / (done if done else 1)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": d.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": config_dict(args),
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d / GEN_PER_SEQ,
+                    "d2h_bytes_per_step": d2h / GEN_PER_SEQ,
+                    "call": f"q3_run: {PROMPT_LEN}-token host prompt in, {GEN_PER_SEQ} host "
+                            "tokens out per call, wall clock incl. prompt ingestion"},
+            "gpu_launches": launches,
+            "engine": dec.engine,
+            "step_roofline": {"alg_bytes_per_step": bytes_total / done,
+                              "achieved_gbs": bytes_total / done / (ms * 1e-3) / 1e9,
+                              "frac_of_8tbs": bytes_total / done / (ms * 1e-3) / 1e9 / NOMINAL_HBM_GBS,
+                              "frac_of_measured": bytes_total / done / (ms * 1e-3) / 1e9 / peak},
+            "graph_engine_kernels": kern,
+            "gemv_stream": gemv_stream,
+            "device_error": err,
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+
+
+def measure_gemv_stream(q3b200, dw, peak: float) -> dict:
+    """Each projection over all 28 layers in ONE launch (q3_gemv_q8_layers):
+    the streaming bandwidth of the GEMV kernel without launch gaps."""
+    L = q3b200.lib()
+    out = {}
+    shapes = [("attn_q", "stacked.q8.attn_q.weight", 2048, 1024),
+              ("attn_o", "stacked.q8.attn_output.weight", 1024, 2048),
+              ("gate_up", "stacked.q8.ffn_gate_up.weight", 6144, 1024),
+              ("down", "stacked.q8.ffn_down.weight", 1024, 3072)]
+    ev = q3b200.Events()
+    for name, key, N, K in shapes:
+        w = dw.buffers[key]
+        bpl = N * (K // 32) * 34
+        x = q3b200.DeviceArray.from_host(
+            np.random.default_rng(1).standard_normal((28, K)).astype(np.float16))
+        y = q3b200.DeviceArray((28, N), np.float16)
+        for _ in range(3):
+            assert L.q3_gemv_q8_layers(w.ptr, bpl, x.ptr, y.ptr, N, K, 28, None) == 0
+        reps = 20
+        ev.record_start(None)
+        for _ in range(reps):
+            assert L.q3_gemv_q8_layers(w.ptr, bpl, x.ptr, y.ptr, N, K, 28, None) == 0
+        ev.record_end(None)
+        us = ev.elapsed_ms() * 1e3 / reps
+        b = 28 * (bpl + 2 * K + 2 * N)
+        out[name] = {"us_per_launch": us, "bytes": b, "gbs": b / (us * 1e-6) / 1e9,
+                     "frac_of_measured": b / (us * 1e-6) / 1e9 / peak}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU decode time")
+    ap.add_argument("--ref-budget", type=float, default=60.0, help="seconds, reference arm")
+    ap.add_argument("--quick", action="store_true", help="skip the GEMV streaming sweep")
+    ap.add_argument("--engine", default="graph", choices=["persistent", "graph"])
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    d = Dist() if args.impl == "ours" else None
+    if args.impl == "reference":
+        class _D:
+            rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, _D())
+        return
+    try:
+        run_ours(args, d)
+    finally:
+        d.close()
+
+
+if __name__ == "__main__":
+    main()

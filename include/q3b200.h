@@ -68,6 +68,7 @@ int q3_stream_synchronize(void* stream);
 int q3_event_create(void** event);
 int q3_event_destroy(void* event);
 int q3_event_record(void* event, void* stream);
+int q3_event_synchronize(void* event);
 int q3_event_elapsed_ms(void* start, void* end, float* ms);
 
 /* ------------------------------------------------------------ host math
@@ -223,7 +224,43 @@ int q3_generate_begin(q3_model* m, const int64_t* prompt, int64_t n_prompt, int6
 int q3_generate_steps(q3_model* m, int64_t steps);
 int q3_generate_end(q3_model* m, int64_t* out_tokens, int64_t* n_out);
 
-/* Kernel launches of one generation step (for reporting). */
+/* Per-kernel device times of a generation step: runs `steps` steps of an
+ * instrumented copy of the step graph (a CUDA event recorded between
+ * consecutive kernels) and writes, per kernel in launch order, the average
+ * time in microseconds and its kind (Q3_KIND_*).  Needs cap >= kernels per
+ * step; counts as generation steps of the current generation. */
+#define Q3_KIND_QKV 0     /* RMSNorm + Q|K|V projections */
+#define Q3_KIND_ATTN 1    /* QK-norm + RoPE + KV write + attention */
+#define Q3_KIND_O 2       /* O projection + residual */
+#define Q3_KIND_GATE_UP 3 /* RMSNorm + gate|up + SwiGLU */
+#define Q3_KIND_DOWN 4    /* down projection + residual */
+#define Q3_KIND_VOCAB 5   /* final RMSNorm + vocab GEMV + argmax */
+int q3_model_profile_steps(q3_model* m, int64_t steps, float* times_us, int32_t* kinds,
+                           int64_t cap);
+
+/* Engines.  PERSISTENT: every decode
+ * step of a call runs inside ONE cooperative kernel with one CTA per SM; a
+ * producer warp per CTA streams weight tiles into shared memory ahead of the
+ * grid barriers between phases.  GRAPH (default): the same arithmetic as 141
+ * kernels per step replayed from CUDA graphs with programmatic dependent
+ * launch.  Both give bit-identical results.  Q3_ENGINE=graph|persistent in
+ * the environment selects the engine at creation. */
+#define Q3_ENGINE_GRAPH 0
+#define Q3_ENGINE_PERSISTENT 1
+int q3_model_set_engine(q3_model* m, int engine);
+int q3_model_engine(q3_model* m, int* engine);
+/* Kernels this model has launched so far (all engines). */
+int q3_model_kernel_launches(q3_model* m, int64_t* n);
+
+/* Phase trace of the PERSISTENT engine: runs `steps` generation steps in one
+ * launch and, for step `trace_step`, records per (CTA, phase) four SM clock
+ * global-timer stamps in ns (barrier arrival, barrier release, inputs ready,
+ * work done) into
+ * out[ctas][phases][4] (host; cap entries).  For latency analysis. */
+int q3_model_trace_steps(q3_model* m, int64_t steps, int64_t trace_step, long long* out,
+                         int64_t cap, int* ctas, int* phases);
+
+/* Kernel launches of one generation step of the GRAPH engine. */
 int q3_model_launches_per_step(q3_model* m, int64_t* n);
 /* Device error word of the last run (0: none; see q3_strerror(Q3_ERR_DEVICE)). */
 int q3_model_device_error(q3_model* m, int* code);

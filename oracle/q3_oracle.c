@@ -483,13 +483,12 @@ void q3o_add_f16(const uint16_t* a, const uint16_t* b, uint16_t* y, int n) {
 /* GQA decode attention (model/qwen3_full.mlir:456-530): q head h reads kv
  * head h/2; out = softmax(scale * q.k_t) . v over keys t = 0..T-1, all keys
  * visible (decode mask is all-true), f32 inside, f16 out.  The softmax is
- * evaluated in the blocked order of the CUDA kernel (IREE's own order is not
+ * evaluated in the chunked order of the CUDA kernel (IREE's own order is not
  * pinned): keys fall into chunks of 32; a chunk yields (m, l, o[128]) with
  *   s_t = (fma chain of q_d*k_td over d) * scale,  m = max s_t,
  *   p_t = exp(s_t - m),  l = butterfly sum of p_t,
  *   o_d = fma chain of p_t*v_td over t in key order;
- * chunks merge left to right within splits of 8 chunks, then the split
- * results merge left to right, with
+ * the chunk results are folded left to right with
  *   m = max(ma, mb), a = exp(ma - m), b = exp(mb - m),
  *   l = fma(lb, b, la*a),  o_d = fma(ob_d, b, oa_d*a);
  * finally out_d = f16(o_d / l). */
@@ -515,8 +514,7 @@ void q3o_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, in
     const int kvh = h / 2;
     float qf[Q3O_HD];
     x_to_f32(q + h * Q3O_HD, qf, Q3O_HD);
-    att_part total, split, chunk;
-    int have_total = 0, have_split = 0;
+    att_part total, chunk;
     for (int64_t c = 0; c < nchunks; ++c) {
       float s[32], p[32];
       int valid = 0;
@@ -542,21 +540,10 @@ void q3o_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, in
         const uint16_t* v = vc + (slot0 + c * 32 + l) * row + kvh * Q3O_HD;
         for (int d = 0; d < Q3O_HD; ++d) chunk.o[d] = fmaf(p[l], q3o_h2f(v[d]), chunk.o[d]);
       }
-      if (!have_split) {
-        split = chunk;
-        have_split = 1;
-      } else {
-        att_merge(&split, &chunk);
-      }
-      if ((c + 1) % Q3O_ATT_SPLIT_CHUNKS == 0 || c + 1 == nchunks) {
-        if (!have_total) {
-          total = split;
-          have_total = 1;
-        } else {
-          att_merge(&total, &split);
-        }
-        have_split = 0;
-      }
+      if (c == 0)
+        total = chunk;
+      else
+        att_merge(&total, &chunk);
     }
     for (int d = 0; d < Q3O_HD; ++d) out[h * Q3O_HD + d] = q3o_f2h(total.o[d] / total.l);
   }

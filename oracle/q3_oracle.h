@@ -28,9 +28,8 @@ extern "C" {
 #define Q3O_QBLK 32
 #define Q3O_QBYTES 34
 
-/* attention blocking shared with the CUDA kernel (see q3o_attention) */
+/* attention chunk shared with the CUDA kernel (see q3o_attention) */
 #define Q3O_ATT_CHUNK 32
-#define Q3O_ATT_SPLIT_CHUNKS 8
 
 /* numeric primitives */
 float q3o_h2f(uint16_t h);

@@ -10,6 +10,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <utility>
 #include <thread>
 #include <vector>
 
@@ -17,6 +19,7 @@
 #include "q3_common.cuh"
 #include "q3_gemv.cuh"
 #include "q3_iree.cuh"
+#include "q3_persist.cuh"
 #include "q3b200.h"
 
 using namespace q3;
@@ -169,6 +172,10 @@ extern "C" int q3_event_record(void* e, void* s) {
   Q3_CUDA(cudaEventRecord((cudaEvent_t)e, (cudaStream_t)s));
   return Q3_OK;
 }
+extern "C" int q3_event_synchronize(void* e) {
+  Q3_CUDA(cudaEventSynchronize((cudaEvent_t)e));
+  return Q3_OK;
+}
 extern "C" int q3_event_elapsed_ms(void* a, void* b, float* ms) {
   Q3_REQUIRE(ms, "null out pointer");
   Q3_CUDA(cudaEventElapsedTime(ms, (cudaEvent_t)a, (cudaEvent_t)b));
@@ -248,16 +255,37 @@ static std::mutex g_attr_mu;
 
 template <typename F>
 static int ensure_smem_attr(F* fn, size_t bytes) {
-  // cudaFuncSetAttribute is per device; set the cap once per (function, device).
-  static bool done[64] = {false};
+  // The dynamic shared-memory cap is a per-(kernel, device) attribute; raise it
+  // once for each kernel function (keyed by its address) on each device.
+  static std::set<std::pair<const void*, int>> done;
+  if (bytes <= 48 * 1024) return Q3_OK;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lk(g_attr_mu);
-  if (dev >= 0 && dev < 64 && done[dev]) return Q3_OK;
-  (void)bytes;
+  const auto key = std::make_pair((const void*)fn, dev);
+  if (done.count(key)) return Q3_OK;
   Q3_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDynSmem));
-  if (dev >= 0 && dev < 64) done[dev] = true;
+  done.insert(key);
   return Q3_OK;
+}
+
+// Launch with optional programmatic dependent launch (PDL): the kernel may
+// begin while the previous kernel in the stream finishes; kernels call
+// griddepcontrol.wait before touching that kernel's outputs.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
 struct LaunchShape {
@@ -286,7 +314,7 @@ static LaunchShape stream_shape(int ntiles, uint32_t tile_bytes, int ctas_per_sm
 }
 
 template <int G, int ORDER, int MODE>
-static int launch_q8_t(Q8GemvArgs a, cudaStream_t st, int* launches) {
+static int launch_q8_t(Q8GemvArgs a, cudaStream_t st, int* launches, bool pdl) {
   const uint32_t rowbytes = (uint32_t)(a.K / kQBlk) * kQBytes;
   const uint32_t tile_bytes = rowbytes * kTileRows * (MODE == kModeSwiglu ? 2u : 1u);
   const int ntiles = a.nseg * (a.seg_rows / kTileRows);
@@ -294,18 +322,18 @@ static int launch_q8_t(Q8GemvArgs a, cudaStream_t st, int* launches) {
   a.nstages = ls.nstages;
   int rc = ensure_smem_attr(k_gemv_q8<G, ORDER, MODE>, ls.smem);
   if (rc) return rc;
-  k_gemv_q8<G, ORDER, MODE><<<ls.grid, kGemvThreads, ls.smem, st>>>(a);
-  Q3_LAUNCHED();
+  Q3_CUDA(launch_ex(k_gemv_q8<G, ORDER, MODE>, dim3(ls.grid), dim3(kGemvThreads), ls.smem, st, pdl,
+                    a));
   if (launches) ++*launches;
   return Q3_OK;
 }
 
 template <int ORDER, int MODE>
-static int launch_q8(const Q8GemvArgs& a, cudaStream_t st, int* launches) {
+static int launch_q8(const Q8GemvArgs& a, cudaStream_t st, int* launches, bool pdl = false) {
   switch ((a.K + 1023) / 1024) {
-    case 1: return launch_q8_t<1, ORDER, MODE>(a, st, launches);
-    case 2: return launch_q8_t<2, ORDER, MODE>(a, st, launches);
-    case 3: return launch_q8_t<3, ORDER, MODE>(a, st, launches);
+    case 1: return launch_q8_t<1, ORDER, MODE>(a, st, launches, pdl);
+    case 2: return launch_q8_t<2, ORDER, MODE>(a, st, launches, pdl);
+    case 3: return launch_q8_t<3, ORDER, MODE>(a, st, launches, pdl);
     default: return set_err(Q3_ERR_UNSUPPORTED, "K=%d above 3072", a.K);
   }
 }
@@ -399,15 +427,14 @@ extern "C" size_t q3_vocab_argmax_workspace_bytes(void) {
   return sizeof(ArgmaxPartial) * kArgmaxMaxGrid + 256;
 }
 
-static int launch_vocab(VocabArgs a, cudaStream_t st, int* launches) {
+static int launch_vocab(VocabArgs a, cudaStream_t st, int* launches, bool pdl = false) {
   const uint32_t tile_bytes = (uint32_t)a.K * 2u * kTileRows;
   LaunchShape ls = stream_shape(a.N / kTileRows, tile_bytes, 2);
   if (ls.grid > kArgmaxMaxGrid) ls.grid = kArgmaxMaxGrid;
   a.nstages = ls.nstages;
   int rc = ensure_smem_attr(k_vocab_argmax, ls.smem);
   if (rc) return rc;
-  k_vocab_argmax<<<ls.grid, kGemvThreads, ls.smem, st>>>(a);
-  Q3_LAUNCHED();
+  Q3_CUDA(launch_ex(k_vocab_argmax, dim3(ls.grid), dim3(kGemvThreads), ls.smem, st, pdl, a));
   if (launches) ++*launches;
   return Q3_OK;
 }
@@ -433,17 +460,21 @@ extern "C" int q3_vocab_argmax(const void* w, const void* x, const void* gamma, 
 }
 
 // attention -----------------------------------------------------------------
-static int max_splits_for(int64_t S) { return (int)((S + kAttSplit - 1) / kAttSplit); }
-
-extern "C" size_t q3_attention_workspace_bytes(int64_t S) {
-  const int ms = max_splits_for(S < 1 ? 1 : S);
-  return sizeof(AttnPartial) * (size_t)kNKV * ms * 2 + 256;
+// Chunks of 32 keys a cache of S positions can hold, and 8-chunk groups.
+static int max_chunks_for(int64_t S) { return (int)((S + kAttChunk - 1) / kAttChunk); }
+static int max_groups_for(int64_t S) {
+  return (max_chunks_for(S) + kAttSplitChunks - 1) / kAttSplitChunks;
 }
 
-static int launch_attn(const AttnArgs& a, int batch, cudaStream_t st, int* launches) {
-  dim3 grid(kNKV, a.max_splits, batch);
-  k_attn_decode<<<grid, 256, 0, st>>>(a);
-  Q3_LAUNCHED();
+extern "C" size_t q3_attention_workspace_bytes(int64_t S) {
+  const int mc = max_chunks_for(S < 1 ? 1 : S);
+  return sizeof(AttnPartial) * (size_t)kNKV * mc * 2 + 256;
+}
+
+static int launch_attn(const AttnArgs& a, int batch, cudaStream_t st, int* launches,
+                       bool pdl = false) {
+  dim3 grid(kNKV, (unsigned)max_groups_for((int64_t)a.max_chunks * kAttChunk), batch);
+  Q3_CUDA(launch_ex(k_attn_decode, grid, dim3(256), 0, st, pdl, a));
   if (launches) ++*launches;
   return Q3_OK;
 }
@@ -472,9 +503,9 @@ extern "C" int q3_decode_attention(const void* qkv, const void* q_norm, const vo
   a.pos = pos;
   a.pos_stride = 1;
   a.out = (uint16_t*)out;
-  a.max_splits = max_splits_for(S);
+  a.max_chunks = max_chunks_for(S);
   a.part = (AttnPartial*)ws;
-  a.counters = (unsigned int*)((uint8_t*)ws + sizeof(AttnPartial) * (size_t)kNKV * a.max_splits * 2);
+  a.counters = (unsigned int*)((uint8_t*)ws + sizeof(AttnPartial) * (size_t)kNKV * a.max_chunks * 2);
   return launch_attn(a, 1, (cudaStream_t)stream, nullptr);
 }
 
@@ -557,17 +588,49 @@ struct q3_model {
   SeqState* h_st = nullptr;
   int64_t* h_tokens = nullptr;
   // graphs
-  cudaGraphExec_t g_ingest = nullptr, g_gen = nullptr;
+  cudaGraphExec_t g_ingest = nullptr, g_gen = nullptr, g_prof = nullptr;
   int launches_gen = 0, launches_ingest = 0;
+  std::vector<cudaEvent_t> prof_events;
+  std::vector<int32_t> prof_kinds;
   // generation bookkeeping
   int64_t gen_n_prompt = 0, gen_pos0 = 0, gen_max = 0;
   bool gen_active = false;
   // chat
+  // engines: CUDA graphs of per-phase kernels, or one persistent kernel
+  int engine = Q3_ENGINE_GRAPH;  // measured faster at batch 1 for now
+  int persist_grid = 0;          // CTAs of the persistent kernel (one per SM)
+  unsigned int* grid_ctr = nullptr;
+  int64_t kernel_launches = 0;   // kernels launched by this model so far
+  long long* trace_dev = nullptr; // persistent-kernel phase trace (when tracing)
+  int trace_step = -1;
   bool chat_ready = false;
   int64_t chat_pos = 0, chat_max = 0;
 };
 
-static int enqueue_layers(q3_model* m, bool ingest, int* launches) {
+// Optional instrumentation while capturing: after every kernel an event is
+// recorded and the kernel's kind appended (profiling graph only).
+struct StepProbe {
+  std::vector<cudaEvent_t>* events = nullptr;
+  std::vector<int32_t>* kinds = nullptr;
+};
+
+static int probe_mark(const StepProbe* pr, cudaStream_t st, int kind) {
+  if (!pr || !pr->events) return Q3_OK;
+  cudaEvent_t e;
+  Q3_CUDA(cudaEventCreate(&e));
+  pr->events->push_back(e);
+  pr->kinds->push_back(kind);
+  Q3_CUDA(cudaEventRecordWithFlags(e, st, cudaEventRecordExternal));
+  return Q3_OK;
+}
+
+#define Q3_PROBE(kind)                          \
+  do {                                          \
+    int rc_ = probe_mark(probe, st, (kind));    \
+    if (rc_) return rc_;                        \
+  } while (0)
+
+static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepProbe* probe) {
   cudaStream_t st = m->stream;
   const int32_t* stop = &m->st->stop;
   for (int l = 0; l < kLayers; ++l) {
@@ -593,8 +656,9 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches) {
       a.embd = (const uint16_t*)m->w.token_embd;
       a.embed_out = m->x;
     }
-    int rc = launch_q8<kOrderMlir, kModeNormIn>(a, st, launches);
+    int rc = launch_q8<kOrderMlir, kModeNormIn>(a, st, launches, true);
     if (rc) return rc;
+    Q3_PROBE(Q3_KIND_QKV);
     // 2) QK-norm + RoPE + KV write + attention
     AttnArgs t;
     memset(&t, 0, sizeof(t));
@@ -612,19 +676,21 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches) {
     t.pos_stride = 1;
     t.stop = stop;
     t.out = m->attn;
-    t.max_splits = max_splits_for(m->S);
+    t.max_chunks = max_chunks_for(m->S);
     t.part = m->att_part;
     t.counters = m->att_counters;
     t.err = m->err;
-    rc = launch_attn(t, 1, st, launches);
+    rc = launch_attn(t, 1, st, launches, true);
     if (rc) return rc;
+    Q3_PROBE(Q3_KIND_ATTN);
     // 3) O projection + residual: h1 = x + W_o . attn
     a = q8_args_single((const uint8_t*)m->w.q8_attn_output + l * kBplO, m->attn, m->h1, m->x,
                        1024, 2048);
     a.seq = m->st;
     a.err = m->err;
-    rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches);
+    rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches, true);
     if (rc) return rc;
+    Q3_PROBE(Q3_KIND_O);
     // 4) RMSNorm + gate|up + SwiGLU: act = swiglu(W_gu . rmsnorm(h1))
     a = q8_args_single((const uint8_t*)m->w.q8_ffn_gate_up + l * kBplGU, m->h1, m->act, nullptr,
                        3072, 1024);
@@ -632,21 +698,24 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches) {
     a.up_off_bytes = 3072 * rb;
     a.seq = m->st;
     a.err = m->err;
-    rc = launch_q8<kOrderMlir, kModeSwiglu>(a, st, launches);
+    rc = launch_q8<kOrderMlir, kModeSwiglu>(a, st, launches, true);
     if (rc) return rc;
+    Q3_PROBE(Q3_KIND_GATE_UP);
     // 5) down projection + residual: x = h1 + W_d . act
     a = q8_args_single((const uint8_t*)m->w.q8_ffn_down + l * kBplD, m->act, m->x, m->h1, 1024,
                        3072);
     a.seq = m->st;
     a.err = m->err;
     if (ingest && l == kLayers - 1) a.advance = m->st;
-    rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches);
+    rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches, true);
     if (rc) return rc;
+    Q3_PROBE(Q3_KIND_DOWN);
   }
   return Q3_OK;
 }
 
-static int enqueue_vocab(q3_model* m, int* launches) {
+static int enqueue_vocab(q3_model* m, int* launches, const StepProbe* probe) {
+  cudaStream_t st = m->stream;
   VocabArgs v;
   memset(&v, 0, sizeof(v));
   v.w = (const uint16_t*)m->w.output_T;
@@ -660,15 +729,20 @@ static int enqueue_vocab(q3_model* m, int* launches) {
   v.seq = m->st;
   v.tokens = m->tokens;
   v.err = m->err;
-  return launch_vocab(v, m->stream, launches);
+  int rc = launch_vocab(v, st, launches, true);
+  if (rc) return rc;
+  Q3_PROBE(Q3_KIND_VOCAB);
+  return Q3_OK;
 }
 
-static int capture(q3_model* m, bool ingest, cudaGraphExec_t* out, int* launches) {
+static int capture(q3_model* m, bool ingest, cudaGraphExec_t* out, int* launches,
+                   const StepProbe* probe = nullptr) {
   cudaGraph_t g = nullptr;
   Q3_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
   int n = 0;
-  int rc = enqueue_layers(m, ingest, &n);
-  if (rc == Q3_OK && !ingest) rc = enqueue_vocab(m, &n);
+  int rc = probe_mark(probe, m->stream, -1);
+  if (rc == Q3_OK) rc = enqueue_layers(m, ingest, &n, probe);
+  if (rc == Q3_OK && !ingest) rc = enqueue_vocab(m, &n, probe);
   cudaError_t e = cudaStreamEndCapture(m->stream, &g);
   if (rc) {
     if (g) cudaGraphDestroy(g);
@@ -686,8 +760,11 @@ static void model_free(q3_model* m) {
   if (!m) return;
   if (m->g_ingest) cudaGraphExecDestroy(m->g_ingest);
   if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
+  if (m->g_prof) cudaGraphExecDestroy(m->g_prof);
+  for (cudaEvent_t e : m->prof_events) cudaEventDestroy(e);
   void* dev[] = {m->kc, m->vc, m->rope_cos, m->rope_sin, m->x, m->qkv, m->attn, m->h1, m->act,
-                 m->logits, m->tokens, m->st, m->am_part, m->att_part, m->err};
+                 m->logits, m->tokens, m->st, m->am_part, m->att_part, m->err, m->grid_ctr,
+                 m->trace_dev};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (m->h_st) cudaFreeHost(m->h_st);
@@ -706,6 +783,22 @@ static void model_free(q3_model* m) {
                      #ptr, cudaGetErrorString(e_));                                  \
     }                                                                                \
   } while (0)
+
+// The persistent engine needs one co-resident CTA per SM (cooperative launch).
+static int persist_setup(q3_model* m) {
+  Q3_CUDA(cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kPersistSmem));
+  int per_sm = 0;
+  Q3_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent,
+                                                          kGemvThreads, kPersistSmem));
+  int coop = 0;
+  Q3_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device));
+  m->persist_grid = (per_sm >= 1 && coop) ? current_sms() : 0;
+  if (m->persist_grid > kArgmaxMaxGrid) m->persist_grid = 0;
+  Q3_CUDA(cudaMalloc((void**)&m->grid_ctr, 256));
+  Q3_CUDA(cudaMemset(m->grid_ctr, 0, 256));
+  return Q3_OK;
+}
 
 extern "C" int q3_model_create(const q3_weights* w, int64_t S, void* stream, q3_model** out) {
   Q3_REQUIRE(w && out, "null pointer");
@@ -753,7 +846,7 @@ extern "C" int q3_model_create(const q3_weights* w, int64_t S, void* stream, q3_
   m->am_counter = (unsigned int*)((uint8_t*)m->am_part + sizeof(ArgmaxPartial) * kArgmaxMaxGrid);
   Q3_MALLOC(m->att_part, q3_attention_workspace_bytes(S));
   m->att_counters = (unsigned int*)((uint8_t*)m->att_part +
-                                    sizeof(AttnPartial) * (size_t)kNKV * max_splits_for(S) * 2);
+                                    sizeof(AttnPartial) * (size_t)kNKV * max_chunks_for(S) * 2);
   Q3_MALLOC(m->err, sizeof(int));
   if (cudaMallocHost((void**)&m->h_st, sizeof(SeqState)) != cudaSuccess ||
       cudaMallocHost((void**)&m->h_tokens, (size_t)(S + 1) * sizeof(int64_t)) != cudaSuccess) {
@@ -778,11 +871,38 @@ extern "C" int q3_model_create(const q3_weights* w, int64_t S, void* stream, q3_
   chk(cudaStreamSynchronize(m->stream));
   if (rc == Q3_OK) rc = capture(m, true, &m->g_ingest, &m->launches_ingest);
   if (rc == Q3_OK) rc = capture(m, false, &m->g_gen, &m->launches_gen);
+  if (rc == Q3_OK) rc = persist_setup(m);
   if (rc != Q3_OK) {
     model_free(m);
     return rc;
   }
+  const char* env = getenv("Q3_ENGINE");
+  if (env && strcmp(env, "graph") == 0) m->engine = Q3_ENGINE_GRAPH;
+  if (env && strcmp(env, "persistent") == 0 && m->persist_grid > 0) m->engine = Q3_ENGINE_PERSISTENT;
+  if (m->persist_grid == 0) m->engine = Q3_ENGINE_GRAPH;
   *out = m;
+  return Q3_OK;
+}
+
+extern "C" int q3_model_set_engine(q3_model* m, int engine) {
+  Q3_REQUIRE(m, "null model");
+  Q3_REQUIRE(engine == Q3_ENGINE_GRAPH || engine == Q3_ENGINE_PERSISTENT, "unknown engine %d",
+             engine);
+  if (engine == Q3_ENGINE_PERSISTENT && m->persist_grid == 0)
+    return set_err(Q3_ERR_UNSUPPORTED, "the persistent kernel cannot be co-resident here");
+  m->engine = engine;
+  return Q3_OK;
+}
+
+extern "C" int q3_model_engine(q3_model* m, int* engine) {
+  Q3_REQUIRE(m && engine, "null pointer");
+  *engine = m->engine;
+  return Q3_OK;
+}
+
+extern "C" int q3_model_kernel_launches(q3_model* m, int64_t* n) {
+  Q3_REQUIRE(m && n, "null pointer");
+  *n = m->kernel_launches;
   return Q3_OK;
 }
 
@@ -828,9 +948,71 @@ static int seq_begin(q3_model* m, const int64_t* toks, int64_t pos0, int64_t n, 
   return Q3_OK;
 }
 
+// Enqueue n_ingest prompt steps (no vocab head) then n_gen steps that end
+// with the vocab head + argmax, on the model's engine.
 static int launch_graphs(q3_model* m, int64_t n_ingest, int64_t n_gen) {
+  if (n_ingest + n_gen == 0) return Q3_OK;
+  if (m->engine == Q3_ENGINE_PERSISTENT) {
+    PersistArgs a;
+    memset(&a, 0, sizeof(a));
+    a.token_embd = (const uint16_t*)m->w.token_embd;
+    a.output_norm = (const uint16_t*)m->w.output_norm;
+    a.output_T = (const uint16_t*)m->w.output_T;
+    a.attn_norm = (const uint16_t*)m->w.attn_norm;
+    a.ffn_norm = (const uint16_t*)m->w.ffn_norm;
+    a.q_norm = (const uint16_t*)m->w.attn_q_norm;
+    a.k_norm = (const uint16_t*)m->w.attn_k_norm;
+    a.wq = (const uint8_t*)m->w.q8_attn_q;
+    a.wk = (const uint8_t*)m->w.q8_attn_k;
+    a.wv = (const uint8_t*)m->w.q8_attn_v;
+    a.wo = (const uint8_t*)m->w.q8_attn_output;
+    a.wgu = (const uint8_t*)m->w.q8_ffn_gate_up;
+    a.wd = (const uint8_t*)m->w.q8_ffn_down;
+    a.kc = m->kc;
+    a.vc = m->vc;
+    a.rope_cos = m->rope_cos;
+    a.rope_sin = m->rope_sin;
+    a.S = m->S;
+    a.x = m->x;
+    a.qkv = m->qkv;
+    a.attn = m->attn;
+    a.h1 = m->h1;
+    a.act = m->act;
+    a.logits = m->logits;
+    a.tokens = m->tokens;
+    a.seq = m->st;
+    a.am_part = m->am_part;
+    a.am_counter = m->am_counter;
+    a.att_part = m->att_part;
+    a.att_counters = m->att_counters;
+    a.max_chunks = max_chunks_for(m->S);
+    a.grid_ctr = m->grid_ctr;
+    a.err = m->err;
+    a.n_steps = (int)(n_ingest + n_gen);
+    a.vocab_from = (int)n_ingest;
+    a.trace = m->trace_dev;
+    a.trace_step = m->trace_step;
+    // counters start at zero (they re-arm themselves, unless a run was cut short)
+    Q3_CUDA(cudaMemsetAsync(m->grid_ctr, 0, sizeof(unsigned int), m->stream));
+    Q3_CUDA(cudaMemsetAsync(m->am_counter, 0, sizeof(unsigned int), m->stream));
+    Q3_CUDA(cudaMemsetAsync(m->att_counters, 0, kNKV * sizeof(unsigned int), m->stream));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(m->persist_grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = kPersistSmem;
+    cfg.stream = m->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q3_CUDA(cudaLaunchKernelEx(&cfg, k_decode_persistent, a));
+    m->kernel_launches += 1;
+    return Q3_OK;
+  }
   for (int64_t i = 0; i < n_ingest; ++i) Q3_CUDA(cudaGraphLaunch(m->g_ingest, m->stream));
   for (int64_t i = 0; i < n_gen; ++i) Q3_CUDA(cudaGraphLaunch(m->g_gen, m->stream));
+  m->kernel_launches += n_ingest * m->launches_ingest + n_gen * m->launches_gen;
   return Q3_OK;
 }
 
@@ -955,4 +1137,60 @@ extern "C" int q3_chat_turn(q3_model* m, const int64_t* toks, int64_t n, int64_t
   // model/qwen3_full.mlir:2216-2218: current_pos = new_pos + (count + 1)
   m->chat_pos = p0 + n + got + 1;
   return Q3_OK;
+}
+
+extern "C" int q3_model_profile_steps(q3_model* m, int64_t steps, float* times_us, int32_t* kinds,
+                                      int64_t cap) {
+  Q3_REQUIRE(m && times_us && kinds && steps >= 1, "bad arguments");
+  if (!m->gen_active) return set_err(Q3_ERR_STATE, "no generation in progress");
+  if (!m->g_prof) {
+    StepProbe pr{&m->prof_events, &m->prof_kinds};
+    int n = 0;
+    int rc = capture(m, false, &m->g_prof, &n, &pr);
+    if (rc) return rc;
+  }
+  const int64_t nk = (int64_t)m->prof_events.size() - 1;
+  Q3_REQUIRE(cap >= nk, "cap %lld below the %lld kernels of a step", (long long)cap, (long long)nk);
+  std::vector<double> acc((size_t)nk, 0.0);
+  for (int64_t s = 0; s < steps; ++s) {
+    Q3_CUDA(cudaGraphLaunch(m->g_prof, m->stream));
+    Q3_CUDA(cudaStreamSynchronize(m->stream));
+    for (int64_t i = 0; i < nk; ++i) {
+      float ms = 0.0f;
+      Q3_CUDA(cudaEventElapsedTime(&ms, m->prof_events[i], m->prof_events[i + 1]));
+      acc[(size_t)i] += ms;
+    }
+  }
+  for (int64_t i = 0; i < nk; ++i) {
+    times_us[i] = (float)(acc[(size_t)i] / (double)steps * 1000.0);
+    kinds[i] = m->prof_kinds[(size_t)i + 1];
+  }
+  return Q3_OK;
+}
+
+extern "C" int q3_model_trace_steps(q3_model* m, int64_t steps, int64_t trace_step,
+                                    long long* out, int64_t cap, int* ctas, int* phases) {
+  Q3_REQUIRE(m && out && ctas && phases && steps >= 1, "bad arguments");
+  Q3_REQUIRE(trace_step >= 0 && trace_step < steps, "trace_step outside the launch");
+  if (!m->gen_active) return set_err(Q3_ERR_STATE, "no generation in progress");
+  if (m->engine != Q3_ENGINE_PERSISTENT) return set_err(Q3_ERR_STATE, "tracing needs the persistent engine");
+  const int64_t n = (int64_t)m->persist_grid * kTracePhases * 4;
+  Q3_REQUIRE(cap >= n, "cap %lld below %lld", (long long)cap, (long long)n);
+  if (!m->trace_dev) Q3_CUDA(cudaMalloc((void**)&m->trace_dev, (size_t)n * sizeof(long long)));
+  Q3_CUDA(cudaMemsetAsync(m->trace_dev, 0, (size_t)n * sizeof(long long), m->stream));
+  m->trace_step = (int)trace_step;
+  int rc = launch_graphs(m, 0, steps);
+  m->trace_step = -1;
+  long long* dev = m->trace_dev;
+  m->trace_dev = nullptr;
+  if (rc == Q3_OK) {
+    cudaError_t e = cudaMemcpyAsync(out, dev, (size_t)n * sizeof(long long), cudaMemcpyDeviceToHost,
+                                    m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) rc = set_err(Q3_ERR_CUDA, "trace copy: %s", cudaGetErrorString(e));
+  }
+  m->trace_dev = dev;
+  *ctas = m->persist_grid;
+  *phases = kTracePhases;
+  return rc;
 }

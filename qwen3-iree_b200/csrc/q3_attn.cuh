@@ -1,4 +1,4 @@
-// q3_attn.cuh -- GQA decode attention for sm_100a (one launch per layer).
+// q3_attn.cuh -- GQA decode attention for sm_100a.
 //
 // Replaces, for one layer and one or more independent sequences:
 //   QK-RMSNorm (model/qwen3_full.mlir:646-702), RoPE (:324-454), the KV-cache
@@ -6,13 +6,14 @@
 //   keys 0..pos (:456-530), with the reference's whole-slice KV copy
 //   (:715-720) removed: the kernel attends straight out of the flat cache.
 //
-// Split-KV flash decode.  CTA (kv head h, split s, sequence b) owns keys
-// [256 s, 256 s + 256); each of its 8 warps takes one chunk of 32 keys
-// (lane = key for q.k, lane = 4 head dims for p.v), both q heads 2h, 2h+1
-// at once so every K/V row is read once.  Chunk results merge left to right
-// inside the CTA; split results merge left to right in the last CTA to
-// finish (a counter per (sequence, kv head), no spin-waits).  The CPU oracle
-// (q3o_attention) states the same order.
+// Flash decode over chunks of 32 keys.  A group (one CTA, 8 warps) owns 8
+// consecutive chunks of one kv head h; each warp turns one chunk into a
+// partial (m, l, o[128]) for both q heads 2h and 2h+1, so every K/V row is
+// read once (lane = key for q.k, lane = 4 head dims for p.v; all loads of a
+// chunk are issued before its arithmetic).  The CTA that finishes last for
+// head h (an arrival counter, no spin-waits) folds all chunk partials of h
+// left to right.  The CPU oracle (q3o_attention) states the same order, so
+// any assignment of groups to CTAs gives the same bits.
 #pragma once
 
 #include "q3_common.cuh"
@@ -20,9 +21,10 @@
 
 namespace q3 {
 
-struct AttnPartial {
-  float m, l;
+struct AttnPartial {  // 528 bytes: o first so the float4 accesses stay 16-byte aligned
   float o[kHD];
+  float m, l;
+  float pad[2];
 };
 
 struct AttnArgs {
@@ -44,11 +46,39 @@ struct AttnArgs {
   int stop_stride;
   uint16_t* out;            // [B][2048] f16
   int64_t out_stride;
-  AttnPartial* part;        // [B][8][max_splits][2]
+  AttnPartial* part;        // [B][8][max_chunks][2] chunk partials
   unsigned int* counters;   // [B][8], zero between launches
-  int max_splits;
+  int max_chunks;           // >= ceil(S / 32)
   int* err;
 };
+
+// Everything one group needs about one (sequence, layer).
+struct AttnCtx {
+  const uint16_t* qkv;
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  const float* ct;  // RoPE cos row at pos
+  const float* sn;  // RoPE sin row at pos
+  uint16_t* kc;
+  uint16_t* vc;
+  int64_t slot0;
+  int64_t pos;
+  uint16_t* out;
+  AttnPartial* part;      // [8][max_chunks][2]
+  unsigned int* counters; // [8]
+  int max_chunks;
+};
+
+struct AttnSmem {
+  uint16_t qs[2][kHD];
+  uint16_t ks[kHD];
+  int last;
+};
+
+__device__ __forceinline__ int attn_nchunks(int64_t pos) { return (int)((pos + kAttChunk) / kAttChunk); }
+__device__ __forceinline__ int attn_ngroups(int64_t pos) {
+  return (attn_nchunks(pos) + kAttSplitChunks - 1) / kAttSplitChunks;
+}
 
 // Per-head RMSNorm (f16 out) then NeoX RoPE (f16 out) for one 128-wide head.
 // Lane l produces outputs l, l+32, l+64, l+96.
@@ -57,7 +87,7 @@ __device__ __forceinline__ void head_norm_rope(const uint16_t* x, const uint16_t
                                                uint16_t* dst) {
   float v[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) v[i] = h2f(x[lane + 32 * i]);
+  for (int i = 0; i < 4; ++i) v[i] = h2f(__ldcg(reinterpret_cast<const unsigned short*>(x) + lane + 32 * i));
   float ss = 0.0f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) ss = __fmaf_rn(v[i], v[i], ss);
@@ -84,75 +114,71 @@ __device__ __forceinline__ void att_merge(float& m, float& l, float (&o)[4], flo
   m = mm;
 }
 
-__global__ void __launch_bounds__(256) k_attn_decode(const __grid_constant__ AttnArgs a) {
-  __shared__ __align__(16) uint16_t qs[2][kHD];
-  __shared__ __align__(16) uint16_t ks[kHD];
-  __shared__ AttnPartial cp[kAttSplitChunks][2];
-  __shared__ int is_last;
-  const int h = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
+// One group (kv head h, chunks 8g .. 8g+7) on the 256 consumer threads of a
+// CTA.  Must be called by all of them.  Returns after the head's output is
+// written if this CTA was the last of head h, else after its partials are.
+__device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnSmem& sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (a.stop != nullptr && a.stop[(int64_t)b * a.stop_stride] != 0) return;
-  const int64_t pos = a.pos[(int64_t)b * a.pos_stride];
-  if (pos < 0 || pos >= a.S || pos >= a.rope_pos) {
-    if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
-    return;
-  }
-  const int64_t T = pos + 1;
-  const int nsplit = (int)((T + kAttSplit - 1) / kAttSplit);
-  if (split >= nsplit) return;
-
-  const uint16_t* qkv = a.qkv + (int64_t)b * a.qkv_stride;
-  uint16_t* kc = a.kc + (int64_t)b * a.cache_stride;
-  uint16_t* vc = a.vc + (int64_t)b * a.cache_stride;
-  const float* ct = a.rope_cos + pos * 64;
-  const float* sn = a.rope_sin + pos * 64;
+  const int64_t pos = c.pos, T = pos + 1;
+  const int nch = attn_nchunks(pos);
+  const int ngroups = attn_ngroups(pos);
+  const int64_t rowel = (int64_t)kNKV * kHD;
 
   // 1) q heads 2h, 2h+1 and k head h: norm + rope into shared memory
   if (warp < 3) {
-    const float c0 = ct[lane], s0 = sn[lane], c1 = ct[lane + 32], s1 = sn[lane + 32];
+    const float c0 = c.ct[lane], s0 = c.sn[lane], c1 = c.ct[lane + 32], s1 = c.sn[lane + 32];
     if (warp < 2)
-      head_norm_rope(qkv + (2 * h + warp) * kHD, a.q_norm, c0, s0, c1, s1, lane, qs[warp]);
+      head_norm_rope(c.qkv + (2 * h + warp) * kHD, c.q_norm, c0, s0, c1, s1, lane, sm.qs[warp]);
     else
-      head_norm_rope(qkv + 2048 + h * kHD, a.k_norm, c0, s0, c1, s1, lane, ks);
+      head_norm_rope(c.qkv + 2048 + h * kHD, c.k_norm, c0, s0, c1, s1, lane, sm.ks);
   }
-  __syncthreads();
-  // 2) the CTA holding key `pos` writes the new K (normed, roped) and V rows
-  const int64_t rowel = (int64_t)kNKV * kHD;
-  if (split == nsplit - 1 && threadIdx.x < kHD) {
-    const int64_t off = (a.slot0 + pos) * rowel + h * kHD + threadIdx.x;
-    kc[off] = ks[threadIdx.x];
-    vc[off] = qkv[3072 + h * kHD + threadIdx.x];
+  consumer_sync();
+  // 2) the group holding key `pos` writes the new K (normed, roped) and V rows
+  if (g == ngroups - 1 && threadIdx.x < kHD) {
+    const int64_t off = (c.slot0 + pos) * rowel + h * kHD + threadIdx.x;
+    c.kc[off] = sm.ks[threadIdx.x];
+    c.vc[off] = __ldcg(reinterpret_cast<const unsigned short*>(c.qkv) + 3072 + h * kHD + threadIdx.x);
   }
-  __syncthreads();
+  consumer_sync();
 
-  // 3) one chunk of 32 keys per warp
-  const int64_t t0 = (int64_t)(split * kAttSplitChunks + warp) * kAttChunk;
-  if (t0 < T) {
+  // 3) one chunk of 32 keys per warp -> its partial in global memory
+  const int ci = g * kAttSplitChunks + warp;
+  if (ci < nch) {
+    const int64_t t0 = (int64_t)ci * kAttChunk;
     const int64_t t = t0 + lane;
     const bool valid = t < T;
+    const int nvalid = (int)((T - t0) < kAttChunk ? (T - t0) : kAttChunk);
+    // issue every load of the chunk first: this lane's K row, and 4 dims of all V rows
+    uint4 kv[kHD / 8];
+    const uint4* kr = reinterpret_cast<const uint4*>(c.kc + (c.slot0 + (valid ? t : t0)) * rowel + h * kHD);
+#pragma unroll
+    for (int v = 0; v < kHD / 8; ++v) kv[v] = __ldcg(kr + v);
+    uint2 vv[kAttChunk];
+    const uint16_t* vbase = c.vc + (c.slot0 + t0) * rowel + h * kHD + 4 * lane;
+#pragma unroll
+    for (int tt = 0; tt < kAttChunk; ++tt)
+      vv[tt] = tt < nvalid ? __ldcg(reinterpret_cast<const uint2*>(vbase + (int64_t)tt * rowel))
+                           : make_uint2(0u, 0u);
     float s[2] = {-__int_as_float(0x7f800000), -__int_as_float(0x7f800000)};
     if (valid) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kc + (a.slot0 + t) * rowel + h * kHD);
-      const uint4* q0 = reinterpret_cast<const uint4*>(qs[0]);
-      const uint4* q1 = reinterpret_cast<const uint4*>(qs[1]);
+      const uint4* q0 = reinterpret_cast<const uint4*>(sm.qs[0]);
+      const uint4* q1 = reinterpret_cast<const uint4*>(sm.qs[1]);
       float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll 4
+#pragma unroll
       for (int v = 0; v < kHD / 8; ++v) {
-        const uint4 kv = kr[v];
         const uint4 x0 = q0[v], x1 = q1[v];
-        a0 = fma_h2(x0.x, kv.x, a0);
-        a0 = fma_h2(x0.y, kv.y, a0);
-        a0 = fma_h2(x0.z, kv.z, a0);
-        a0 = fma_h2(x0.w, kv.w, a0);
-        a1 = fma_h2(x1.x, kv.x, a1);
-        a1 = fma_h2(x1.y, kv.y, a1);
-        a1 = fma_h2(x1.z, kv.z, a1);
-        a1 = fma_h2(x1.w, kv.w, a1);
+        a0 = fma_h2(x0.x, kv[v].x, a0);
+        a0 = fma_h2(x0.y, kv[v].y, a0);
+        a0 = fma_h2(x0.z, kv[v].z, a0);
+        a0 = fma_h2(x0.w, kv[v].w, a0);
+        a1 = fma_h2(x1.x, kv[v].x, a1);
+        a1 = fma_h2(x1.y, kv[v].y, a1);
+        a1 = fma_h2(x1.z, kv[v].z, a1);
+        a1 = fma_h2(x1.w, kv[v].w, a1);
       }
       s[0] = __fmul_rn(a0, kAttnScale);
       s[1] = __fmul_rn(a1, kAttnScale);
     }
-    const int nvalid = (int)((T - t0) < kAttChunk ? (T - t0) : kAttChunk);
     float m[2], p[2], l[2];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -161,96 +187,95 @@ __global__ void __launch_bounds__(256) k_attn_decode(const __grid_constant__ Att
       l[hh] = warp_sum(p[hh]);
     }
     float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint16_t* vbase = vc + (a.slot0 + t0) * rowel + h * kHD + 4 * lane;
-    for (int tt = 0; tt < nvalid; ++tt) {
+#pragma unroll
+    for (int tt = 0; tt < kAttChunk; ++tt) {
       const float p0 = __shfl_sync(0xffffffffu, p[0], tt);
       const float p1 = __shfl_sync(0xffffffffu, p[1], tt);
-      const uint2 vv = *reinterpret_cast<const uint2*>(vbase + (int64_t)tt * rowel);
-      const float v0 = h2f((uint16_t)(vv.x & 0xffffu)), v1 = h2f((uint16_t)(vv.x >> 16));
-      const float v2 = h2f((uint16_t)(vv.y & 0xffffu)), v3 = h2f((uint16_t)(vv.y >> 16));
-      o0[0] = __fmaf_rn(p0, v0, o0[0]);
-      o0[1] = __fmaf_rn(p0, v1, o0[1]);
-      o0[2] = __fmaf_rn(p0, v2, o0[2]);
-      o0[3] = __fmaf_rn(p0, v3, o0[3]);
-      o1[0] = __fmaf_rn(p1, v0, o1[0]);
-      o1[1] = __fmaf_rn(p1, v1, o1[1]);
-      o1[2] = __fmaf_rn(p1, v2, o1[2]);
-      o1[3] = __fmaf_rn(p1, v3, o1[3]);
-    }
-    if (lane == 0) {
-      cp[warp][0].m = m[0];
-      cp[warp][0].l = l[0];
-      cp[warp][1].m = m[1];
-      cp[warp][1].l = l[1];
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      cp[warp][0].o[4 * lane + j] = o0[j];
-      cp[warp][1].o[4 * lane + j] = o1[j];
-    }
-  }
-  __syncthreads();
-
-  // 4) merge this split's chunks left to right (warp hh merges q head 2h+hh)
-  const int64_t keys_here = T - (int64_t)split * kAttSplit;
-  const int nchunk_here = keys_here >= kAttSplit ? kAttSplitChunks
-                                                 : (int)((keys_here + kAttChunk - 1) / kAttChunk);
-  AttnPartial* gpart = a.part + (((int64_t)b * kNKV + h) * a.max_splits) * 2;
-  if (warp < 2) {
-    const int hh = warp;
-    float m = cp[0][hh].m, l = cp[0][hh].l, o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o[j] = cp[0][hh].o[4 * lane + j];
-    for (int c = 1; c < nchunk_here; ++c) {
-      float ob[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ob[j] = cp[c][hh].o[4 * lane + j];
-      att_merge(m, l, o, cp[c][hh].m, cp[c][hh].l, ob);
-    }
-    if (nsplit == 1) {
-      uint16_t* out = a.out + (int64_t)b * a.out_stride + (2 * h + hh) * kHD;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) out[4 * lane + j] = f2h(__fdiv_rn(o[j], l));
-    } else {
-      AttnPartial* gp = gpart + split * 2 + hh;
-      if (lane == 0) {
-        gp->m = m;
-        gp->l = l;
+      if (tt < nvalid) {
+        const float v0 = h2f((uint16_t)(vv[tt].x & 0xffffu)), v1 = h2f((uint16_t)(vv[tt].x >> 16));
+        const float v2 = h2f((uint16_t)(vv[tt].y & 0xffffu)), v3 = h2f((uint16_t)(vv[tt].y >> 16));
+        o0[0] = __fmaf_rn(p0, v0, o0[0]);
+        o0[1] = __fmaf_rn(p0, v1, o0[1]);
+        o0[2] = __fmaf_rn(p0, v2, o0[2]);
+        o0[3] = __fmaf_rn(p0, v3, o0[3]);
+        o1[0] = __fmaf_rn(p1, v0, o1[0]);
+        o1[1] = __fmaf_rn(p1, v1, o1[1]);
+        o1[2] = __fmaf_rn(p1, v2, o1[2]);
+        o1[3] = __fmaf_rn(p1, v3, o1[3]);
       }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) gp->o[4 * lane + j] = o[j];
     }
+    AttnPartial* gp = c.part + ((int64_t)h * c.max_chunks + ci) * 2;
+    if (lane == 0) {
+      gp[0].m = m[0];
+      gp[0].l = l[0];
+      gp[1].m = m[1];
+      gp[1].l = l[1];
+    }
+    *reinterpret_cast<float4*>(&gp[0].o[4 * lane]) = make_float4(o0[0], o0[1], o0[2], o0[3]);
+    *reinterpret_cast<float4*>(&gp[1].o[4 * lane]) = make_float4(o1[0], o1[1], o1[2], o1[3]);
   }
-  if (nsplit == 1) return;
   __threadfence();
-  __syncthreads();
+  consumer_sync();
   if (threadIdx.x == 0) {
-    unsigned int* ctr = a.counters + (int64_t)b * kNKV + h;
-    const unsigned prev = atomicAdd(ctr, 1u);
-    is_last = (prev == (unsigned)(nsplit - 1));
-    if (is_last) *ctr = 0u;
+    const unsigned prev = atomicAdd(c.counters + h, 1u);
+    sm.last = (prev == (unsigned)(ngroups - 1));
+    if (sm.last) c.counters[h] = 0u;
   }
-  __syncthreads();
-  if (!is_last) return;
+  consumer_sync();
+  if (!sm.last) return;
   __threadfence();
-  // 5) last CTA of this (sequence, kv head): merge the splits left to right
+  // 4) last group of head h: fold all chunk partials left to right
   if (warp < 2) {
     const int hh = warp;
-    const volatile AttnPartial* gp = gpart + hh;
-    float m = gp->m, l = gp->l, o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o[j] = gp->o[4 * lane + j];
-    for (int sp = 1; sp < nsplit; ++sp) {
-      const volatile AttnPartial* q = gpart + sp * 2 + hh;
-      float ob[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ob[j] = q->o[4 * lane + j];
-      att_merge(m, l, o, q->m, q->l, ob);
+    const AttnPartial* base = c.part + (int64_t)h * c.max_chunks * 2 + hh;
+    float m = __ldcg(&base->m), l = __ldcg(&base->l), o[4];
+    {
+      const float4 t4 = __ldcg(reinterpret_cast<const float4*>(&base->o[4 * lane]));
+      o[0] = t4.x, o[1] = t4.y, o[2] = t4.z, o[3] = t4.w;
     }
-    uint16_t* out = a.out + (int64_t)b * a.out_stride + (2 * h + hh) * kHD;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) out[4 * lane + j] = f2h(__fdiv_rn(o[j], l));
+    for (int k = 1; k < nch; ++k) {
+      const AttnPartial* q = base + (int64_t)k * 2;
+      const float4 t4 = __ldcg(reinterpret_cast<const float4*>(&q->o[4 * lane]));
+      const float ob[4] = {t4.x, t4.y, t4.z, t4.w};
+      att_merge(m, l, o, __ldcg(&q->m), __ldcg(&q->l), ob);
+    }
+    uint16_t* out = c.out + (2 * h + hh) * kHD + 4 * lane;
+    uint2 pk;
+    pk.x = (uint32_t)f2h(__fdiv_rn(o[0], l)) | ((uint32_t)f2h(__fdiv_rn(o[1], l)) << 16);
+    pk.y = (uint32_t)f2h(__fdiv_rn(o[2], l)) | ((uint32_t)f2h(__fdiv_rn(o[3], l)) << 16);
+    *reinterpret_cast<uint2*>(out) = pk;
   }
+}
+
+// Standalone launch: grid (8 kv heads, max groups, sequences), 256 threads.
+__global__ void __launch_bounds__(256) k_attn_decode(const __grid_constant__ AttnArgs a) {
+  __shared__ __align__(16) AttnSmem sm;
+  const int h = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  pdl_launch_dependents();
+  pdl_wait();
+  if (a.stop != nullptr && a.stop[(int64_t)b * a.stop_stride] != 0) return;
+  const int64_t pos = a.pos[(int64_t)b * a.pos_stride];
+  if (pos < 0 || pos >= a.S || pos >= a.rope_pos ||
+      attn_nchunks(pos) > a.max_chunks) {
+    if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
+    return;
+  }
+  if (g >= attn_ngroups(pos)) return;
+  AttnCtx c;
+  c.qkv = a.qkv + (int64_t)b * a.qkv_stride;
+  c.q_norm = a.q_norm;
+  c.k_norm = a.k_norm;
+  c.ct = a.rope_cos + pos * 64;
+  c.sn = a.rope_sin + pos * 64;
+  c.kc = a.kc + (int64_t)b * a.cache_stride;
+  c.vc = a.vc + (int64_t)b * a.cache_stride;
+  c.slot0 = a.slot0;
+  c.pos = pos;
+  c.out = a.out + (int64_t)b * a.out_stride;
+  c.part = a.part + (int64_t)b * kNKV * a.max_chunks * 2;
+  c.counters = a.counters + (int64_t)b * kNKV;
+  c.max_chunks = a.max_chunks;
+  attn_group(c, h, g, sm);
 }
 
 }  // namespace q3

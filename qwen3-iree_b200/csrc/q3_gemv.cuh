@@ -129,6 +129,34 @@ __device__ __forceinline__ void load_x_blocks_norm(const uint16_t* x, const uint
   }
 }
 
+// Barrier over the 256 consumer threads (warps 0-7) only: the producer warp
+// never joins it.
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// The same RMSNorm computed once per CTA by the 256 consumer threads into
+// shared memory: x staged in xs, ss in warp 0's lane-strided order, then
+// xs[k] = f16((x_k / r) * g_k).  x 16-byte aligned, K a multiple of 8.
+__device__ __forceinline__ void cta_rmsnorm_to_smem(const uint16_t* x, const uint16_t* g, int K,
+                                                    uint16_t* xs, float* rs) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < K / 8; i += 256)
+    reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(x)[i];
+  consumer_sync();
+  if (tid < 32) {
+    float ss = 0.0f;
+    for (int k = tid; k < K; k += 32) {
+      const float v = h2f(xs[k]);
+      ss = __fmaf_rn(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if (tid == 0) *rs = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), kEps));
+  }
+  consumer_sync();
+  const float r = *rs;
+  for (int k = tid; k < K; k += 256) xs[k] = rms_apply(xs[k], g[k], r);
+  consumer_sync();
+}
+
 template <int G>
 __device__ __forceinline__ void h2_to_f32(const uint32_t (&xr)[G][16], float (&xf)[G][32]) {
 #pragma unroll
@@ -236,8 +264,9 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
   const int tiles_per_seg = a.seg_rows / kTileRows;
   const int ntiles = a.nseg * tiles_per_seg;
   Ring ring = ring_setup(smem, a.nstages, tile_bytes, kGemvConsumerWarps);
-
-  if (a.seq != nullptr && a.seq->stop) return;
+  // Weights do not depend on the previous kernel: let the next kernel launch
+  // and this one's copies start before the previous kernel has finished.
+  pdl_launch_dependents();
 
   if (warp == kGemvConsumerWarps) {
     // ---------------- producer ----------------
@@ -263,28 +292,33 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
   }
 
   // ---------------- consumers ----------------
+  __shared__ __align__(16) uint16_t xs[3072];
+  __shared__ float rs;
+  pdl_wait();  // the previous kernel's outputs (activations, state) are visible
+  const bool stopped = a.seq != nullptr && a.seq->stop != 0;
   uint32_t xr[G][16];
   const uint16_t* xcur = nullptr;
-  if (MODE == kModeNormIn || MODE == kModeSwiglu) {
+  if ((MODE == kModeNormIn || MODE == kModeSwiglu) && !stopped) {
     const uint16_t* x = a.seg[0].x;
     if (a.tokens != nullptr) {
       int64_t tok = a.tokens[a.seq->pos];
       if (tok < 0 || tok >= kVocab) {
-        if (lane == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
+        if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
         tok = 0;
       }
       x = a.embd + tok * (int64_t)kDim;
       if (blockIdx.x == 0 && warp == 0 && a.embed_out != nullptr)
         for (int k = lane; k < a.K; k += 32) a.embed_out[k] = x[k];
     }
-    load_x_blocks_norm<G>(x, a.norm_g, a.K, lane, xr);
+    cta_rmsnorm_to_smem(x, a.norm_g, a.K, xs, &rs);
+    load_x_blocks<G>(xs, nb, lane, xr);
   }
 
   int i = 0;
   for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
     const int seg = t / tiles_per_seg;
     const int r0 = (t % tiles_per_seg) * kTileRows;
-    if (MODE == kModePlain || MODE == kModeResid) {
+    if ((MODE == kModePlain || MODE == kModeResid) && !stopped) {
       if (a.seg[seg].x != xcur) {
         xcur = a.seg[seg].x;
         load_x_blocks<G>(xcur, nb, lane, xr);
@@ -292,22 +326,25 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
     }
     const int s = i % ring.ns;
     if (!mbar_wait(&ring.full[s], (uint32_t)((i / ring.ns) & 1), a.err, kErrTimeoutFull)) break;
-    const uint32_t base = smem_u32(ring.buf + (size_t)s * ring.stage_bytes);
-    const int row = r0 + warp;
-    const float d = q8_row_dot<G, ORDER>(base + rowbytes * warp, nb, lane, xr);
-    if (MODE == kModeSwiglu) {
-      const float u = q8_row_dot<G, ORDER>(base + rowbytes * (kTileRows + warp), nb, lane, xr);
-      if (lane == 0) a.seg[seg].y[row] = swiglu_h(f2h(d), f2h(u));
-    } else if (MODE == kModeResid) {
-      if (lane == 0)
-        a.seg[seg].y[row] = f2h(__fadd_rn(h2f(a.seg[seg].r[row]), h2f(f2h(d))));
-    } else {
-      if (lane == 0) a.seg[seg].y[row] = f2h(d);
+    if (!stopped) {
+      const uint32_t base = smem_u32(ring.buf + (size_t)s * ring.stage_bytes);
+      const int row = r0 + warp;
+      const float d = q8_row_dot<G, ORDER>(base + rowbytes * warp, nb, lane, xr);
+      if (MODE == kModeSwiglu) {
+        const float u = q8_row_dot<G, ORDER>(base + rowbytes * (kTileRows + warp), nb, lane, xr);
+        if (lane == 0) a.seg[seg].y[row] = swiglu_h(f2h(d), f2h(u));
+      } else if (MODE == kModeResid) {
+        if (lane == 0)
+          a.seg[seg].y[row] = f2h(__fadd_rn(h2f(a.seg[seg].r[row]), h2f(f2h(d))));
+      } else {
+        if (lane == 0) a.seg[seg].y[row] = f2h(d);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&ring.empty[s]);
   }
-  if (a.advance != nullptr && blockIdx.x == 0 && threadIdx.x == 0) a.advance->pos += 1;
+  if (a.advance != nullptr && !stopped && blockIdx.x == 0 && threadIdx.x == 0)
+    a.advance->pos += 1;
 }
 
 // --------------------------------------------------------------------------
@@ -355,7 +392,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
   const uint32_t tile_bytes = rowbytes * kTileRows;
   const int ntiles = a.N / kTileRows;
   Ring ring = ring_setup(smem, a.nstages, tile_bytes, kGemvConsumerWarps);
-  if (a.seq != nullptr && a.seq->stop) return;
+  pdl_launch_dependents();
+  __shared__ __align__(16) uint16_t xs[kVocabK];
+  __shared__ float rs;
+  __shared__ int stopped_s;
 
   if (warp == kGemvConsumerWarps) {
     if (lane == 0) {
@@ -372,16 +412,20 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
       ring_drain(ring, i);
     }
   } else {
+    pdl_wait();
+    const bool stopped = a.seq != nullptr && a.seq->stop != 0;
+    if (threadIdx.x == 0) stopped_s = stopped;
     // lane-strided inputs x[l + 32 i], normalised in f32 and rounded to f16
     uint16_t xh[kVocabK / 32];
-    if (a.norm_g != nullptr) {
-      const float r = rms_denominator(a.x, a.K, lane);
+    if (!stopped) {
+      if (a.norm_g != nullptr) {
+        cta_rmsnorm_to_smem(a.x, a.norm_g, a.K, xs, &rs);
 #pragma unroll
-      for (int i = 0; i < kVocabK / 32; ++i)
-        xh[i] = rms_apply(a.x[lane + 32 * i], a.norm_g[lane + 32 * i], r);
-    } else {
+        for (int i = 0; i < kVocabK / 32; ++i) xh[i] = xs[lane + 32 * i];
+      } else {
 #pragma unroll
-      for (int i = 0; i < kVocabK / 32; ++i) xh[i] = a.x[lane + 32 * i];
+        for (int i = 0; i < kVocabK / 32; ++i) xh[i] = a.x[lane + 32 * i];
+      }
     }
     float best_v = -__int_as_float(0x7f800000);
     int64_t best_i = -1;
@@ -389,6 +433,11 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
       const int s = i % ring.ns;
       if (!mbar_wait(&ring.full[s], (uint32_t)((i / ring.ns) & 1), a.err, kErrTimeoutFull)) break;
+      if (stopped) {  // drain the ring without computing
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ring.empty[s]);
+        continue;
+      }
       const uint32_t row = smem_u32(ring.buf + (size_t)s * ring.stage_bytes) + rowbytes * warp;
       float acc = 0.0f;
 #pragma unroll
@@ -411,6 +460,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
     }
   }
   __syncthreads();
+  if (stopped_s) return;
   if (threadIdx.x == 0) {
     float bv = -__int_as_float(0x7f800000);
     int64_t bi = -1;

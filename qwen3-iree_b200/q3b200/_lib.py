@@ -55,6 +55,7 @@ SIGNATURES = {
     "q3_event_create": [PP],
     "q3_event_destroy": [P],
     "q3_event_record": [P, P],
+    "q3_event_synchronize": [P],
     "q3_event_elapsed_ms": [P, P, ctypes.POINTER(ctypes.c_float)],
     "q3_rope_table": [I64, P, P],
     "q3_quantize_q8_0": [P, I64, P],
@@ -86,6 +87,12 @@ SIGNATURES = {
     "q3_generate_end": [P, P, PI64],
     "q3_model_launches_per_step": [P, PI64],
     "q3_model_device_error": [P, ctypes.POINTER(ctypes.c_int)],
+    "q3_model_profile_steps": [P, I64, P, P, I64],
+    "q3_model_set_engine": [P, I],
+    "q3_model_engine": [P, ctypes.POINTER(ctypes.c_int)],
+    "q3_model_kernel_launches": [P, PI64],
+    "q3_model_trace_steps": [P, I64, I64, P, I64, ctypes.POINTER(ctypes.c_int),
+                             ctypes.POINTER(ctypes.c_int)],
     "q3_strerror": [I],
     "q3_last_error": [],
 }

@@ -100,7 +100,7 @@ class Events:
         call("q3_event_record", self.end, stream)
 
     def elapsed_ms(self) -> float:
-        call("q3_stream_synchronize", None)
+        call("q3_event_synchronize", self.end)
         ms = ctypes.c_float()
         call("q3_event_elapsed_ms", self.start, self.end, ctypes.byref(ms))
         return ms.value

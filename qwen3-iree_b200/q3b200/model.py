@@ -47,7 +47,8 @@ class DeviceWeights:
 class Qwen3Decoder:
     """One decoder (KV cache, activations, graphs) on the current device."""
 
-    def __init__(self, weights: DeviceWeights | dict, max_seq_len: int = 1024, stream=None):
+    def __init__(self, weights: DeviceWeights | dict, max_seq_len: int = 1024, stream=None,
+                 engine: str | None = None):
         self.weights = weights if isinstance(weights, DeviceWeights) else DeviceWeights(weights)
         self.max_seq_len = int(max_seq_len)
         h = ctypes.c_void_p()
@@ -55,6 +56,8 @@ class Qwen3Decoder:
              ctypes.byref(h))
         self.handle = h.value
         self.stream = lib().q3_model_stream(self.handle)
+        if engine is not None:
+            self.set_engine(engine)
 
     # -- @run (model/qwen3_full.mlir:2113-2167)
     def run(self, tokens, max_tokens: int, eos: int) -> tuple[np.ndarray, int]:
@@ -105,6 +108,40 @@ class Qwen3Decoder:
         n = ctypes.c_int64(0)
         call("q3_generate_end", self.handle, out.ctypes.data, ctypes.byref(n))
         return out[:n.value], n.value
+
+    def profile_steps(self, steps: int) -> tuple[np.ndarray, np.ndarray]:
+        """(per-kernel average microseconds, kinds) over `steps` generation steps."""
+        cap = 512
+        t = np.zeros(cap, np.float32)
+        k = np.zeros(cap, np.int32)
+        call("q3_model_profile_steps", self.handle, int(steps), t.ctypes.data, k.ctypes.data, cap)
+        n = self.launches_per_step()
+        return t[:n].copy(), k[:n].copy()
+
+    ENGINES = {"graph": 0, "persistent": 1}
+
+    def set_engine(self, name: str) -> None:
+        call("q3_model_set_engine", self.handle, self.ENGINES[name])
+
+    @property
+    def engine(self) -> str:
+        e = ctypes.c_int(-1)
+        call("q3_model_engine", self.handle, ctypes.byref(e))
+        return {v: k for k, v in self.ENGINES.items()}[e.value]
+
+    def trace_steps(self, steps: int, trace_step: int) -> np.ndarray:
+        """Persistent engine: [ctas, phases, 4] SM-clock stamps of one step."""
+        cap = 1024 * 160 * 4
+        out = np.zeros(cap, np.int64)
+        c, p = ctypes.c_int(), ctypes.c_int()
+        call("q3_model_trace_steps", self.handle, int(steps), int(trace_step), out.ctypes.data,
+             cap, ctypes.byref(c), ctypes.byref(p))
+        return out[:c.value * p.value * 4].reshape(c.value, p.value, 4)
+
+    def kernel_launches(self) -> int:
+        n = ctypes.c_int64(0)
+        call("q3_model_kernel_launches", self.handle, ctypes.byref(n))
+        return n.value
 
     def launches_per_step(self) -> int:
         n = ctypes.c_int64(0)

@@ -11,6 +11,11 @@ pytestmark = pytest.mark.gpu
 EOS = 151645
 
 
+@pytest.fixture(params=["persistent", "graph"])
+def engine(request):
+    return request.param
+
+
 @pytest.fixture(scope="module")
 def models(gpu, O, model_weights):
     from q3b200.weights import to_oracle_dict
@@ -20,10 +25,10 @@ def models(gpu, O, model_weights):
     return dw, om
 
 
-def test_decode_steps_bit_exact(gpu, O, models):
+def test_decode_steps_bit_exact(gpu, O, models, engine):
     dw, om = models
     S = 64
-    dec = gpu.Qwen3Decoder(dw, max_seq_len=S)
+    dec = gpu.Qwen3Decoder(dw, max_seq_len=S, engine=engine)
     kc, vc = om.new_cache(S)
     tok = 9
     for pos in range(4):
@@ -35,12 +40,12 @@ def test_decode_steps_bit_exact(gpu, O, models):
     dec.close()
 
 
-def test_run_256_greedy_tokens_identical(gpu, O, models):
+def test_run_256_greedy_tokens_identical(gpu, O, models, engine):
     """32 prompt ids U[0,151936), 256 generated, cache 1024."""
     dw, om = models
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, 151936, size=32, dtype=np.int64)
-    dec = gpu.Qwen3Decoder(dw, max_seq_len=1024)
+    dec = gpu.Qwen3Decoder(dw, max_seq_len=1024, engine=engine)
     out, n = dec.run(prompt, 256, EOS)
     assert dec.device_error() == 0
     want, _, _ = om.generate(prompt, 256, EOS, 1024)
@@ -50,12 +55,12 @@ def test_run_256_greedy_tokens_identical(gpu, O, models):
     dec.close()
 
 
-def test_eos_rule_matches_reference(gpu, O, models):
+def test_eos_rule_matches_reference(gpu, O, models, engine):
     """@generate stops only when the LAST token of a group of 4 is eos
     (model/qwen3_full.mlir:1412-1419, :1528-1530)."""
     dw, om = models
     prompt = np.array([1, 2, 3], np.int64)
-    dec = gpu.Qwen3Decoder(dw, max_seq_len=64)
+    dec = gpu.Qwen3Decoder(dw, max_seq_len=64, engine=engine)
     free, n = dec.run(prompt, 12, -7)
     assert n == 12
     # eos equal to the last token of the first group: stops after 4 tokens
@@ -70,12 +75,12 @@ def test_eos_rule_matches_reference(gpu, O, models):
     dec.close()
 
 
-def test_chat_turns_match_oracle(gpu, O, models):
+def test_chat_turns_match_oracle(gpu, O, models, engine):
     """@init_chat/@chat_turn: zero cache, turn = ingest + generate, then the
     position moves by n_tokens + n_out + 1 (model/qwen3_full.mlir:2216-2218)."""
     dw, om = models
     S = 128
-    dec = gpu.Qwen3Decoder(dw, max_seq_len=S)
+    dec = gpu.Qwen3Decoder(dw, max_seq_len=S, engine=engine)
     dec.init_chat(S)
     kc, vc = om.new_cache(S)
     pos = 0
