@@ -138,6 +138,24 @@ int q3_decode_attention(const void* qkv, const void* q_norm, const void* k_norm,
                         void* k_cache, void* v_cache, int64_t slot0, int64_t S,
                         const int64_t* pos, void* out, void* workspace, void* stream);
 
+/* The same decode attention for callers that cannot allocate device memory
+ * where they launch (e.g. a kernel substituted into an IREE executable gets
+ * only its bindings; code under a fixed memory plan may not cudaMalloc).  No
+ * workspace argument and no allocation: the kernel's scratch (softmax
+ * partials, arrival counters) lives in a static device array inside the
+ * library, sized for S <= 4096 positions (about 1.08 MB per device, held
+ * until the process exits); larger S returns Q3_ERR_INVALID.  The first call
+ * on each device looks up that array's device address (call it once before
+ * any stream capture).  All calls share the one array: calls that overlap on
+ * the GPU (concurrent streams, several host threads) race and must not be
+ * issued.  Each call clears the counters it needs.  Results equal
+ * q3_decode_attention bit for bit.  This entry point has no counterpart in
+ * the reference. */
+int q3_decode_attention_noalloc(const void* qkv, const void* q_norm, const void* k_norm,
+                                const float* rope_cos, const float* rope_sin, int64_t rope_rows,
+                                void* k_cache, void* v_cache, int64_t slot0, int64_t S,
+                                const int64_t* pos, void* out, void* stream);
+
 /* ------------------------------------------------- IREE-ABI kernels
  * The six substituted executables of compile.sh:36-42 / :58-65, compiled for
  * sm_100a with the same export names and parameter lists

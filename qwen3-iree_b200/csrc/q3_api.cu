@@ -509,6 +509,77 @@ extern "C" int q3_decode_attention(const void* qkv, const void* q_norm, const vo
   return launch_attn(a, 1, (cudaStream_t)stream, nullptr);
 }
 
+// Attention with no caller workspace -------------------------------------------
+// Some callers cannot allocate device memory at the point where they launch:
+// a kernel substituted into an IREE executable receives only its bindings and
+// push constants (the HAL allocates nothing on its behalf), and code that
+// runs inside a fixed memory plan must not call cudaMalloc.  For them this
+// entry point keeps the attention kernel's scratch (the per-chunk softmax
+// partials and the per-head arrival counters) in one file-scope device array
+// sized for contexts of up to kNoAllocMaxPositions positions (1,081,600
+// bytes; every device that loads this library holds it until process exit).
+constexpr int64_t kNoAllocMaxPositions = 4096;
+constexpr int kNoAllocChunks = (int)(kNoAllocMaxPositions / kAttChunk);
+constexpr size_t kNoAllocPartBytes = sizeof(AttnPartial) * (size_t)kNKV * kNoAllocChunks * 2;
+static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocPartBytes + 256];
+
+// Device address of g_attn_scratch per device.  In host code the symbol is a
+// host-side stand-in, never a device address; the address comes from
+// cudaGetSymbolAddress, taken once per device with that device current.
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[64] = {nullptr};
+
+extern "C" int q3_decode_attention_noalloc(const void* qkv, const void* q_norm, const void* k_norm,
+                                           const float* rope_cos, const float* rope_sin,
+                                           int64_t rope_rows, void* kc, void* vc, int64_t slot0,
+                                           int64_t S, const int64_t* pos, void* out,
+                                           void* stream) {
+  Q3_REQUIRE(qkv && q_norm && k_norm && rope_cos && rope_sin && kc && vc && pos && out,
+             "null pointer");
+  Q3_REQUIRE(S >= 1 && slot0 >= 0 && rope_rows >= 1, "bad S / slot0 / rope_rows");
+  Q3_REQUIRE(S <= kNoAllocMaxPositions,
+             "S=%lld exceeds the %lld positions the static attention scratch holds; use "
+             "q3_decode_attention with a workspace",
+             (long long)S, (long long)kNoAllocMaxPositions);
+  Q3_REQUIRE(aligned16(qkv) && aligned16(kc) && aligned16(vc),
+             "qkv and caches must be 16-byte aligned");
+  int dev = 0;
+  Q3_CUDA(cudaGetDevice(&dev));
+  Q3_REQUIRE(dev >= 0 && dev < 64, "device ordinal %d out of range", dev);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (g_scratch_addr[dev] == nullptr) {
+      void* p = nullptr;
+      Q3_CUDA(cudaGetSymbolAddress(&p, g_attn_scratch));
+      g_scratch_addr[dev] = p;
+    }
+    scratch = g_scratch_addr[dev];
+  }
+  unsigned int* counters = (unsigned int*)((uint8_t*)scratch + kNoAllocPartBytes);
+  // the counters must start at zero; the partials are written before they are read
+  Q3_CUDA(cudaMemsetAsync(counters, 0, kNKV * sizeof(unsigned int), (cudaStream_t)stream));
+  AttnArgs a;
+  memset(&a, 0, sizeof(a));
+  a.qkv = (const uint16_t*)qkv;
+  a.q_norm = (const uint16_t*)q_norm;
+  a.k_norm = (const uint16_t*)k_norm;
+  a.rope_cos = rope_cos;
+  a.rope_sin = rope_sin;
+  a.rope_pos = rope_rows;
+  a.kc = (uint16_t*)kc;
+  a.vc = (uint16_t*)vc;
+  a.slot0 = slot0;
+  a.S = S;
+  a.pos = pos;
+  a.pos_stride = 1;
+  a.out = (uint16_t*)out;
+  a.max_chunks = kNoAllocChunks;
+  a.part = (AttnPartial*)scratch;
+  a.counters = counters;
+  return launch_attn(a, 1, (cudaStream_t)stream, nullptr);
+}
+
 // IREE-ABI dispatch launchers --------------------------------------------------
 #define Q3_IREE_CHECK(w, b1, b2)                                                  \
   Q3_REQUIRE((w) && (b1) && (b2), "null binding");                                \

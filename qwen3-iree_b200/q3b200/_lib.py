@@ -69,6 +69,7 @@ SIGNATURES = {
     "q3_vocab_argmax": [P, P, P, P, P, P, I, I, P],
     "q3_attention_workspace_bytes": [I64],
     "q3_decode_attention": [P, P, P, P, P, I64, P, P, I64, I64, P, P, P, P],
+    "q3_decode_attention_noalloc": [P, P, P, P, P, I64, P, P, I64, I64, P, P, P],
     "q3_iree_dispatch_3": [P, P, P, U32, U32, P],
     "q3_iree_dispatch_4": [P, P, P, U32, U32, U32, P],
     "q3_iree_dispatch_12": [P, P, P, U32, U32, P],
