@@ -283,6 +283,58 @@ int q3_model_launches_per_step(q3_model* m, int64_t* n);
 /* Device error word of the last run (0: none; see q3_strerror(Q3_ERR_DEVICE)). */
 int q3_model_device_error(q3_model* m, int* code);
 
+/* ------------------------------------------------------------------ batched decode
+ * B independent sequences (1 <= B <= 64) decoded together.  The reference
+ * decodes one sequence at a time (model/qwen3_full.mlir:751-864, per-layer
+ * dispatch order); these entry points run the same per-sequence arithmetic
+ * with each projection as one [B,K]x[K,N] tensor-core contraction (tcgen05,
+ * weights dequantised to f16 = f16(scale*q) as model/qwen3_full.mlir:564-579
+ * does), so results match the reference within rel-L2 1e-3, not bit for bit.
+ * Activations are row-major [B padded to 16][K] f16; rows >= B are ignored. */
+
+/* Batched Q8_0 projection: rows [row0, row0+N) of the Q8_0 matrix `w`
+ * (w_rows rows of K, the reference's [N][K/32] x 34-byte layout) times the B
+ * activation rows x[b][K] -> y[b][N].
+ *   mode 0: y = W x;   mode 1: y = r + W x (r laid out like y);
+ *   mode 2: gate rows [row0, row0+N), up rows [row0+N, row0+2N):
+ *           y = silu(gate) * up in f16 (model/qwen3_full.mlir:829-839).
+ * N % 128 == 0, K % 256 == 0, K <= 3072. */
+int q3_bgemm_q8(const void* w, int64_t w_rows, int64_t row0, const void* x, void* y,
+                const void* r, int B, int N, int K, int mode, void* stream);
+/* Batched vocab GEMV + argmax (model/qwen3_full.mlir:1456-1509 per row):
+ * logits[b][N] (optional, f16) and tokens[b] = first index of the largest f16
+ * logit of xn[b] (xn already normalised).  Workspace zero-filled once. */
+size_t q3_bvocab_workspace_bytes(void);
+int q3_bvocab_argmax(const void* w, int N, const void* xn, int B, void* logits, int64_t* tokens,
+                     void* ws, void* stream);
+
+/* Batched decoder: caches of max_batch sequences x max_seq_len positions. */
+typedef struct q3_batch q3_batch;
+int q3_batch_create(const q3_weights* w, int max_batch, int64_t max_seq_len, void* stream,
+                    q3_batch** out);
+int q3_batch_destroy(q3_batch* m);
+void* q3_batch_stream(q3_batch* m);
+/* Sequence b: prompt prompts[b*stride .. + n_prompt[b]), fed one token per
+ * step from position 0 (the reference's @prefill_all semantics,
+ * model/qwen3_full.mlir:1541-1570); after the prompt each step appends the
+ * greedy argmax. */
+int q3_batch_begin(q3_batch* m, int B, const int64_t* prompts, int64_t stride,
+                   const int64_t* n_prompt);
+/* Benchmark set-up: sequence b holds ctx[b] cached positions of seeded
+ * pseudo-random K/V and feeds tok[b] at position ctx[b]. */
+int q3_batch_begin_random(q3_batch* m, int B, const int64_t* ctx, const int64_t* tok,
+                          uint64_t seed);
+/* Enqueue `steps` decode steps of all B sequences (asynchronous). */
+int q3_batch_steps(q3_batch* m, int64_t steps);
+/* Token table [B][max_seq_len+1] and positions [B] to the host (either may
+ * be NULL), and the device error word; synchronises. */
+int q3_batch_read(q3_batch* m, int64_t* tokens, int64_t* positions, int* device_err);
+/* Argmax history [B][max_seq_len+1] to the host: entry p+1 of row b is the
+ * greedy token after the step that fed position p, prompt positions included
+ * (-1 where no step ran); for teacher-forced checks.  Synchronises. */
+int q3_batch_read_argmax(q3_batch* m, int64_t* out);
+int q3_batch_kernel_launches(q3_batch* m, int64_t* n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,570 @@
+// q3_batch.cuh -- batched decode (B independent sequences, B <= 64) for sm_100a.
+//
+// At batch 16-64 a projection is a real contraction, [B,K] x [K,N], and runs
+// on the 5th-generation tensor cores: tcgen05.mma (kind::f16, M=128 weight
+// rows, N = B padded to a multiple of 16, f32 accumulators in TMEM).
+//
+// Q8_0 weights (k_bgemm_q8): a producer thread brings 128 rows x 256 K of raw
+// Q8_0 bytes into shared memory with one tensor TMA (the row stride of the
+// reference layout is a multiple of 16 bytes, so a [128 x 272-byte] box
+// works) and the activations' K-slices with SWIZZLE_128B tensor TMA; four
+// dequantising warps turn each 64-wide K-slice into f16 weights in the
+// canonical SWIZZLE_128B layout -- w = f16(scale * q), the f16 dequant of the
+// reference's own fused-GEMV region (model/qwen3_full.mlir:564-579) -- and one
+// thread issues the MMAs.  The same four warps read the accumulators back with
+// tcgen05.ld and apply the epilogue (residual add, or SwiGLU over a gate tile
+// and its up tile held in two accumulators).
+//
+// f16 vocab head (k_bvocab): weight tiles and activations both arrive by
+// SWIZZLE_128B tensor TMA; each CTA walks tiles of 128 vocabulary rows,
+// rounds logits to f16 and keeps, per sequence, the first index of the
+// largest value; the last CTA reduces the per-CTA candidates and advances the
+// sequences.
+//
+// Accumulation order inside the tensor core is not the reference kernels'
+// order, so batched results agree with the CPU oracle within a tolerance
+// (rel-L2 <= 1e-3), not bit for bit; the batch-1 path is the bit-exact one.
+#pragma once
+
+#include "q3_attn.cuh"
+#include "q3_common.cuh"
+#include "q3_gemv.cuh"
+#include "q3_tc.cuh"
+
+namespace q3 {
+
+constexpr int kBMaxBatch = 64;
+constexpr int kBgThreads = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 dequant + epilogue
+constexpr int kBgRawStages = 2;
+constexpr int kBgSubStages = 4;
+constexpr uint32_t kBgRawBytes = 128u * 272u;  // 128 rows x 8 Q8_0 blocks
+constexpr uint32_t kBgAtomA = 128u * 128u;     // 128 rows x 64 f16, SWIZZLE_128B
+
+enum BGemmMode : int { kBgPlain = 0, kBgResid = 1, kBgSwiglu = 2 };
+
+// Device state of one sequence of a batch.
+struct BatchSeq {
+  int64_t pos;       // position of the token fed this step
+  int64_t n_gen;     // tokens generated so far
+  int64_t n_prompt;  // tokens[pos+1] is overwritten only once pos+1 >= n_prompt
+  int64_t pad;
+};
+
+struct BGemmArgs {
+  CUtensorMap wmap[3];   // Q8_0 weights viewed as u16 [rows_total, rowbytes/2], box {136, 128}
+  CUtensorMap xmap;      // activations f16 [npad, K], box {64, npad}, SWIZZLE_128B
+  int wseg_rows[3];      // output rows served by wmap[i] (segments concatenated)
+  int64_t wrow0[3];      // first weight row (layer * N) in each map
+  int K;
+  int B;                 // live sequences (<= npad)
+  int ldy;               // output row stride (elements) per sequence
+  uint16_t* y;           // [npad][ldy] f16
+  const uint16_t* r;     // residual [npad][ldy] (kBgResid)
+  int64_t up_rows;       // kBgSwiglu: offset (rows) from a gate row to its up row
+  int* err;              // optional device error word (pipeline wait timed out)
+};
+
+// K=64 slices in flight between the dequantising warps and the MMA thread;
+// two accumulators (gate + up) leave room for two.
+__host__ __device__ constexpr int bgemm_substages(int naccum) { return naccum == 2 ? 2 : 4; }
+
+__host__ __device__ constexpr size_t bgemm_smem_bytes(int npad, int naccum) {
+  return 1024 /*align slack*/ + (size_t)naccum * bgemm_substages(naccum) * kBgAtomA +
+         (size_t)bgemm_substages(naccum) * npad * 128 +
+         (size_t)kBgRawStages * naccum * kBgRawBytes;
+}
+
+// Dequantise one 64-wide K-slice (two Q8_0 blocks at shared byte address
+// `raw`) of row r into the SWIZZLE_128B atom at `atom`.
+__device__ __forceinline__ void dequant_slice(uint32_t raw, uint32_t atom, uint32_t r) {
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    const Q8BlockWords bw = q8_load_block(raw + 34u * blk);
+    const uint32_t s2 = bw.scale16 | (bw.scale16 << 16);
+#pragma unroll
+    for (int w = 0; w < 8; w += 2) {
+      uint32_t a01, a23, b01, b23;
+      q8x4_to_h2(bw.q[w], a01, a23);
+      q8x4_to_h2(bw.q[w + 1], b01, b23);
+      uint32_t o0, o1, o2, o3;
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o0) : "r"(a01), "r"(s2));
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o1) : "r"(a23), "r"(s2));
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o2) : "r"(b01), "r"(s2));
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o3) : "r"(b23), "r"(s2));
+      const uint32_t c = (uint32_t)(blk * 4 + w / 2);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(atom + sw128_chunk_offset(r, c)),
+                   "r"(o0), "r"(o1), "r"(o2), "r"(o3)
+                   : "memory");
+    }
+  }
+}
+
+// Batched Q8_0 GEMM.  Grid: one CTA per 128 output rows (kBgSwiglu: per 128
+// gate rows, with their 128 up rows).  NPAD = batch padded to 16.
+template <int NPAD, int MODE>
+__global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constant__ BGemmArgs a) {
+  constexpr int NACC = MODE == kBgSwiglu ? 2 : 1;   // accumulators (gate, up)
+  constexpr int SUB = bgemm_substages(NACC);
+  constexpr uint32_t TCOLS = NPAD * NACC <= 32 ? 32 : NPAD * NACC <= 64 ? 64 : 128;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t raw_full[kBgRawStages], raw_empty[kBgRawStages];
+  __shared__ __align__(8) uint64_t x_full[kBgSubStages], a_full[kBgSubStages], ax_empty[kBgSubStages];
+  __shared__ __align__(8) uint64_t acc_full;
+  __shared__ uint32_t tmem_base;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t sA = base;                                        // [NACC][4][16 KB]
+  const uint32_t sX = sA + NACC * SUB * kBgAtomA;         // [4][NPAD*128]
+  const uint32_t sR = sX + SUB * NPAD * 128;              // [2][NACC][34816]
+  const int nsub = a.K / 64;
+  const int nchunk = a.K / 256;
+  const int n0 = blockIdx.x * 128;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kBgRawStages; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 4);
+    }
+    for (int i = 0; i < SUB; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&a_full[i], 4);
+      mbar_init(&ax_empty[i], 1);
+    }
+    mbar_init(&acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base, TCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_launch_dependents();
+  const uint32_t tmem = tmem_base;
+  const uint32_t idesc = idesc_f16_f32(128, NPAD);
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      // which weight map serves rows n0.. (segments concatenated)
+      int seg = 0;
+      int64_t row = n0;
+      while (seg < 2 && row >= a.wseg_rows[seg]) {
+        row -= a.wseg_rows[seg];
+        ++seg;
+      }
+      const CUtensorMap* wm = &a.wmap[seg];
+      const int y0 = (int)(a.wrow0[seg] + row);
+      prefetch_tmap(wm);
+      prefetch_tmap(&a.xmap);
+      pdl_wait();  // activations come from the previous kernel
+      int c_done = 0, i_done = 0;  // loads issued
+      bool ok = true;
+      for (int c = 0; ok && c < nchunk; ++c) {
+        const int rs = c % kBgRawStages;
+        if (c >= kBgRawStages &&
+            !mbar_wait_own(&raw_empty[rs], ((c / kBgRawStages) - 1) & 1, a.err, kErrTimeoutEmpty))
+          break;
+        mbar_expect_tx(&raw_full[rs], NACC * kBgRawBytes);
+        for (int acc = 0; acc < NACC; ++acc)
+          tma_load_2d(smem_raw + (sR - smem_u32(smem_raw)) + (rs * NACC + acc) * kBgRawBytes, wm,
+                      c * 136, y0 + (int)(acc * a.up_rows), &raw_full[rs]);
+        c_done = c + 1;
+        for (int j = 0; j < 4; ++j) {
+          const int i = c * 4 + j, ss = i % SUB;
+          if (i >= SUB &&
+              !mbar_wait_own(&ax_empty[ss], ((i / SUB) - 1) & 1, a.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&x_full[ss], NPAD * 128);
+          tma_load_2d(smem_raw + (sX - smem_u32(smem_raw)) + ss * NPAD * 128, &a.xmap, i * 64, 0,
+                      &x_full[ss]);
+          i_done = i + 1;
+        }
+      }
+      // the CTA may not exit before every issued copy has landed
+      for (int st = 0; st < kBgRawStages && st < c_done; ++st)
+        mbar_wait_own(&raw_full[st], ((c_done - 1 - st) / kBgRawStages) & 1, a.err, kErrTimeoutFull);
+      for (int st = 0; st < SUB && st < i_done; ++st)
+        mbar_wait_own(&x_full[st], ((i_done - 1 - st) / SUB) & 1, a.err, kErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      for (int i = 0; i < nsub; ++i) {
+        const int ss = i % SUB;
+        const uint32_t par = (i / SUB) & 1;
+        if (!mbar_wait_own(&a_full[ss], par, a.err, kErrTimeoutFull)) break;
+        if (!mbar_wait_own(&x_full[ss], par, a.err, kErrTimeoutFull)) break;
+        tc_fence_after();
+        for (int acc = 0; acc < NACC; ++acc) {
+          const uint32_t aa = sA + (acc * SUB + ss) * kBgAtomA;
+          const uint32_t xx = sX + ss * NPAD * 128;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tmem + acc * NPAD, sw128_desc(aa + 32 * kk), sw128_desc(xx + 32 * kk), idesc,
+                     (i | kk) != 0);
+        }
+        umma_commit(&ax_empty[ss]);
+      }
+      umma_commit(&acc_full);
+      mbar_wait_own(&acc_full, 0, a.err, kErrTimeoutFull);  // no MMA in flight at dealloc
+    }
+  } else {
+    // ------------------------------------------------ dequant, then epilogue
+    const uint32_t r = 32u * (warp & 3) + lane;  // this thread's weight row / TMEM lane
+    pdl_wait();  // the epilogue reads the previous kernels' residual stream
+    for (int c = 0; c < nchunk; ++c) {
+      const int rs = c % kBgRawStages;
+      if (!mbar_wait_own(&raw_full[rs], (c / kBgRawStages) & 1, a.err, kErrTimeoutFull)) break;
+      for (int j = 0; j < 4; ++j) {
+        const int i = c * 4 + j, ss = i % SUB;
+        if (i >= SUB &&
+            !mbar_wait_own(&ax_empty[ss], ((i / SUB) - 1) & 1, a.err, kErrTimeoutEmpty))
+          break;
+        for (int acc = 0; acc < NACC; ++acc)
+          dequant_slice(sR + (rs * NACC + acc) * kBgRawBytes + r * 272u + 68u * j,
+                        sA + (acc * SUB + ss) * kBgAtomA, r);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[ss]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&raw_empty[rs]);
+    }
+    // epilogue
+    if (mbar_wait_own(&acc_full, 0, a.err, kErrTimeoutFull)) {
+      tc_fence_after();
+      const uint32_t lane_base = (32u * (warp & 3)) << 16;
+      const int n = n0 + (int)r;
+#pragma unroll
+      for (int col0 = 0; col0 < NPAD; col0 += 16) {
+        uint32_t v[16], u[16];
+        tmem_ld16(tmem + lane_base + col0, v);
+        if (MODE == kBgSwiglu) tmem_ld16(tmem + lane_base + NPAD + col0, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int b = col0 + j;
+          if (b < a.B) {
+            const float d = __uint_as_float(v[j]);
+            uint16_t out;
+            if (MODE == kBgSwiglu) {
+              out = swiglu_h(f2h(d), f2h(__uint_as_float(u[j])));
+            } else if (MODE == kBgResid) {
+              out = f2h(__fadd_rn(h2f(a.r[(int64_t)b * a.ldy + n]), h2f(f2h(d))));
+            } else {
+              out = f2h(d);
+            }
+            a.y[(int64_t)b * a.ldy + n] = out;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TCOLS);
+  }
+}
+
+// Per-sequence RMSNorm of model/qwen3_full.mlir:134-165 into the GEMM operand
+// buffer xn [npad][K] (padding rows stay zero).  With `tokens`, the input of
+// sequence b is embedding row tokens[b * tok_stride + seq[b].pos] and is also
+// stored as the residual stream x.
+struct BNormArgs {
+  const uint16_t* x;     // [npad][K] residual (ignored when tokens != nullptr)
+  uint16_t* x_out;       // embedding copy target (tokens != nullptr)
+  const uint16_t* gamma;
+  uint16_t* xn;          // [npad][K]
+  int K;
+  int B;
+  const int64_t* tokens; // [B][tok_stride]
+  int64_t tok_stride;
+  const BatchSeq* seq;
+  const uint16_t* embd;
+  int* err;
+};
+
+__global__ void __launch_bounds__(256) k_bnorm(const __grid_constant__ BNormArgs a) {
+  __shared__ __align__(16) uint16_t xs[3072];
+  __shared__ float rs;
+  const int b = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
+  if (b >= a.B) return;
+  const uint16_t* x = a.x + (int64_t)b * a.K;
+  if (a.tokens != nullptr) {
+    const int64_t pos = a.seq[b].pos;
+    int64_t tok = 0;
+    if (pos < 0 || pos >= a.tok_stride) {
+      if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
+    } else {
+      tok = a.tokens[(int64_t)b * a.tok_stride + pos];
+      if (tok < 0 || tok >= kVocab) {
+        if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
+        tok = 0;
+      }
+    }
+    x = a.embd + tok * (int64_t)kDim;
+    for (int i = threadIdx.x; i < a.K / 8; i += 256)
+      reinterpret_cast<uint4*>(a.x_out + (int64_t)b * a.K)[i] = reinterpret_cast<const uint4*>(x)[i];
+  }
+  cta_rmsnorm_to_smem(x, a.gamma, a.K, xs, &rs);
+  for (int i = threadIdx.x; i < a.K / 8; i += 256)
+    reinterpret_cast<uint4*>(a.xn + (int64_t)b * a.K)[i] = reinterpret_cast<const uint4*>(xs)[i];
+}
+
+// ---------------------------------------------------------------- vocab head
+struct BVocabArgs {
+  CUtensorMap wmap;      // f16 [151936, 1024], box {64, 128}, SWIZZLE_128B
+  CUtensorMap xmap;      // f16 [npad, 1024], box {64, npad}, SWIZZLE_128B
+  int B;
+  int ntiles;            // vocabulary rows / 128
+  uint16_t* logits;      // optional [B][ld_logits]
+  int64_t ld_logits;
+  ArgmaxPartial* part;   // [gridDim.x][64]
+  unsigned int* counter;
+  int64_t* tokens;       // [B][tok_stride]; tokens[b][pos+1] = argmax
+  int64_t tok_stride;
+  BatchSeq* seq;         // advanced by the last CTA (pos += 1, n_gen += 1)
+  int64_t* token_out;    // optional [B]
+  int64_t* amax;         // optional [B][tok_stride]: argmax after every position, prompt included
+  int* err;              // optional device error word
+};
+
+constexpr int kBvAStages = 4;
+
+__host__ __device__ constexpr size_t bvocab_smem_bytes(int npad) {
+  return 1024 + (size_t)16 * npad * 128 /* all of x */ + (size_t)kBvAStages * kBgAtomA + 256;
+}
+
+template <int NPAD>
+__global__ void __launch_bounds__(kBgThreads, 1) k_bvocab(const __grid_constant__ BVocabArgs a) {
+  constexpr uint32_t TCOLS = 2 * NPAD <= 32 ? 32 : 2 * NPAD <= 64 ? 64 : 128;  // double buffer
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t x_full, a_full[kBvAStages], a_empty[kBvAStages];
+  __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], mma_done;
+  __shared__ uint32_t tmem_base;
+  __shared__ float wbv[4][NPAD];
+  __shared__ int64_t wbi[4][NPAD];
+  __shared__ int is_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t sX = base;                         // 16 atoms of [NPAD x 64]
+  const uint32_t sA = sX + 16 * NPAD * 128;         // [4][16 KB]
+  uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
+
+  if (threadIdx.x == 0) {
+    mbar_init(&x_full, 1);
+    for (int i = 0; i < kBvAStages; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(&mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base, TCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_launch_dependents();
+  const uint32_t tmem = tmem_base;
+  const uint32_t idesc = idesc_f16_f32(128, NPAD);
+  const int ntile_mine = (a.ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&a.wmap);
+      prefetch_tmap(&a.xmap);
+      // weights first: they do not depend on the previous kernel
+      const int total = ntile_mine * 16;
+      int i_done = 0;
+      bool x_issued = false;
+      for (int i = 0; i < total; ++i) {
+        const int t = (int)blockIdx.x + (i >> 4) * (int)gridDim.x, j = i & 15;
+        const int s = i % kBvAStages;
+        if (i >= kBvAStages &&
+            !mbar_wait_own(&a_empty[s], ((i / kBvAStages) - 1) & 1, a.err, kErrTimeoutEmpty))
+          break;
+        mbar_expect_tx(&a_full[s], kBgAtomA);
+        tma_load_2d(gbase + (sA - base) + s * kBgAtomA, &a.wmap, j * 64, t * 128, &a_full[s]);
+        i_done = i + 1;
+        if (!x_issued && i == kBvAStages - 1) {
+          pdl_wait();
+          mbar_expect_tx(&x_full, 16 * NPAD * 128);
+          for (int q = 0; q < 16; ++q) tma_load_2d(gbase + q * NPAD * 128, &a.xmap, q * 64, 0, &x_full);
+          x_issued = true;
+        }
+      }
+      if (!x_issued) {
+        pdl_wait();
+        mbar_expect_tx(&x_full, 16 * NPAD * 128);
+        for (int q = 0; q < 16; ++q) tma_load_2d(gbase + q * NPAD * 128, &a.xmap, q * 64, 0, &x_full);
+      }
+      // the CTA may not exit before every issued copy has landed
+      mbar_wait_own(&x_full, 0, a.err, kErrTimeoutFull);
+      for (int st = 0; st < kBvAStages && st < i_done; ++st)
+        mbar_wait_own(&a_full[st], ((i_done - 1 - st) / kBvAStages) & 1, a.err, kErrTimeoutFull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait_own(&x_full, 0, a.err, kErrTimeoutFull);
+      int i = 0;
+      for (int k = 0; ok && k < ntile_mine; ++k) {
+        const int ab = k & 1;
+        if (k >= 2 && !mbar_wait_own(&acc_empty[ab], ((k / 2) - 1) & 1, a.err, kErrTimeoutEmpty)) break;
+        tc_fence_after();
+        for (int j = 0; j < 16; ++j, ++i) {
+          const int s = i % kBvAStages;
+          if (!mbar_wait_own(&a_full[s], (i / kBvAStages) & 1, a.err, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aa = sA + s * kBgAtomA, xx = sX + j * NPAD * 128;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tmem + ab * NPAD, sw128_desc(aa + 32 * kk), sw128_desc(xx + 32 * kk), idesc,
+                     (j | kk) != 0);
+          umma_commit(&a_empty[s]);
+        }
+        umma_commit(&acc_full[ab]);
+      }
+      umma_commit(&mma_done);
+      mbar_wait_own(&mma_done, 0, a.err, kErrTimeoutFull);  // no MMA in flight at dealloc
+    }
+  } else {
+    // epilogue warps: per sequence, the best (value, index) of this CTA;
+    // lane j of a warp keeps the candidates of sequences j, j+32.
+    const int q = warp & 3;
+    const uint32_t lane_base = (32u * q) << 16;
+    constexpr int PER_LANE = (NPAD + 31) / 32;
+    float bv[PER_LANE];
+    int64_t bi[PER_LANE];
+#pragma unroll
+    for (int k = 0; k < PER_LANE; ++k) {
+      bv[k] = -__int_as_float(0x7f800000);
+      bi[k] = -1;
+    }
+    pdl_wait();
+    for (int k = 0; k < ntile_mine; ++k) {
+      const int t = (int)blockIdx.x + k * (int)gridDim.x;
+      const int ab = k & 1;
+      if (!mbar_wait_own(&acc_full[ab], (k / 2) & 1, a.err, kErrTimeoutFull)) break;
+      tc_fence_after();
+      const int64_t n = (int64_t)t * 128 + 32 * q + lane;
+#pragma unroll
+      for (int col0 = 0; col0 < NPAD; col0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + lane_base + ab * NPAD + col0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int b = col0 + j;
+          const uint16_t lh = f2h(__uint_as_float(v[j]));
+          if (a.logits != nullptr && b < a.B) a.logits[(int64_t)b * a.ld_logits + n] = lh;
+          float lv = h2f(lh);
+          int64_t li = n;
+          // warp argmax over its 32 rows (a total order: any reduction order works)
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, lv, off);
+            const int64_t oi = __shfl_xor_sync(0xffffffffu, li, off);
+            if (am_better(ov, oi, lv, li)) {
+              lv = ov;
+              li = oi;
+            }
+          }
+          if (lane == (b & 31) && am_better(lv, li, bv[b >> 5], bi[b >> 5])) {
+            bv[b >> 5] = lv;
+            bi[b >> 5] = li;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+    }
+#pragma unroll
+    for (int k = 0; k < PER_LANE; ++k) {
+      const int b = lane + 32 * k;
+      if (b < NPAD) {
+        wbv[q][b] = bv[k];
+        wbi[q][b] = bi[k];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TCOLS);
+  }
+  // CTA candidate per sequence, then the last CTA reduces all of them
+  if (threadIdx.x < NPAD) {
+    const int b = threadIdx.x;
+    float v = -__int_as_float(0x7f800000);
+    int64_t ii = -1;
+    for (int w = 0; w < 4; ++w)
+      if (am_better(wbv[w][b], wbi[w][b], v, ii)) {
+        v = wbv[w][b];
+        ii = wbi[w][b];
+      }
+    a.part[(int64_t)blockIdx.x * kBMaxBatch + b].v = v;
+    a.part[(int64_t)blockIdx.x * kBMaxBatch + b].i = ii;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(a.counter, 1u);
+    is_last = (prev == gridDim.x - 1);
+    if (is_last) *a.counter = 0u;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (threadIdx.x < a.B) {
+    const int b = threadIdx.x;
+    float v = -__int_as_float(0x7f800000);
+    int64_t ii = -1;
+    for (int c = 0; c < (int)gridDim.x; ++c) {
+      const ArgmaxPartial* p = a.part + (int64_t)c * kBMaxBatch + b;
+      const float pv = __ldcg(&p->v);
+      const int64_t pi = __ldcg(reinterpret_cast<const long long*>(&p->i));
+      if (am_better(pv, pi, v, ii)) {
+        v = pv;
+        ii = pi;
+      }
+    }
+    if (a.token_out != nullptr) a.token_out[b] = ii;
+    if (a.seq != nullptr) {
+      BatchSeq& s = a.seq[b];
+      if (s.pos < 0 || s.pos + 1 >= a.tok_stride) {  // no room for the next token
+        if (a.err) atomicCAS(a.err, 0, kErrBadPos);
+      } else {
+        if (a.amax != nullptr) a.amax[(int64_t)b * a.tok_stride + s.pos + 1] = ii;
+        if (s.pos + 1 >= s.n_prompt) {  // past the prompt: the argmax is the next token
+          a.tokens[(int64_t)b * a.tok_stride + s.pos + 1] = ii;
+          s.n_gen += 1;
+        }
+        s.pos += 1;
+      }
+    }
+  }
+}
+
+}  // namespace q3

@@ -1,0 +1,121 @@
+// q3_tc.cuh -- sm_100a tensor-core (tcgen05 / TMEM) and tensor-TMA helpers,
+// written directly in PTX.
+//
+// Shared-memory operands use the canonical K-major SWIZZLE_128B layout: a
+// "swizzle atom" is 8 rows x 128 bytes (64 f16 along K); the 16-byte chunk c
+// of row r is stored at chunk position c ^ (r % 8); atoms of consecutive 8-row
+// groups are 1024 bytes apart (the descriptor's stride byte offset).  A tensor
+// TMA load with CU_TENSOR_MAP_SWIZZLE_128B and a 64-element inner box writes
+// exactly this layout; the dequantising warps write it by hand.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+#include "q3_common.cuh"
+
+namespace q3 {
+
+// ---------------------------------------------------------------- TMEM
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Generic-proxy shared-memory writes -> visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] x B[smem desc]^T, kind::f16 (f16 x f16 -> f32).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on `bar` when every tcgen05.mma issued so far by this thread completes.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane (warp w reads lanes
+// 32*(w%4) .. +31; taddr carries the lane base in bits 16..31).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 1024-byte stride
+// between 8-row groups, descriptor version 1 (sm_100).  `saddr` is the shared
+// address of the operand's first byte (1024-byte aligned atom base, plus
+// 32 bytes per K=16 step inside the atom).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address, 16-byte units
+  d |= (uint64_t)1u << 16;                  // leading byte offset (unused when swizzled)
+  d |= (uint64_t)(1024u >> 4) << 32;        // stride byte offset
+  d |= (uint64_t)1u << 46;                  // version
+  d |= (uint64_t)2u << 61;                  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor of kind::f16 with f16 A/B, f32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4)                        // D format: f32
+         | (0u << 7) | (0u << 10)         // A, B: f16
+         | ((uint32_t)(N >> 3) << 17)     // N / 8
+         | ((uint32_t)(M >> 4) << 24);    // M / 16
+}
+
+// Byte offset of 16-byte chunk c of row r in a K-major SWIZZLE_128B operand
+// made of consecutive 8-row atoms.
+__device__ __forceinline__ uint32_t sw128_chunk_offset(uint32_t r, uint32_t c) {
+  return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
+}
+
+// ---------------------------------------------------------------- tensor TMA
+// 2-D tiled load (no multicast) of box {x.., y..} at coordinates (x, y),
+// completion on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+}  // namespace q3

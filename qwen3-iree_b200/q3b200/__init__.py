@@ -6,8 +6,8 @@ PyTorch.  Mirrors the public functions of the reference's IREE module
 """
 from ._lib import LIB_PATH, Q3Error, lib
 from .device import DeviceArray, Events, device_count, device_info, set_device, synchronize
-from .model import DeviceWeights, Qwen3Decoder
+from .model import BatchDecoder, DeviceWeights, Qwen3Decoder
 from .weights import synthetic_weights
 
 __all__ = ["LIB_PATH", "Q3Error", "lib", "DeviceArray", "Events", "device_count", "device_info",
-           "set_device", "synchronize", "DeviceWeights", "Qwen3Decoder", "synthetic_weights"]
+           "set_device", "synchronize", "BatchDecoder", "DeviceWeights", "Qwen3Decoder", "synthetic_weights"]

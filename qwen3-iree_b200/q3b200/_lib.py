@@ -94,6 +94,18 @@ SIGNATURES = {
     "q3_model_kernel_launches": [P, PI64],
     "q3_model_trace_steps": [P, I64, I64, P, I64, ctypes.POINTER(ctypes.c_int),
                              ctypes.POINTER(ctypes.c_int)],
+    "q3_bgemm_q8": [P, I64, I64, P, P, P, I, I, I, I, P],
+    "q3_bvocab_workspace_bytes": [],
+    "q3_bvocab_argmax": [P, I, P, I, P, P, P, P],
+    "q3_batch_create": [ctypes.POINTER(Weights), I, I64, P, PP],
+    "q3_batch_destroy": [P],
+    "q3_batch_stream": [P],
+    "q3_batch_begin": [P, I, P, I64, P],
+    "q3_batch_begin_random": [P, I, P, P, ctypes.c_uint64],
+    "q3_batch_steps": [P, I64],
+    "q3_batch_read": [P, P, P, ctypes.POINTER(ctypes.c_int)],
+    "q3_batch_read_argmax": [P, P],
+    "q3_batch_kernel_launches": [P, PI64],
     "q3_strerror": [I],
     "q3_last_error": [],
 }
@@ -103,6 +115,8 @@ _RESTYPE = {
     "q3_vocab_argmax_workspace_bytes": SZ,
     "q3_attention_workspace_bytes": SZ,
     "q3_model_stream": P,
+    "q3_bvocab_workspace_bytes": SZ,
+    "q3_batch_stream": P,
 }
 
 _lib: ctypes.CDLL | None = None

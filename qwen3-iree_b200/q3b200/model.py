@@ -166,3 +166,75 @@ class Qwen3Decoder:
             self.close()
         except Exception:
             pass
+
+
+class BatchDecoder:
+    """B independent sequences decoded together (B <= 64): tcgen05 tensor-core
+    projections and vocab head; attention per sequence over its own cache."""
+
+    def __init__(self, weights: DeviceWeights | dict, max_batch: int, max_seq_len: int,
+                 stream=None):
+        self.weights = weights if isinstance(weights, DeviceWeights) else DeviceWeights(weights)
+        self.max_batch, self.max_seq_len = int(max_batch), int(max_seq_len)
+        h = ctypes.c_void_p()
+        call("q3_batch_create", ctypes.byref(self.weights.struct), self.max_batch,
+             self.max_seq_len, stream, ctypes.byref(h))
+        self.handle = h.value
+        self.stream = lib().q3_batch_stream(self.handle)
+        self.B = 0
+
+    def begin(self, prompts: list) -> None:
+        """Sequence b starts at position 0 with prompt tokens prompts[b]."""
+        B = len(prompts)
+        width = max(len(p) for p in prompts)
+        tab = np.zeros((B, width), np.int64)
+        lens = np.array([len(p) for p in prompts], np.int64)
+        for b, p in enumerate(prompts):
+            tab[b, :len(p)] = p
+        call("q3_batch_begin", self.handle, B, tab.ctypes.data, width, lens.ctypes.data)
+        self.B = B
+
+    def begin_random(self, ctx_lens, tokens, seed: int = 0) -> None:
+        """Sequence b has a context of ctx_lens[b] pseudo-random cached positions."""
+        c = np.ascontiguousarray(ctx_lens, np.int64)
+        t = np.ascontiguousarray(tokens, np.int64)
+        call("q3_batch_begin_random", self.handle, c.size, c.ctypes.data, t.ctypes.data, seed)
+        self.B = c.size
+
+    def steps(self, n: int) -> None:
+        call("q3_batch_steps", self.handle, int(n))
+
+    def read(self):
+        """(tokens [B, S+1], positions [B]); raises on a device error word."""
+        toks = np.zeros((self.B, self.max_seq_len + 1), np.int64)
+        pos = np.zeros(self.B, np.int64)
+        err = ctypes.c_int(0)
+        call("q3_batch_read", self.handle, toks.ctypes.data, pos.ctypes.data, ctypes.byref(err))
+        if err.value:
+            raise RuntimeError(f"device error word {err.value}")
+        return toks, pos
+
+    def read_argmax(self) -> np.ndarray:
+        """[B, S+1]: entry p+1 is the greedy token after feeding position p."""
+        out = np.zeros((self.B, self.max_seq_len + 1), np.int64)
+        call("q3_batch_read_argmax", self.handle, out.ctypes.data)
+        return out
+
+    def kernel_launches(self) -> int:
+        n = ctypes.c_int64(0)
+        call("q3_batch_kernel_launches", self.handle, ctypes.byref(n))
+        return n.value
+
+    def synchronize(self) -> None:
+        call("q3_stream_synchronize", self.stream)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib().q3_batch_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
