@@ -42,6 +42,17 @@ constexpr uint32_t kBgAtomA = 128u * 128u;     // 128 rows x 64 f16, SWIZZLE_128
 
 enum BGemmMode : int { kBgPlain = 0, kBgResid = 1, kBgSwiglu = 2 };
 
+// A pipeline wait of the batched kernels gives up after ~0.2 s (a whole
+// decode step takes milliseconds) and records in the error word
+//   bits 0-3: kErrTimeout*, bits 4-7: wait site, bits 8-15: launch tag
+//   (layer * 8 + kernel), bits 16-27: CTA index.
+constexpr long long kBatchSpinCycles = 400000000ll;
+__device__ __forceinline__ int bwait_code(int code, int site, int tag) {
+  return code | (site << 4) | ((tag & 0xff) << 8) | (((int)blockIdx.x & 0xfff) << 16);
+}
+#define Q3_BWAIT(bar, parity, code, site) \
+  mbar_wait_own((bar), (parity), a.err, bwait_code((code), (site), a.tag), kBatchSpinCycles)
+
 // Device state of one sequence of a batch.
 struct BatchSeq {
   int64_t pos;       // position of the token fed this step
@@ -62,6 +73,7 @@ struct BGemmArgs {
   const uint16_t* r;     // residual [npad][ldy] (kBgResid)
   int64_t up_rows;       // kBgSwiglu: offset (rows) from a gate row to its up row
   int* err;              // optional device error word (pipeline wait timed out)
+  int tag;               // launch tag recorded with a timeout
 };
 
 // K=64 slices in flight between the dequantising warps and the MMA thread;
@@ -165,7 +177,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       for (int c = 0; ok && c < nchunk; ++c) {
         const int rs = c % kBgRawStages;
         if (c >= kBgRawStages &&
-            !mbar_wait_own(&raw_empty[rs], ((c / kBgRawStages) - 1) & 1, a.err, kErrTimeoutEmpty))
+            !Q3_BWAIT(&raw_empty[rs], ((c / kBgRawStages) - 1) & 1, kErrTimeoutEmpty, 1))
           break;
         mbar_expect_tx(&raw_full[rs], NACC * kBgRawBytes);
         for (int acc = 0; acc < NACC; ++acc)
@@ -175,7 +187,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
         for (int j = 0; j < 4; ++j) {
           const int i = c * 4 + j, ss = i % SUB;
           if (i >= SUB &&
-              !mbar_wait_own(&ax_empty[ss], ((i / SUB) - 1) & 1, a.err, kErrTimeoutEmpty)) {
+              !Q3_BWAIT(&ax_empty[ss], ((i / SUB) - 1) & 1, kErrTimeoutEmpty, 2)) {
             ok = false;
             break;
           }
@@ -187,9 +199,9 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       }
       // the CTA may not exit before every issued copy has landed
       for (int st = 0; st < kBgRawStages && st < c_done; ++st)
-        mbar_wait_own(&raw_full[st], ((c_done - 1 - st) / kBgRawStages) & 1, a.err, kErrTimeoutFull);
+        Q3_BWAIT(&raw_full[st], ((c_done - 1 - st) / kBgRawStages) & 1, kErrTimeoutFull, 3);
       for (int st = 0; st < SUB && st < i_done; ++st)
-        mbar_wait_own(&x_full[st], ((i_done - 1 - st) / SUB) & 1, a.err, kErrTimeoutFull);
+        Q3_BWAIT(&x_full[st], ((i_done - 1 - st) / SUB) & 1, kErrTimeoutFull, 4);
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
@@ -197,8 +209,8 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       for (int i = 0; i < nsub; ++i) {
         const int ss = i % SUB;
         const uint32_t par = (i / SUB) & 1;
-        if (!mbar_wait_own(&a_full[ss], par, a.err, kErrTimeoutFull)) break;
-        if (!mbar_wait_own(&x_full[ss], par, a.err, kErrTimeoutFull)) break;
+        if (!Q3_BWAIT(&a_full[ss], par, kErrTimeoutFull, 5)) break;
+        if (!Q3_BWAIT(&x_full[ss], par, kErrTimeoutFull, 6)) break;
         tc_fence_after();
         for (int acc = 0; acc < NACC; ++acc) {
           const uint32_t aa = sA + (acc * SUB + ss) * kBgAtomA;
@@ -211,7 +223,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
         umma_commit(&ax_empty[ss]);
       }
       umma_commit(&acc_full);
-      mbar_wait_own(&acc_full, 0, a.err, kErrTimeoutFull);  // no MMA in flight at dealloc
+      Q3_BWAIT(&acc_full, 0, kErrTimeoutFull, 7);  // no MMA in flight at dealloc
     }
   } else {
     // ------------------------------------------------ dequant, then epilogue
@@ -219,11 +231,11 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
     pdl_wait();  // the epilogue reads the previous kernels' residual stream
     for (int c = 0; c < nchunk; ++c) {
       const int rs = c % kBgRawStages;
-      if (!mbar_wait_own(&raw_full[rs], (c / kBgRawStages) & 1, a.err, kErrTimeoutFull)) break;
+      if (!Q3_BWAIT(&raw_full[rs], (c / kBgRawStages) & 1, kErrTimeoutFull, 8)) break;
       for (int j = 0; j < 4; ++j) {
         const int i = c * 4 + j, ss = i % SUB;
         if (i >= SUB &&
-            !mbar_wait_own(&ax_empty[ss], ((i / SUB) - 1) & 1, a.err, kErrTimeoutEmpty))
+            !Q3_BWAIT(&ax_empty[ss], ((i / SUB) - 1) & 1, kErrTimeoutEmpty, 9))
           break;
         for (int acc = 0; acc < NACC; ++acc)
           dequant_slice(sR + (rs * NACC + acc) * kBgRawBytes + r * 272u + 68u * j,
@@ -236,7 +248,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       if (lane == 0) mbar_arrive(&raw_empty[rs]);
     }
     // epilogue
-    if (mbar_wait_own(&acc_full, 0, a.err, kErrTimeoutFull)) {
+    if (Q3_BWAIT(&acc_full, 0, kErrTimeoutFull, 10)) {
       tc_fence_after();
       const uint32_t lane_base = (32u * (warp & 3)) << 16;
       const int n = n0 + (int)r;
@@ -336,6 +348,7 @@ struct BVocabArgs {
   int64_t* token_out;    // optional [B]
   int64_t* amax;         // optional [B][tok_stride]: argmax after every position, prompt included
   int* err;              // optional device error word
+  int tag;               // launch tag recorded with a timeout
 };
 
 constexpr int kBvAStages = 4;
@@ -398,7 +411,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bvocab(const __grid_constant_
         const int t = (int)blockIdx.x + (i >> 4) * (int)gridDim.x, j = i & 15;
         const int s = i % kBvAStages;
         if (i >= kBvAStages &&
-            !mbar_wait_own(&a_empty[s], ((i / kBvAStages) - 1) & 1, a.err, kErrTimeoutEmpty))
+            !Q3_BWAIT(&a_empty[s], ((i / kBvAStages) - 1) & 1, kErrTimeoutEmpty, 11))
           break;
         mbar_expect_tx(&a_full[s], kBgAtomA);
         tma_load_2d(gbase + (sA - base) + s * kBgAtomA, &a.wmap, j * 64, t * 128, &a_full[s]);
@@ -416,21 +429,21 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bvocab(const __grid_constant_
         for (int q = 0; q < 16; ++q) tma_load_2d(gbase + q * NPAD * 128, &a.xmap, q * 64, 0, &x_full);
       }
       // the CTA may not exit before every issued copy has landed
-      mbar_wait_own(&x_full, 0, a.err, kErrTimeoutFull);
+      Q3_BWAIT(&x_full, 0, kErrTimeoutFull, 12);
       for (int st = 0; st < kBvAStages && st < i_done; ++st)
-        mbar_wait_own(&a_full[st], ((i_done - 1 - st) / kBvAStages) & 1, a.err, kErrTimeoutFull);
+        Q3_BWAIT(&a_full[st], ((i_done - 1 - st) / kBvAStages) & 1, kErrTimeoutFull, 13);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      bool ok = mbar_wait_own(&x_full, 0, a.err, kErrTimeoutFull);
+      bool ok = Q3_BWAIT(&x_full, 0, kErrTimeoutFull, 14);
       int i = 0;
       for (int k = 0; ok && k < ntile_mine; ++k) {
         const int ab = k & 1;
-        if (k >= 2 && !mbar_wait_own(&acc_empty[ab], ((k / 2) - 1) & 1, a.err, kErrTimeoutEmpty)) break;
+        if (k >= 2 && !Q3_BWAIT(&acc_empty[ab], ((k / 2) - 1) & 1, kErrTimeoutEmpty, 15)) break;
         tc_fence_after();
         for (int j = 0; j < 16; ++j, ++i) {
           const int s = i % kBvAStages;
-          if (!mbar_wait_own(&a_full[s], (i / kBvAStages) & 1, a.err, kErrTimeoutFull)) {
+          if (!Q3_BWAIT(&a_full[s], (i / kBvAStages) & 1, kErrTimeoutFull, 16)) {
             ok = false;
             break;
           }
@@ -445,7 +458,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bvocab(const __grid_constant_
         umma_commit(&acc_full[ab]);
       }
       umma_commit(&mma_done);
-      mbar_wait_own(&mma_done, 0, a.err, kErrTimeoutFull);  // no MMA in flight at dealloc
+      Q3_BWAIT(&mma_done, 0, kErrTimeoutFull, 17);  // no MMA in flight at dealloc
     }
   } else {
     // epilogue warps: per sequence, the best (value, index) of this CTA;
@@ -464,7 +477,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bvocab(const __grid_constant_
     for (int k = 0; k < ntile_mine; ++k) {
       const int t = (int)blockIdx.x + k * (int)gridDim.x;
       const int ab = k & 1;
-      if (!mbar_wait_own(&acc_full[ab], (k / 2) & 1, a.err, kErrTimeoutFull)) break;
+      if (!Q3_BWAIT(&acc_full[ab], (k / 2) & 1, kErrTimeoutFull, 18)) break;
       tc_fence_after();
       const int64_t n = (int64_t)t * 128 + 32 * q + lane;
 #pragma unroll

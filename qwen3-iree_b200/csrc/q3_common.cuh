@@ -182,12 +182,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 // Bounded wait that records `code` in *err on timeout but, unlike mbar_wait,
 // keeps waiting when some other kernel raised *err: a pipeline role that
 // stops early must still see its own copies and MMAs complete.
-__device__ __forceinline__ bool mbar_wait_own(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_own(uint64_t* bar, uint32_t parity, int* err, int code,
+                                              long long limit = kSpinCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > kSpinCycles) {
+    if (clock64() - t0 > limit) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }
