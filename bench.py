@@ -17,6 +17,8 @@ stream) of the K timed steps, max over ranks.  e2e: q3_run (the public call
 mirroring the reference's @run) with host prompt in / host tokens out, wall
 clock, as scripts/benchmark.py measures it.  N>1 (torchrun): independent
 replicas, one per GPU, no collective on the data path (replicas only).
+"batched": BASELINE configs[3] (B=32) and configs[4] (B=64 per replica) on the
+tensor-core batched path, device time of 128 steps.
 """
 from __future__ import annotations
 
@@ -359,6 +361,8 @@ def run_ours(args, d: Dist) -> None:
 
     # streaming GEMV bandwidth: 28 layers of one projection in one launch
     gemv_stream = measure_gemv_stream(q3b200, dw, peak) if not args.quick else {}
+    batched = {} if args.no_batched else {
+        k: measure_batched(q3b200, dw, d, k, args.seed, peak, args.warmup) for k in BATCHED}
 
     # end to end through the public call (host prompt in, host tokens out)
     e2e_vals = []
@@ -406,10 +410,94 @@ def run_ours(args, d: Dist) -> None:
                               "frac_of_measured": bytes_total / done / (ms * 1e-3) / 1e9 / peak},
             "graph_engine_kernels": kern,
             "gemv_stream": gemv_stream,
+            "batched": batched,
             "device_error": err,
         }
         print(json.dumps(line), flush=True)
     dec.close()
+
+
+BATCHED = {"b32": (32, 128, 2048, "configs[3]"), "b64": (64, 512, 4096, "configs[4]")}
+BATCH_STEPS = 128
+BATCH_KINDS = {0: "qkv", 1: "attn", 2: "o", 3: "gate_up", 4: "down", 5: "vocab", 6: "norm"}
+# activation f16 elements (in, out) per sequence of the batched projections
+BATCH_ACT = {"qkv": (1024, 4096), "o": (2048 + 1024, 1024), "gate_up": (1024, 3072),
+             "down": (3072 + 1024, 1024)}
+
+
+def batch_kernel_bytes(name: str, B: int, pos) -> float:
+    """Algorithmic HBM bytes of one launch of a batched-step kernel; pos are
+    the sequences' positions (each attends pos+1 keys)."""
+    if name in Q8_BYTES:
+        i, o = BATCH_ACT[name]
+        return Q8_BYTES[name] + 2 * B * (i + o)
+    if name == "attn":
+        return float(sum(2 * KV_ROW * (int(p) + 1) + 2 * KV_ROW + 8192 + 4096 for p in pos))
+    if name == "vocab":
+        return 151936 * 1024 * 2 + B * 2048 + B * 16
+    return B * (2048 + 2048) + 2048  # norm: x in, xn out, gamma
+
+
+def measure_batched(q3b200, dw, d: Dist, key: str, seed: int, peak: float, warmup: int) -> dict:
+    """B sequences whose cached contexts are
+    U[lo, hi] positions of seeded pseudo-random K/V, 128 decode steps of all of
+    them (tcgen05 projections, split-KV attention per sequence).  Device time
+    of the 128 steps (CUDA events on the decoder's stream), max over ranks;
+    tokens summed over ranks (replicas)."""
+    B, lo, hi, cfg = BATCHED[key]
+    rng = np.random.default_rng(seed + B)
+    ctx = rng.integers(lo, hi + 1, size=B)
+    tok = rng.integers(0, 151936, size=B)
+    S = hi + BATCH_STEPS + warmup + 2
+    bd = q3b200.BatchDecoder(dw, max_batch=B, max_seq_len=S)
+    bd.begin_random(ctx, tok, seed=seed)
+    bd.steps(warmup)
+    bd.synchronize()
+    ev = q3b200.Events()
+    l0 = bd.kernel_launches()
+    d.barrier()
+    ev.record_start(bd.stream)
+    bd.steps(BATCH_STEPS)
+    ev.record_end(bd.stream)
+    ms = ev.elapsed_ms()
+    launches = bd.kernel_launches() - l0
+    toks, pos = bd.read()
+    assert (pos == ctx + warmup + BATCH_STEPS).all(), "batched positions did not advance"
+    # per-kernel device times (serialised by events) over a few more steps
+    prof_steps = 4
+    times_us, kinds = bd.profile_steps(prof_steps)
+    bd.close()
+    ppos = ctx + warmup + BATCH_STEPS + prof_steps // 2
+    kern = {}
+    for kind, name in BATCH_KINDS.items():
+        sel = times_us[kinds == kind]
+        if sel.size == 0:
+            continue
+        b = batch_kernel_bytes(name, B, ppos)
+        avg = float(sel.mean())
+        kern[name] = {"launches_per_step": int(sel.size), "avg_us": avg,
+                      "total_us_per_step": float(sel.sum()), "alg_bytes_per_launch": b,
+                      "achieved_gbs": b / (avg * 1e-6) / 1e9}
+    tot = float(times_us.sum())
+    for k in kern.values():
+        k["share"] = k["total_us_per_step"] / tot
+    dom = max(kern, key=lambda k: kern[k]["total_us_per_step"])
+    t_max = d.max(ms)
+    w = sum(Q8_BYTES.values()) * 28 + VOCAB_BYTES + NORM_BYTES
+    kv = sum(28 * (2 * KV_ROW * (int(c) + i + 1) + 2 * KV_ROW)
+             for i in range(warmup, warmup + BATCH_STEPS) for c in ctx)
+    step_b = (w * BATCH_STEPS + kv) / BATCH_STEPS
+    gbs = step_b / (ms / BATCH_STEPS * 1e-3) / 1e9
+    return {"workload": f"{cfg}: B={B} sequences, context U[{lo},{hi}], {BATCH_STEPS} decode steps",
+            "tok_s": d.sum(B * BATCH_STEPS) / (t_max / 1e3), "ms_per_step": t_max / BATCH_STEPS,
+            "alg_bytes_per_step": step_b, "achieved_gbs": gbs, "frac_of_measured": gbs / peak,
+            "frac_of_8tbs": gbs / NOMINAL_HBM_GBS, "launches_per_step": launches / BATCH_STEPS,
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["achieved_gbs"],
+                         "peak": peak, "unit": "GB/s",
+                         "frac": kern[dom]["achieved_gbs"] / peak},
+            "kernels": kern,
+            "l2": "inputs larger than L2 (779 MB of weights + the KV caches every step)"}
 
 
 def measure_gemv_stream(q3b200, dw, peak: float) -> dict:
@@ -454,6 +542,7 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=60.0, help="seconds, reference arm")
     ap.add_argument("--quick", action="store_true", help="skip the GEMV streaming sweep")
     ap.add_argument("--engine", default="graph", choices=["persistent", "graph"])
+    ap.add_argument("--no-batched", action="store_true", help="skip the B=32 / B=64 legs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     d = Dist() if args.impl == "ours" else None

@@ -253,6 +253,7 @@ int q3_generate_end(q3_model* m, int64_t* out_tokens, int64_t* n_out);
 #define Q3_KIND_GATE_UP 3 /* RMSNorm + gate|up + SwiGLU */
 #define Q3_KIND_DOWN 4    /* down projection + residual */
 #define Q3_KIND_VOCAB 5   /* final RMSNorm + vocab GEMV + argmax */
+#define Q3_KIND_NORM 6    /* stand-alone RMSNorm (batched decoder only) */
 int q3_model_profile_steps(q3_model* m, int64_t steps, float* times_us, int32_t* kinds,
                            int64_t cap);
 
@@ -333,6 +334,11 @@ int q3_batch_read(q3_batch* m, int64_t* tokens, int64_t* positions, int* device_
  * greedy token after the step that fed position p, prompt positions included
  * (-1 where no step ran); for teacher-forced checks.  Synchronises. */
 int q3_batch_read_argmax(q3_batch* m, int64_t* out);
+/* Per-kernel device times of `steps` decode steps (which advance the
+ * sequences), averaged per kernel of a step: times_us[i], kinds[i]
+ * (Q3_KIND_*) for i < *n_kernels; events between kernels serialise them. */
+int q3_batch_profile_steps(q3_batch* m, int64_t steps, float* times_us, int32_t* kinds,
+                           int64_t cap, int64_t* n_kernels);
 int q3_batch_kernel_launches(q3_batch* m, int64_t* n);
 
 #ifdef __cplusplus

@@ -1,0 +1,159 @@
+"""ctypes twin of the reference's scripts/benchmark.py.
+
+The reference times `@run` of an IREE module once per prompt
+(scripts/benchmark.py:52-81): chat-formatted prompt tokens in, up to
+MAX_TOKENS greedy tokens out, output cut at the first end-of-text token,
+tok/s = kept tokens / wall time of the call, then mean +- std over the
+prompts (:157-170) and a JSON dump (:203-206).  This twin makes the same
+calls through libq3b200.so (`Qwen3Decoder.run` = q3_run), with no IREE and
+no PyTorch.
+
+Differences forced by this environment: there is no checkpoint or
+tokenizer.json here, so weights are the seeded random-init model of the
+benchmark configs and prompts are token-id lists -- seeded ones by default,
+one line of ids per prompt with --prompts-file, or text with --tokenizer.
+
+  python -m q3b200.benchmark [--max-tokens 128] [--json out.json]
+  python -m q3b200.benchmark --batch 32 --context 128 2048 --steps 128
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+import time
+
+import numpy as np
+
+EOS_TOKEN = 151645
+MAX_TOKENS = 128
+VOCAB = 151936
+CHAT_TEMPLATE = "<|im_start|>user\n{}<|im_end|>\n<|im_start|>assistant\n"
+
+
+def trim_eos(tokens, eos: int = EOS_TOKEN) -> list[int]:
+    """Tokens up to (not including) the first end-of-text token
+    (scripts/benchmark.py:77-79)."""
+    tokens = [int(t) for t in tokens]
+    return tokens[:tokens.index(eos)] if eos in tokens else tokens
+
+
+def synthetic_prompts(n: int = 10, seed: int = 0) -> list[list[int]]:
+    """n seeded token-id prompts of increasing length (12..48 ids, the range
+    of short chat-formatted questions)."""
+    rng = np.random.default_rng(seed)
+    lengths = np.linspace(12, 48, n).astype(int)
+    return [rng.integers(0, VOCAB, size=int(L)).tolist() for L in lengths]
+
+
+def read_prompts_file(path: str) -> list[list[int]]:
+    """One prompt per non-empty line: whitespace- or comma-separated token ids."""
+    out = []
+    for line in open(path):
+        ids = [int(t) for t in line.replace(",", " ").split()]
+        if ids:
+            out.append(ids)
+    return out
+
+
+def load_tokenizer(path: str | None):
+    if not path:
+        return None
+    from tokenizers import Tokenizer  # optional dependency, only with --tokenizer
+
+    return Tokenizer.from_file(path)
+
+
+def bench_one(dec, tokens: list[int], max_tokens: int, eos: int = EOS_TOKEN):
+    """One @run call (scripts/benchmark.py:52-81): (n_in, n_out, seconds)."""
+    t0 = time.perf_counter()
+    out, n = dec.run(np.asarray(tokens, np.int64), max_tokens, eos)
+    dt = time.perf_counter() - t0
+    return len(tokens), len(trim_eos(out[:n], eos)), dt
+
+
+def bench_batched(dw, B: int, lo: int, hi: int, steps: int, seed: int = 0) -> dict:
+    """B sequences with cached contexts of U[lo, hi] positions, `steps`
+    decode steps of all of them on the tensor-core batched path."""
+    from . import BatchDecoder, Events
+
+    rng = np.random.default_rng(seed + B)
+    ctx = rng.integers(lo, hi + 1, size=B)
+    tok = rng.integers(0, VOCAB, size=B)
+    bd = BatchDecoder(dw, max_batch=B, max_seq_len=int(hi + steps + 5))
+    bd.begin_random(ctx, tok, seed=seed)
+    bd.steps(3)
+    bd.synchronize()
+    ev = Events()
+    ev.record_start(bd.stream)
+    bd.steps(steps)
+    ev.record_end(bd.stream)
+    ms = ev.elapsed_ms()
+    _, pos = bd.read()
+    bd.close()
+    assert (pos == ctx + 3 + steps).all()
+    return {"batch": B, "context": [lo, hi], "steps": steps, "ms_per_step": ms / steps,
+            "tok_s": B * steps / (ms / 1e3)}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description="Benchmark Qwen3-0.6B Q8_0 decode on libq3b200.so")
+    ap.add_argument("--max-tokens", type=int, default=MAX_TOKENS)
+    ap.add_argument("--prompts-file", default=None, help="one line of token ids per prompt")
+    ap.add_argument("--tokenizer", default=None, help="tokenizer.json (text prompts)")
+    ap.add_argument("--text", action="append", default=None, help="text prompt (with --tokenizer)")
+    ap.add_argument("--seed", type=int, default=0, help="weights and synthetic prompts")
+    ap.add_argument("--engine", default="graph", choices=["graph", "persistent"])
+    ap.add_argument("--max-seq-len", type=int, default=1024)
+    ap.add_argument("--json", default=None, help="write results here")
+    ap.add_argument("--batch", type=int, default=0, help="batched mode: B sequences")
+    ap.add_argument("--context", type=int, nargs=2, default=[128, 2048], metavar=("LO", "HI"))
+    ap.add_argument("--steps", type=int, default=128, help="batched mode: decode steps")
+    ap.add_argument("--device", type=int, default=0)
+    args = ap.parse_args(argv)
+
+    from . import DeviceWeights, Qwen3Decoder, set_device
+    from .weights import synthetic_weights
+
+    set_device(args.device)
+    dw = DeviceWeights(synthetic_weights(seed=args.seed))
+
+    if args.batch:
+        r = bench_batched(dw, args.batch, args.context[0], args.context[1], args.steps, args.seed)
+        print(f"  B={r['batch']} context U[{args.context[0]},{args.context[1]}] "
+              f"{r['steps']} steps: {r['ms_per_step']:.3f} ms/step, {r['tok_s']:.0f} tok/s",
+              flush=True)
+        if args.json:
+            with open(args.json, "w") as f:
+                json.dump(r, f, indent=2)
+        return 0
+
+    tok = load_tokenizer(args.tokenizer)
+    if tok is not None and args.text:
+        prompts = [tok.encode(CHAT_TEMPLATE.format(t)).ids for t in args.text]
+        labels = [t[:40] for t in args.text]
+    else:
+        prompts = (read_prompts_file(args.prompts_file) if args.prompts_file
+                   else synthetic_prompts(seed=args.seed))
+        labels = [f"{len(p)} ids" for p in prompts]
+
+    dec = Qwen3Decoder(dw, max_seq_len=args.max_seq_len, engine=args.engine)
+    bench_one(dec, prompts[0], 4)  # graph capture and first-call set-up
+    tps = []
+    for i, (p, label) in enumerate(zip(prompts, labels)):
+        n_in, n_out, dt = bench_one(dec, p, args.max_tokens)
+        tps.append(n_out / dt if dt > 0 else 0.0)
+        print(f"  [{i + 1:2d}/{len(prompts)}] {label:<40s} in={n_in:3d} out={n_out:3d} "
+              f"{dt:6.3f}s {tps[-1]:7.1f} tok/s", flush=True)
+    mean, std = float(np.mean(tps)), float(np.std(tps))
+    print(f"  -> mean={mean:.1f} +- {std:.1f} tok/s", flush=True)
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump({"libq3b200": {"tps": tps, "mean": mean, "std": std,
+                                     "prompts": labels, "engine": dec.engine}}, f, indent=2)
+    dec.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -214,6 +214,17 @@ class BatchDecoder:
             raise RuntimeError(f"device error word {err.value}")
         return toks, pos
 
+    def profile_steps(self, steps: int):
+        """(times_us, kinds) per kernel of one step, averaged over `steps`
+        decode steps (which advance the sequences)."""
+        cap = 512
+        t = np.zeros(cap, np.float32)
+        k = np.zeros(cap, np.int32)
+        n = ctypes.c_int64(0)
+        call("q3_batch_profile_steps", self.handle, int(steps), t.ctypes.data, k.ctypes.data, cap,
+             ctypes.byref(n))
+        return t[:n.value].copy(), k[:n.value].copy()
+
     def read_argmax(self) -> np.ndarray:
         """[B, S+1]: entry p+1 is the greedy token after feeding position p."""
         out = np.zeros((self.B, self.max_seq_len + 1), np.int64)
