@@ -299,9 +299,13 @@ int q3_model_device_error(q3_model* m, int* code);
  *   mode 0: y = W x;   mode 1: y = r + W x (r laid out like y);
  *   mode 2: gate rows [row0, row0+N), up rows [row0+N, row0+2N):
  *           y = silu(gate) * up in f16 (model/qwen3_full.mlir:829-839).
- * N % 128 == 0, K % 256 == 0, K <= 3072. */
+ * N % 128 == 0, K % 256 == 0, K <= 3072.  ksplit CTAs (one thread-block
+ * cluster) share each 128-row tile, each over K/ksplit; ksplit divides K/256,
+ * is at most 8 and leaves at most 2 chunks of 256 per CTA (1 for mode 2);
+ * 0 picks one.  No workspace: the split partials are summed in shared memory,
+ * in split order. */
 int q3_bgemm_q8(const void* w, int64_t w_rows, int64_t row0, const void* x, void* y,
-                const void* r, int B, int N, int K, int mode, void* stream);
+                const void* r, int B, int N, int K, int mode, int ksplit, void* stream);
 /* Batched vocab GEMV + argmax (model/qwen3_full.mlir:1456-1509 per row):
  * logits[b][N] (optional, f16) and tokens[b] = first index of the largest f16
  * logit of xn[b] (xn already normalised).  Workspace zero-filled once. */

@@ -488,10 +488,13 @@ void q3o_add_f16(const uint16_t* a, const uint16_t* b, uint16_t* y, int n) {
  *   s_t = (fma chain of q_d*k_td over d) * scale,  m = max s_t,
  *   p_t = exp(s_t - m),  l = butterfly sum of p_t,
  *   o_d = fma chain of p_t*v_td over t in key order;
- * the chunk results are folded left to right with
+ * chunks are folded in two levels -- left to right within each group of
+ * Q3O_ATT_GROUP consecutive chunks (one CTA of the kernel), then the group
+ * results left to right -- each fold step being
  *   m = max(ma, mb), a = exp(ma - m), b = exp(mb - m),
  *   l = fma(lb, b, la*a),  o_d = fma(ob_d, b, oa_d*a);
- * finally out_d = f16(o_d / l). */
+ * finally out_d = f16(o_d / l).  With T <= 256 there is one group and the
+ * fold is a plain left-to-right fold of the chunks. */
 typedef struct {
   float m, l;
   float o[Q3O_HD];
@@ -514,7 +517,7 @@ void q3o_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, in
     const int kvh = h / 2;
     float qf[Q3O_HD];
     x_to_f32(q + h * Q3O_HD, qf, Q3O_HD);
-    att_part total, chunk;
+    att_part total, group, chunk;
     for (int64_t c = 0; c < nchunks; ++c) {
       float s[32], p[32];
       int valid = 0;
@@ -540,10 +543,16 @@ void q3o_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, in
         const uint16_t* v = vc + (slot0 + c * 32 + l) * row + kvh * Q3O_HD;
         for (int d = 0; d < Q3O_HD; ++d) chunk.o[d] = fmaf(p[l], q3o_h2f(v[d]), chunk.o[d]);
       }
-      if (c == 0)
-        total = chunk;
+      if (c % Q3O_ATT_GROUP == 0)
+        group = chunk;
       else
-        att_merge(&total, &chunk);
+        att_merge(&group, &chunk);
+      if (c % Q3O_ATT_GROUP == Q3O_ATT_GROUP - 1 || c == nchunks - 1) {
+        if (c < Q3O_ATT_GROUP)
+          total = group;
+        else
+          att_merge(&total, &group);
+      }
     }
     for (int d = 0; d < Q3O_HD; ++d) out[h * Q3O_HD + d] = q3o_f2h(total.o[d] / total.l);
   }

@@ -30,6 +30,7 @@ extern "C" {
 
 /* attention chunk shared with the CUDA kernel (see q3o_attention) */
 #define Q3O_ATT_CHUNK 32
+#define Q3O_ATT_GROUP 8  /* chunks folded together before the cross-group fold */
 
 /* numeric primitives */
 float q3o_h2f(uint16_t h);

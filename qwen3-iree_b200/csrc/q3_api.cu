@@ -4,6 +4,7 @@
 // CUDA graphs of the fused kernels.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -288,6 +289,32 @@ static cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, size_t 
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+// The same with thread-block clusters of cluster_y CTAs along y.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_cluster(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t st, bool pdl, int cluster_y, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = 1;
+  attr[n].val.clusterDim.y = (unsigned)cluster_y;
+  attr[n].val.clusterDim.z = 1;
+  ++n;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 struct LaunchShape {
   int grid, nstages;
   size_t smem;
@@ -471,10 +498,25 @@ extern "C" size_t q3_attention_workspace_bytes(int64_t S) {
   return sizeof(AttnPartial) * (size_t)kNKV * mc * 2 + 256;
 }
 
+// K/V loads issued before the norms (1 CTA per SM at 182 registers) or after
+// them (2 CTAs per SM); Q3_ATTN_EARLY=0|1 overrides the per-batch default.
+static bool attn_early_loads(int batch) {
+  static int env = -2;
+  if (env == -2) {
+    const char* e = getenv("Q3_ATTN_EARLY");
+    env = (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : -1;
+  }
+  if (env >= 0) return env == 1;
+  return batch == 1;
+}
+
 static int launch_attn(const AttnArgs& a, int batch, cudaStream_t st, int* launches,
                        bool pdl = false) {
   dim3 grid(kNKV, (unsigned)max_groups_for((int64_t)a.max_chunks * kAttChunk), batch);
-  Q3_CUDA(launch_ex(k_attn_decode, grid, dim3(256), 0, st, pdl, a));
+  if (attn_early_loads(batch))
+    Q3_CUDA(launch_ex(k_attn_decode<true>, grid, dim3(256), 0, st, pdl, a));
+  else
+    Q3_CUDA(launch_ex(k_attn_decode<false>, grid, dim3(256), 0, st, pdl, a));
   if (launches) ++*launches;
   return Q3_OK;
 }

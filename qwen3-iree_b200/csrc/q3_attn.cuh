@@ -9,11 +9,14 @@
 // Flash decode over chunks of 32 keys.  A group (one CTA, 8 warps) owns 8
 // consecutive chunks of one kv head h; each warp turns one chunk into a
 // partial (m, l, o[128]) for both q heads 2h and 2h+1, so every K/V row is
-// read once (lane = key for q.k, lane = 4 head dims for p.v; all loads of a
-// chunk are issued before its arithmetic).  The CTA that finishes last for
-// head h (an arrival counter, no spin-waits) folds all chunk partials of h
-// left to right.  The CPU oracle (q3o_attention) states the same order, so
-// any assignment of groups to CTAs gives the same bits.
+// read once (lane = key for q.k, lane = 4 head dims for p.v; a chunk's loads
+// are issued before everything else the CTA does).  The CTA folds its chunk
+// partials left to right in shared memory; with one group (pos < 256) that is
+// the result, otherwise it publishes the group partial and the CTA that
+// finishes last for head h (an arrival counter, no spin-waits) folds the
+// group partials left to right, loading eight at a time.  The CPU oracle
+// (q3o_attention) states the same two-level order, so any assignment of
+// groups to CTAs gives the same bits.
 #pragma once
 
 #include "q3_common.cuh"
@@ -70,6 +73,7 @@ struct AttnCtx {
 };
 
 struct AttnSmem {
+  AttnPartial part[kAttSplitChunks][2];  // this CTA's chunk partials when it holds every chunk
   uint16_t qs[2][kHD];
   uint16_t ks[kHD];
   int last;
@@ -114,15 +118,58 @@ __device__ __forceinline__ void att_merge(float& m, float& l, float (&o)[4], flo
   m = mm;
 }
 
+// Fold the first n partials of a group held in shared memory, left to right.
+__device__ __forceinline__ void fold_smem(const AttnSmem& sm, int n, int hh, int lane, float& m,
+                                          float& l, float (&o)[4]) {
+  m = sm.part[0][hh].m;
+  l = sm.part[0][hh].l;
+  {
+    const float4 t4 = *reinterpret_cast<const float4*>(&sm.part[0][hh].o[4 * lane]);
+    o[0] = t4.x, o[1] = t4.y, o[2] = t4.z, o[3] = t4.w;
+  }
+  for (int k = 1; k < n; ++k) {
+    const AttnPartial& q = sm.part[k][hh];
+    const float4 t4 = *reinterpret_cast<const float4*>(&q.o[4 * lane]);
+    const float ob[4] = {t4.x, t4.y, t4.z, t4.w};
+    att_merge(m, l, o, q.m, q.l, ob);
+  }
+}
+
 // One group (kv head h, chunks 8g .. 8g+7) on the 256 consumer threads of a
 // CTA.  Must be called by all of them.  Returns after the head's output is
-// written if this CTA was the last of head h, else after its partials are.
+// written if this CTA was the last of head h, else after its group partial is.
+// EARLY: issue the K/V loads before the norms (latency hidden, more live
+// registers); otherwise right after them.  Both give the same bits.
+template <bool EARLY>
 __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnSmem& sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t pos = c.pos, T = pos + 1;
   const int nch = attn_nchunks(pos);
   const int ngroups = attn_ngroups(pos);
   const int64_t rowel = (int64_t)kNKV * kHD;
+  const int ci = g * kAttSplitChunks + warp;
+  const bool have = ci < nch;
+  const int64_t t0 = (int64_t)ci * kAttChunk;
+  const int64_t t = t0 + lane;
+  const bool valid = have && t < T;
+  const int nvalid = !have ? 0 : (int)((T - t0) < kAttChunk ? (T - t0) : kAttChunk);
+
+  // 0) this warp's K/V loads go out first (they do not depend on the norms
+  //    below): this lane's K row, and 4 dims of every V row of the chunk.  Key
+  //    pos is written by this launch and is substituted after step 1.
+  uint4 kv[kHD / 8];
+  uint2 vv[kAttChunk];
+  auto load_chunk = [&]() {
+    const uint4* kr = reinterpret_cast<const uint4*>(c.kc + (c.slot0 + (valid ? t : t0)) * rowel + h * kHD);
+#pragma unroll
+    for (int v = 0; v < kHD / 8; ++v) kv[v] = __ldcg(kr + v);
+    const uint16_t* vbase = c.vc + (c.slot0 + t0) * rowel + h * kHD + 4 * lane;
+#pragma unroll
+    for (int tt = 0; tt < kAttChunk; ++tt)
+      vv[tt] = tt < nvalid ? __ldcg(reinterpret_cast<const uint2*>(vbase + (int64_t)tt * rowel))
+                           : make_uint2(0u, 0u);
+  };
+  if (EARLY && have) load_chunk();
 
   // 1) q heads 2h, 2h+1 and k head h: norm + rope into shared memory
   if (warp < 3) {
@@ -133,32 +180,25 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
       head_norm_rope(c.qkv + 2048 + h * kHD, c.k_norm, c0, s0, c1, s1, lane, sm.ks);
   }
   consumer_sync();
-  // 2) the group holding key `pos` writes the new K (normed, roped) and V rows
+  // 2) the group holding key pos writes the new K (normed, roped) and V rows,
+  //    and the warp holding it takes them from here instead of its stale loads
   if (g == ngroups - 1 && threadIdx.x < kHD) {
     const int64_t off = (c.slot0 + pos) * rowel + h * kHD + threadIdx.x;
     c.kc[off] = sm.ks[threadIdx.x];
     c.vc[off] = __ldcg(reinterpret_cast<const unsigned short*>(c.qkv) + 3072 + h * kHD + threadIdx.x);
   }
-  consumer_sync();
+  if (!EARLY && have) load_chunk();
+  // key pos of this chunk (if any) comes from shared memory / the projection
+  const int tp = (have && pos < t0 + kAttChunk) ? (int)(pos - t0) : -1;
+  if (lane == tp) {
+#pragma unroll
+    for (int v = 0; v < kHD / 8; ++v) kv[v] = reinterpret_cast<const uint4*>(sm.ks)[v];
+  }
+  uint2 nv = make_uint2(0u, 0u);
+  if (tp >= 0) nv = __ldcg(reinterpret_cast<const uint2*>(c.qkv + 3072 + h * kHD + 4 * lane));
 
-  // 3) one chunk of 32 keys per warp -> its partial in global memory
-  const int ci = g * kAttSplitChunks + warp;
-  if (ci < nch) {
-    const int64_t t0 = (int64_t)ci * kAttChunk;
-    const int64_t t = t0 + lane;
-    const bool valid = t < T;
-    const int nvalid = (int)((T - t0) < kAttChunk ? (T - t0) : kAttChunk);
-    // issue every load of the chunk first: this lane's K row, and 4 dims of all V rows
-    uint4 kv[kHD / 8];
-    const uint4* kr = reinterpret_cast<const uint4*>(c.kc + (c.slot0 + (valid ? t : t0)) * rowel + h * kHD);
-#pragma unroll
-    for (int v = 0; v < kHD / 8; ++v) kv[v] = __ldcg(kr + v);
-    uint2 vv[kAttChunk];
-    const uint16_t* vbase = c.vc + (c.slot0 + t0) * rowel + h * kHD + 4 * lane;
-#pragma unroll
-    for (int tt = 0; tt < kAttChunk; ++tt)
-      vv[tt] = tt < nvalid ? __ldcg(reinterpret_cast<const uint2*>(vbase + (int64_t)tt * rowel))
-                           : make_uint2(0u, 0u);
+  // 3) one chunk of 32 keys per warp -> its partial in shared memory
+  if (have) {
     float s[2] = {-__int_as_float(0x7f800000), -__int_as_float(0x7f800000)};
     if (valid) {
       const uint4* q0 = reinterpret_cast<const uint4*>(sm.qs[0]);
@@ -192,8 +232,9 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
       const float p0 = __shfl_sync(0xffffffffu, p[0], tt);
       const float p1 = __shfl_sync(0xffffffffu, p[1], tt);
       if (tt < nvalid) {
-        const float v0 = h2f((uint16_t)(vv[tt].x & 0xffffu)), v1 = h2f((uint16_t)(vv[tt].x >> 16));
-        const float v2 = h2f((uint16_t)(vv[tt].y & 0xffffu)), v3 = h2f((uint16_t)(vv[tt].y >> 16));
+        const uint2 vt = tt == tp ? nv : vv[tt];
+        const float v0 = h2f((uint16_t)(vt.x & 0xffffu)), v1 = h2f((uint16_t)(vt.x >> 16));
+        const float v2 = h2f((uint16_t)(vt.y & 0xffffu)), v3 = h2f((uint16_t)(vt.y >> 16));
         o0[0] = __fmaf_rn(p0, v0, o0[0]);
         o0[1] = __fmaf_rn(p0, v1, o0[1]);
         o0[2] = __fmaf_rn(p0, v2, o0[2]);
@@ -204,7 +245,7 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
         o1[3] = __fmaf_rn(p1, v3, o1[3]);
       }
     }
-    AttnPartial* gp = c.part + ((int64_t)h * c.max_chunks + ci) * 2;
+    AttnPartial* gp = sm.part[warp];
     if (lane == 0) {
       gp[0].m = m[0];
       gp[0].l = l[0];
@@ -214,31 +255,66 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
     *reinterpret_cast<float4*>(&gp[0].o[4 * lane]) = make_float4(o0[0], o0[1], o0[2], o0[3]);
     *reinterpret_cast<float4*>(&gp[1].o[4 * lane]) = make_float4(o1[0], o1[1], o1[2], o1[3]);
   }
-  __threadfence();
   consumer_sync();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(c.counters + h, 1u);
-    sm.last = (prev == (unsigned)(ngroups - 1));
-    if (sm.last) c.counters[h] = 0u;
-  }
-  consumer_sync();
-  if (!sm.last) return;
-  __threadfence();
-  // 4) last group of head h: fold all chunk partials left to right
+
+  // 4) fold this group's chunks left to right (warps 0, 1: q heads 2h, 2h+1)
+  float m, l, o[4];
+  const int hh = warp;
   if (warp < 2) {
-    const int hh = warp;
+    const int ng = nch - g * kAttSplitChunks < kAttSplitChunks ? nch - g * kAttSplitChunks
+                                                               : kAttSplitChunks;
+    fold_smem(sm, ng, hh, lane, m, l, o);
+  }
+  if (ngroups > 1) {
+    // 5) publish the group partial; the CTA that finishes last for head h
+    //    folds the group partials left to right
+    AttnPartial* gpart = c.part + ((int64_t)h * c.max_chunks + g) * 2;
+    if (warp < 2) {
+      if (lane == 0) {
+        gpart[hh].m = m;
+        gpart[hh].l = l;
+      }
+      *reinterpret_cast<float4*>(&gpart[hh].o[4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+    consumer_sync();  // the partial stores precede thread 0's release
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const unsigned prev = atomicAdd(c.counters + h, 1u);
+      sm.last = (prev == (unsigned)(ngroups - 1));
+      if (sm.last) c.counters[h] = 0u;
+      __threadfence();
+    }
+    consumer_sync();
+    if (!sm.last || warp >= 2) return;
     const AttnPartial* base = c.part + (int64_t)h * c.max_chunks * 2 + hh;
-    float m = __ldcg(&base->m), l = __ldcg(&base->l), o[4];
+    m = __ldcg(&base->m);
+    l = __ldcg(&base->l);
     {
       const float4 t4 = __ldcg(reinterpret_cast<const float4*>(&base->o[4 * lane]));
       o[0] = t4.x, o[1] = t4.y, o[2] = t4.z, o[3] = t4.w;
     }
-    for (int k = 1; k < nch; ++k) {
-      const AttnPartial* q = base + (int64_t)k * 2;
-      const float4 t4 = __ldcg(reinterpret_cast<const float4*>(&q->o[4 * lane]));
-      const float ob[4] = {t4.x, t4.y, t4.z, t4.w};
-      att_merge(m, l, o, __ldcg(&q->m), __ldcg(&q->l), ob);
+    for (int k0 = 1; k0 < ngroups; k0 += 8) {  // the loads of eight groups before their merges
+      float4 ob4[8];
+      float mb[8], lb[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (k0 + u < ngroups) {
+          const AttnPartial* q = base + (int64_t)(k0 + u) * 2;
+          ob4[u] = __ldcg(reinterpret_cast<const float4*>(&q->o[4 * lane]));
+          mb[u] = __ldcg(&q->m);
+          lb[u] = __ldcg(&q->l);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (k0 + u < ngroups) {
+          const float ob[4] = {ob4[u].x, ob4[u].y, ob4[u].z, ob4[u].w};
+          att_merge(m, l, o, mb[u], lb[u], ob);
+        }
+      }
     }
+  }
+  if (warp < 2) {
     uint16_t* out = c.out + (2 * h + hh) * kHD + 4 * lane;
     uint2 pk;
     pk.x = (uint32_t)f2h(__fdiv_rn(o[0], l)) | ((uint32_t)f2h(__fdiv_rn(o[1], l)) << 16);
@@ -248,7 +324,8 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
 }
 
 // Standalone launch: grid (8 kv heads, max groups, sequences), 256 threads.
-__global__ void __launch_bounds__(256) k_attn_decode(const __grid_constant__ AttnArgs a) {
+template <bool EARLY>
+__global__ void __launch_bounds__(256, EARLY ? 1 : 2) k_attn_decode(const __grid_constant__ AttnArgs a) {
   __shared__ __align__(16) AttnSmem sm;
   const int h = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   pdl_launch_dependents();
@@ -275,7 +352,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const __grid_constant__ Att
   c.part = a.part + (int64_t)b * kNKV * a.max_chunks * 2;
   c.counters = a.counters + (int64_t)b * kNKV;
   c.max_chunks = a.max_chunks;
-  attn_group(c, h, g, sm);
+  attn_group<EARLY>(c, h, g, sm);
 }
 
 }  // namespace q3

@@ -34,8 +34,9 @@
 namespace q3 {
 
 constexpr int kBMaxBatch = 64;
-constexpr int kBgThreads = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 dequant + epilogue
-constexpr int kBgRawStages = 2;
+constexpr int kBgDqWarps = 8;                     // dequantising warps (one Q8_0 block each)
+constexpr int kBgThreads = 64 + 32 * kBgDqWarps;  // warp 0 TMA, warp 1 MMA, warps 2-9 dequant
+constexpr int kBvThreads = 192;                   // vocab: warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kBgSubStages = 4;
 constexpr uint32_t kBgRawBytes = 128u * 272u;  // 128 rows x 8 Q8_0 blocks
 constexpr uint32_t kBgAtomA = 128u * 128u;     // 128 rows x 64 f16, SWIZZLE_128B
@@ -67,6 +68,7 @@ struct BGemmArgs {
   int wseg_rows[3];      // output rows served by wmap[i] (segments concatenated)
   int64_t wrow0[3];      // first weight row (layer * N) in each map
   int K;
+  int kc;                // 256-wide K chunks per CTA (1 or 2); gridDim.y = K / 256 / kc
   int B;                 // live sequences (<= npad)
   int ldy;               // output row stride (elements) per sequence
   uint16_t* y;           // [npad][ldy] f16
@@ -76,73 +78,129 @@ struct BGemmArgs {
   int tag;               // launch tag recorded with a timeout
 };
 
-// K=64 slices in flight between the dequantising warps and the MMA thread;
-// two accumulators (gate + up) leave room for two.
+// Weight stages (dequantised 64-wide K slices) between the dequantising warps
+// and the MMA thread; two accumulators (gate + up) leave room for two.
 __host__ __device__ constexpr int bgemm_substages(int naccum) { return naccum == 2 ? 2 : 4; }
+constexpr int kBgMaxKc = 2;       // chunks per CTA: all of its activations stay resident
+constexpr int kBgMaxSplits = 8;   // CTAs per tile = one portable cluster
 
-__host__ __device__ constexpr size_t bgemm_smem_bytes(int npad, int naccum) {
+// Dynamic shared memory: weight stages (reused for the f32 partials), every
+// activation slice of the CTA's K range, and one raw stage per chunk.
+__host__ __device__ constexpr size_t bgemm_smem_bytes(int npad, int naccum, int kc) {
   return 1024 /*align slack*/ + (size_t)naccum * bgemm_substages(naccum) * kBgAtomA +
-         (size_t)bgemm_substages(naccum) * npad * 128 +
-         (size_t)kBgRawStages * naccum * kBgRawBytes;
+         (size_t)kc * 4 * npad * 128 + (size_t)kc * naccum * kBgRawBytes;
 }
 
-// Dequantise one 64-wide K-slice (two Q8_0 blocks at shared byte address
-// `raw`) of row r into the SWIZZLE_128B atom at `atom`.
-__device__ __forceinline__ void dequant_slice(uint32_t raw, uint32_t atom, uint32_t r) {
+__device__ __forceinline__ void lds128(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c,
+                                       uint32_t& d) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr));
+}
+
+// Dequantise Q8_0 block BLK (0/1) of 64-wide slice J of weight row r into
+// chunks 4*BLK .. 4*BLK+3 of row r of the SWIZZLE_128B atom, as f16(scale*q)
+// (model/qwen3_full.mlir:564-579).  The block's 34 bytes sit at stage offset
+// r*272 + 68J + 34BLK; three 16-byte loads from the 16-byte boundary D bytes
+// below cover them, and with rows 272 = 17*16 bytes apart the 8 rows of a
+// quarter warp fall on distinct bank groups.
+template <int J, int BLK>
+__device__ __forceinline__ void dequant_block(uint32_t stage, uint32_t atom, uint32_t r) {
+  constexpr int D = (4 * J + 2 * BLK) & 15;
+  const uint32_t a0 = stage + r * 272u + (uint32_t)(68 * J + 34 * BLK - D);
+  uint32_t w[12];
+  lds128(a0, w[0], w[1], w[2], w[3]);
+  lds128(a0 + 16, w[4], w[5], w[6], w[7]);
+  lds128(a0 + 32, w[8], w[9], w[10], w[11]);
+  const uint32_t sc = (D & 2) ? (w[D >> 2] >> 16) : (w[D >> 2] & 0xffffu);
+  const uint32_t s2 = sc | (sc << 16);
+  constexpr int Q = (D + 2) >> 2;  // word holding the first q byte
+  uint32_t q[8];
 #pragma unroll
-  for (int blk = 0; blk < 2; ++blk) {
-    const Q8BlockWords bw = q8_load_block(raw + 34u * blk);
-    const uint32_t s2 = bw.scale16 | (bw.scale16 << 16);
+  for (int i = 0; i < 8; ++i)
+    q[i] = ((D + 2) & 3) == 0 ? w[Q + i] : __byte_perm(w[Q + i], w[Q + i + 1], 0x5432);
 #pragma unroll
-    for (int w = 0; w < 8; w += 2) {
-      uint32_t a01, a23, b01, b23;
-      q8x4_to_h2(bw.q[w], a01, a23);
-      q8x4_to_h2(bw.q[w + 1], b01, b23);
-      uint32_t o0, o1, o2, o3;
-      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o0) : "r"(a01), "r"(s2));
-      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o1) : "r"(a23), "r"(s2));
-      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o2) : "r"(b01), "r"(s2));
-      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o3) : "r"(b23), "r"(s2));
-      const uint32_t c = (uint32_t)(blk * 4 + w / 2);
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(atom + sw128_chunk_offset(r, c)),
-                   "r"(o0), "r"(o1), "r"(o2), "r"(o3)
-                   : "memory");
-    }
+  for (int c = 0; c < 4; ++c) {
+    uint32_t a01, a23, b01, b23;
+    q8x4_to_h2(q[2 * c], a01, a23);
+    q8x4_to_h2(q[2 * c + 1], b01, b23);
+    uint32_t o0, o1, o2, o3;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o0) : "r"(a01), "r"(s2));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o1) : "r"(a23), "r"(s2));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o2) : "r"(b01), "r"(s2));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o3) : "r"(b23), "r"(s2));
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                     atom + sw128_chunk_offset(r, (uint32_t)(4 * BLK + c))),
+                 "r"(o0), "r"(o1), "r"(o2), "r"(o3)
+                 : "memory");
   }
 }
 
-// Batched Q8_0 GEMM.  Grid: one CTA per 128 output rows (kBgSwiglu: per 128
-// gate rows, with their 128 up rows).  NPAD = batch padded to 16.
+template <int J>
+__device__ __forceinline__ void dequant_block_j(int blk, uint32_t stage, uint32_t atom, uint32_t r) {
+  if (blk == 0)
+    dequant_block<J, 0>(stage, atom, r);
+  else
+    dequant_block<J, 1>(stage, atom, r);
+}
+
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// Batched Q8_0 GEMM.  Grid (row tiles, S splits), clusters of the S CTAs of
+// a tile: CTA (t, s) owns output rows 128t .. 128t+127 (kBgSwiglu: those gate
+// rows and their up rows) over 256-wide K chunks [s*kc, (s+1)*kc).  With
+// S = 1 the CTA applies the epilogue straight from TMEM.  With S > 1 each CTA
+// leaves its f32 partial in its own shared memory; after a cluster barrier
+// CTA s reduces items [s*n/S, (s+1)*n/S) of the tile's 128 x NPAD outputs,
+// reading the S partials over distributed shared memory in split order (the
+// same bits whatever the timing), and applies the epilogue.  Every activation
+// slice of the CTA's K range is loaded once, and the weight copies and their
+// dequantisation start before the wait on the previous kernel (weights do
+// not depend on it).  NPAD = batch padded to 16.
 template <int NPAD, int MODE>
 __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constant__ BGemmArgs a) {
   constexpr int NACC = MODE == kBgSwiglu ? 2 : 1;   // accumulators (gate, up)
   constexpr int SUB = bgemm_substages(NACC);
   constexpr uint32_t TCOLS = NPAD * NACC <= 32 ? 32 : NPAD * NACC <= 64 ? 64 : 128;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t raw_full[kBgRawStages], raw_empty[kBgRawStages];
-  __shared__ __align__(8) uint64_t x_full[kBgSubStages], a_full[kBgSubStages], ax_empty[kBgSubStages];
-  __shared__ __align__(8) uint64_t acc_full;
+  __shared__ __align__(8) uint64_t raw_full[kBgMaxKc], x_full, acc_full;
+  __shared__ __align__(8) uint64_t a_full[kBgSubStages], a_empty[kBgSubStages];
   __shared__ uint32_t tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nchunk = a.kc;
+  const int nsub = nchunk * 4;
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t sA = base;                                        // [NACC][4][16 KB]
-  const uint32_t sX = sA + NACC * SUB * kBgAtomA;         // [4][NPAD*128]
-  const uint32_t sR = sX + SUB * NPAD * 128;              // [2][NACC][34816]
-  const int nsub = a.K / 64;
-  const int nchunk = a.K / 256;
-  const int n0 = blockIdx.x * 128;
+  const uint32_t sA = base;                                // [NACC][SUB][16 KB]; partials later
+  const uint32_t sX = sA + NACC * SUB * kBgAtomA;          // [nsub][NPAD*128]
+  const uint32_t sR = sX + nsub * NPAD * 128;              // [nchunk][NACC][34816]
+  uint8_t* const gbase = smem_raw + (base - smem_u32(smem_raw));
+  const int splits = (int)gridDim.y;
+  const int cbase = (int)blockIdx.y * nchunk;              // first 256-wide chunk of this CTA
+  const int tile = blockIdx.x, n0 = tile * 128;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kBgRawStages; ++i) {
-      mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 4);
-    }
+    for (int i = 0; i < kBgMaxKc; ++i) mbar_init(&raw_full[i], 1);
     for (int i = 0; i < SUB; ++i) {
-      mbar_init(&x_full[i], 1);
-      mbar_init(&a_full[i], 4);
-      mbar_init(&ax_empty[i], 1);
+      mbar_init(&a_full[i], kBgDqWarps);
+      mbar_init(&a_empty[i], 1);
     }
+    mbar_init(&x_full, 1);
     mbar_init(&acc_full, 1);
     fence_mbar_init();
   }
@@ -171,111 +229,167 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       const int y0 = (int)(a.wrow0[seg] + row);
       prefetch_tmap(wm);
       prefetch_tmap(&a.xmap);
-      pdl_wait();  // activations come from the previous kernel
-      int c_done = 0, i_done = 0;  // loads issued
-      bool ok = true;
-      for (int c = 0; ok && c < nchunk; ++c) {
-        const int rs = c % kBgRawStages;
-        if (c >= kBgRawStages &&
-            !Q3_BWAIT(&raw_empty[rs], ((c / kBgRawStages) - 1) & 1, kErrTimeoutEmpty, 1))
-          break;
-        mbar_expect_tx(&raw_full[rs], NACC * kBgRawBytes);
+      // weights do not depend on the previous kernel: start them first
+      for (int c = 0; c < nchunk; ++c) {
+        mbar_expect_tx(&raw_full[c], NACC * kBgRawBytes);
         for (int acc = 0; acc < NACC; ++acc)
-          tma_load_2d(smem_raw + (sR - smem_u32(smem_raw)) + (rs * NACC + acc) * kBgRawBytes, wm,
-                      c * 136, y0 + (int)(acc * a.up_rows), &raw_full[rs]);
-        c_done = c + 1;
-        for (int j = 0; j < 4; ++j) {
-          const int i = c * 4 + j, ss = i % SUB;
-          if (i >= SUB &&
-              !Q3_BWAIT(&ax_empty[ss], ((i / SUB) - 1) & 1, kErrTimeoutEmpty, 2)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(&x_full[ss], NPAD * 128);
-          tma_load_2d(smem_raw + (sX - smem_u32(smem_raw)) + ss * NPAD * 128, &a.xmap, i * 64, 0,
-                      &x_full[ss]);
-          i_done = i + 1;
-        }
+          tma_load_2d(gbase + (sR - base) + (c * NACC + acc) * kBgRawBytes, wm, (cbase + c) * 136,
+                      y0 + (int)(acc * a.up_rows), &raw_full[c]);
       }
-      // the CTA may not exit before every issued copy has landed
-      for (int st = 0; st < kBgRawStages && st < c_done; ++st)
-        Q3_BWAIT(&raw_full[st], ((c_done - 1 - st) / kBgRawStages) & 1, kErrTimeoutFull, 3);
-      for (int st = 0; st < SUB && st < i_done; ++st)
-        Q3_BWAIT(&x_full[st], ((i_done - 1 - st) / SUB) & 1, kErrTimeoutFull, 4);
+      pdl_wait();  // activations come from the previous kernel
+      mbar_expect_tx(&x_full, (uint32_t)(nsub * NPAD * 128));
+      for (int i = 0; i < nsub; ++i)
+        tma_load_2d(gbase + (sX - base) + i * NPAD * 128, &a.xmap, (cbase * 4 + i) * 64, 0, &x_full);
+      // the CTA may not exit before every copy has landed
+      for (int c = 0; c < nchunk; ++c) Q3_BWAIT(&raw_full[c], 0, kErrTimeoutFull, 3);
+      Q3_BWAIT(&x_full, 0, kErrTimeoutFull, 4);
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      for (int i = 0; i < nsub; ++i) {
+      bool ok = Q3_BWAIT(&x_full, 0, kErrTimeoutFull, 6);
+      for (int i = 0; ok && i < nsub; ++i) {
         const int ss = i % SUB;
-        const uint32_t par = (i / SUB) & 1;
-        if (!Q3_BWAIT(&a_full[ss], par, kErrTimeoutFull, 5)) break;
-        if (!Q3_BWAIT(&x_full[ss], par, kErrTimeoutFull, 6)) break;
+        if (!Q3_BWAIT(&a_full[ss], (i / SUB) & 1, kErrTimeoutFull, 5)) break;
         tc_fence_after();
         for (int acc = 0; acc < NACC; ++acc) {
           const uint32_t aa = sA + (acc * SUB + ss) * kBgAtomA;
-          const uint32_t xx = sX + ss * NPAD * 128;
+          const uint32_t xx = sX + i * NPAD * 128;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_f16(tmem + acc * NPAD, sw128_desc(aa + 32 * kk), sw128_desc(xx + 32 * kk), idesc,
                      (i | kk) != 0);
         }
-        umma_commit(&ax_empty[ss]);
+        umma_commit(&a_empty[ss]);
       }
       umma_commit(&acc_full);
       Q3_BWAIT(&acc_full, 0, kErrTimeoutFull, 7);  // no MMA in flight at dealloc
     }
   } else {
-    // ------------------------------------------------ dequant, then epilogue
-    const uint32_t r = 32u * (warp & 3) + lane;  // this thread's weight row / TMEM lane
-    pdl_wait();  // the epilogue reads the previous kernels' residual stream
+    // ------------------------------------------------ dequant (8 warps)
+    const uint32_t r = 32u * (uint32_t)(warp & 3) + lane;  // weight row = TMEM lane
+    const int blk = (warp - 2) >> 2;                       // Q8_0 block of each 64-wide slice
     for (int c = 0; c < nchunk; ++c) {
-      const int rs = c % kBgRawStages;
-      if (!Q3_BWAIT(&raw_full[rs], (c / kBgRawStages) & 1, kErrTimeoutFull, 8)) break;
+      if (!Q3_BWAIT(&raw_full[c], 0, kErrTimeoutFull, 8)) break;
+      bool ok = true;
+#pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int i = c * 4 + j, ss = i % SUB;
-        if (i >= SUB &&
-            !Q3_BWAIT(&ax_empty[ss], ((i / SUB) - 1) & 1, kErrTimeoutEmpty, 9))
+        if (i >= SUB && !Q3_BWAIT(&a_empty[ss], ((i / SUB) - 1) & 1, kErrTimeoutEmpty, 9)) {
+          ok = false;
           break;
-        for (int acc = 0; acc < NACC; ++acc)
-          dequant_slice(sR + (rs * NACC + acc) * kBgRawBytes + r * 272u + 68u * j,
-                        sA + (acc * SUB + ss) * kBgAtomA, r);
+        }
+        for (int acc = 0; acc < NACC; ++acc) {
+          const uint32_t stage = sR + (c * NACC + acc) * kBgRawBytes;
+          const uint32_t atom = sA + (acc * SUB + ss) * kBgAtomA;
+          if (j == 0) dequant_block_j<0>(blk, stage, atom, r);
+          if (j == 1) dequant_block_j<1>(blk, stage, atom, r);
+          if (j == 2) dequant_block_j<2>(blk, stage, atom, r);
+          if (j == 3) dequant_block_j<3>(blk, stage, atom, r);
+        }
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[ss]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&raw_empty[rs]);
+      if (!ok) break;
     }
-    // epilogue
-    if (Q3_BWAIT(&acc_full, 0, kErrTimeoutFull, 10)) {
+    // ------------------------------------------------ accumulators out of TMEM (warps 2-5)
+    if (warp < 6) {
+      const bool have = Q3_BWAIT(&acc_full, 0, kErrTimeoutFull, 10);
       tc_fence_after();
-      const uint32_t lane_base = (32u * (warp & 3)) << 16;
-      const int n = n0 + (int)r;
+      const uint32_t lane_base = (32u * (uint32_t)(warp & 3)) << 16;
+      if (have && splits == 1) {
+        pdl_wait();  // reads the residual stream / writes buffers of earlier kernels
+        const int n = n0 + (int)r;
 #pragma unroll
-      for (int col0 = 0; col0 < NPAD; col0 += 16) {
-        uint32_t v[16], u[16];
-        tmem_ld16(tmem + lane_base + col0, v);
-        if (MODE == kBgSwiglu) tmem_ld16(tmem + lane_base + NPAD + col0, u);
-        tmem_wait_ld();
+        for (int col0 = 0; col0 < NPAD; col0 += 16) {
+          uint32_t v[16], u[16];
+          tmem_ld16(tmem + lane_base + col0, v);
+          if (MODE == kBgSwiglu) tmem_ld16(tmem + lane_base + NPAD + col0, u);
+          tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int b = col0 + j;
-          if (b < a.B) {
-            const float d = __uint_as_float(v[j]);
-            uint16_t out;
-            if (MODE == kBgSwiglu) {
-              out = swiglu_h(f2h(d), f2h(__uint_as_float(u[j])));
-            } else if (MODE == kBgResid) {
-              out = f2h(__fadd_rn(h2f(a.r[(int64_t)b * a.ldy + n]), h2f(f2h(d))));
-            } else {
-              out = f2h(d);
+          for (int j = 0; j < 16; ++j) {
+            const int b = col0 + j;
+            if (b < a.B) {
+              const float g = __uint_as_float(v[j]);
+              uint16_t out;
+              if (MODE == kBgSwiglu)
+                out = swiglu_h(f2h(g), f2h(__uint_as_float(u[j])));
+              else if (MODE == kBgResid)
+                out = f2h(__fadd_rn(h2f(a.r[(int64_t)b * a.ldy + n]), h2f(f2h(g))));
+              else
+                out = f2h(g);
+              a.y[(int64_t)b * a.ldy + n] = out;
             }
-            a.y[(int64_t)b * a.ldy + n] = out;
+          }
+        }
+      } else if (splits > 1) {
+        // partial [acc][b][row] f32 over the (now idle) weight stages; rows
+        // contiguous so the remote reads of consecutive rows hit distinct banks
+#pragma unroll
+        for (int acc = 0; acc < NACC; ++acc) {
+#pragma unroll
+          for (int col0 = 0; col0 < NPAD; col0 += 16) {
+            uint32_t v[16];
+            if (have) {
+              tmem_ld16(tmem + lane_base + acc * NPAD + col0, v);
+              tmem_wait_ld();
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = 0u;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              asm volatile("st.shared.b32 [%0], %1;" ::"r"(
+                               sA + (uint32_t)(((acc * NPAD + col0 + j) * 128 + (int)r) * 4)),
+                           "r"(v[j])
+                           : "memory");
           }
         }
       }
     }
+  }
+  if (splits > 1) {
+    // ------------------------------------------------ cluster reduction
+    __syncwarp();
+    cluster_sync_all();  // every CTA's partial is in its shared memory
+    if (warp >= 2) {
+      pdl_wait();  // reads the residual stream / writes buffers of earlier kernels
+      const int t = threadIdx.x - 64;                      // 0 .. 255
+      const int total = 128 * NPAD;
+      const int per = (total + splits - 1) / splits;
+      const int i0 = (int)cluster_rank() * per;
+      const int i1 = i0 + per < total ? i0 + per : total;
+      for (int i = i0 + t; i < i1; i += 32 * kBgDqWarps) {
+        const int b = i >> 7, row = i & 127;
+        if (b >= a.B) continue;
+        float sum[NACC];
+#pragma unroll
+        for (int acc = 0; acc < NACC; ++acc) {
+          float v[kBgMaxSplits];
+          const uint32_t off = sA + (uint32_t)(((acc * NPAD + b) * 128 + row) * 4);
+#pragma unroll
+          for (int sp = 0; sp < kBgMaxSplits; ++sp)
+            v[sp] = sp < splits ? ld_dsmem_f32(off, (uint32_t)sp) : 0.0f;
+          float s0 = v[0];
+#pragma unroll
+          for (int sp = 1; sp < kBgMaxSplits; ++sp)
+            if (sp < splits) s0 = __fadd_rn(s0, v[sp]);
+          sum[acc] = s0;
+        }
+        const int n = n0 + row;
+        uint16_t out;
+        if (MODE == kBgSwiglu)
+          out = swiglu_h(f2h(sum[0]), f2h(sum[NACC - 1]));
+        else if (MODE == kBgResid)
+          out = f2h(__fadd_rn(h2f(a.r[(int64_t)b * a.ldy + n]), h2f(f2h(sum[0]))));
+        else
+          out = f2h(sum[0]);
+        a.y[(int64_t)b * a.ldy + n] = out;
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // no CTA leaves while another still reads its shared memory
   }
   tc_fence_before();
   __syncthreads();
@@ -358,7 +472,7 @@ __host__ __device__ constexpr size_t bvocab_smem_bytes(int npad) {
 }
 
 template <int NPAD>
-__global__ void __launch_bounds__(kBgThreads, 1) k_bvocab(const __grid_constant__ BVocabArgs a) {
+__global__ void __launch_bounds__(kBvThreads, 1) k_bvocab(const __grid_constant__ BVocabArgs a) {
   constexpr uint32_t TCOLS = 2 * NPAD <= 32 ? 32 : 2 * NPAD <= 64 ? 64 : 128;  // double buffer
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t x_full, a_full[kBvAStages], a_empty[kBvAStages];

@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_decode_persistent(const __g
         c.max_chunks = a.max_chunks;
         const int ntask = kNKV * attn_ngroups(pos);
         trace_mark(a, s, p, 2);
-        for (int j = cta; j < ntask; j += G) attn_group(c, j % kNKV, j / kNKV, asm_);
+        for (int j = cta; j < ntask; j += G) attn_group<false>(c, j % kNKV, j / kNKV, asm_);
       } else if (ph == PH_O) {
         uint32_t xr[2][16];
         load_x_blocks_cg<2>(a.attn, lane, xr);

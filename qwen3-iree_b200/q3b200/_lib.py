@@ -94,7 +94,7 @@ SIGNATURES = {
     "q3_model_kernel_launches": [P, PI64],
     "q3_model_trace_steps": [P, I64, I64, P, I64, ctypes.POINTER(ctypes.c_int),
                              ctypes.POINTER(ctypes.c_int)],
-    "q3_bgemm_q8": [P, I64, I64, P, P, P, I, I, I, I, P],
+    "q3_bgemm_q8": [P, I64, I64, P, P, P, I, I, I, I, I, P],
     "q3_bvocab_workspace_bytes": [],
     "q3_bvocab_argmax": [P, I, P, I, P, P, P, P],
     "q3_batch_create": [ctypes.POINTER(Weights), I, I64, P, PP],

@@ -29,33 +29,41 @@ def _w16(O, raw, N, K):
     return O.dequant_q8_0(raw, N * K).reshape(N, K).astype(np.float16)
 
 
-def _bgemm(gpu, w, w_rows, row0, x, N, K, mode, r=None):
+def _bgemm(gpu, w, w_rows, row0, x, N, K, mode, r=None, ksplit=1, calls=1):
     B = x.shape[0]
+    L = gpu.lib()
     dw, dx = _up(gpu, w), _up(gpu, x)
     dy = gpu.DeviceArray((B, N), np.float16)
-    dy.fill_bytes(0xFF)
     dr = _up(gpu, r) if r is not None else None
-    rc = gpu.lib().q3_bgemm_q8(dw.ptr, w_rows, row0, dx.ptr, dy.ptr, dr.ptr if dr else None, B,
-                               N, K, mode, None)
-    assert rc == 0, gpu.lib().q3_last_error()
-    gpu.synchronize(None)
-    return dy.download()
+    outs = []
+    for _ in range(calls):  # split sums are in a fixed order: repeat calls agree bit for bit
+        dy.fill_bytes(0xFF)
+        rc = L.q3_bgemm_q8(dw.ptr, w_rows, row0, dx.ptr, dy.ptr, dr.ptr if dr else None, B, N, K,
+                           mode, ksplit, None)
+        assert rc == 0, L.q3_last_error()
+        gpu.synchronize(None)
+        outs.append(dy.download())
+    for o in outs[1:]:
+        assert np.array_equal(o.view(np.uint16), outs[0].view(np.uint16))
+    return outs[0]
 
 
 @pytest.mark.parametrize("B", [1, 16, 17, 32, 64])
-@pytest.mark.parametrize("N,K", [(2048, 1024), (1024, 2048), (1024, 3072), (128, 256)])
-def test_bgemm_plain(gpu, O, B, N, K):
+@pytest.mark.parametrize("N,K,ksplit", [(2048, 1024, 2), (2048, 1024, 4), (1024, 2048, 8),
+                                        (1024, 2048, 4), (1024, 3072, 6), (128, 256, 1),
+                                        (256, 512, 1), (1024, 3072, 0)])
+def test_bgemm_plain(gpu, O, B, N, K, ksplit):
     rng = np.random.default_rng(B * 131 + N + K)
     w = _q8(O, rng, N, K)
     x = rng.standard_normal((B, K)).astype(np.float16)
-    y = _bgemm(gpu, w, N, 0, x, N, K, 0)
+    y = _bgemm(gpu, w, N, 0, x, N, K, 0, ksplit=ksplit, calls=2 if ksplit > 1 else 1)
     ref = (x.astype(np.float64) @ _w16(O, w, N, K).astype(np.float64).T).astype(np.float16)
     assert np.isfinite(y).all()
     assert rel_l2(y, ref) <= TOL
 
 
-@pytest.mark.parametrize("B", [16, 33])
-def test_bgemm_row_offset_resid(gpu, O, B):
+@pytest.mark.parametrize("B,ksplit", [(16, 4), (33, 8), (64, 4), (1, 8)])
+def test_bgemm_row_offset_resid(gpu, O, B, ksplit):
     """Layer 1 of a two-layer stack (row0 = N), residual epilogue
     y = f16(r + f16(W x)) (model/qwen3_full.mlir:801-805)."""
     N, K = 1024, 2048
@@ -63,22 +71,22 @@ def test_bgemm_row_offset_resid(gpu, O, B):
     w = _q8(O, rng, 2 * N, K)
     x = rng.standard_normal((B, K)).astype(np.float16)
     r = rng.standard_normal((B, N)).astype(np.float16)
-    y = _bgemm(gpu, w, 2 * N, N, x, N, K, 1, r)
+    y = _bgemm(gpu, w, 2 * N, N, x, N, K, 1, r, ksplit=ksplit)
     w16 = _w16(O, w, 2 * N, K)[N:]
     acc = (x.astype(np.float64) @ w16.astype(np.float64).T).astype(np.float16)
     ref = (r.astype(np.float32) + acc.astype(np.float32)).astype(np.float16)
     assert rel_l2(y, ref) <= TOL
 
 
-@pytest.mark.parametrize("B", [16, 48, 64])
-def test_bgemm_swiglu(gpu, O, B):
+@pytest.mark.parametrize("B,ksplit", [(16, 4), (48, 4), (64, 4), (32, 0)])
+def test_bgemm_swiglu(gpu, O, B, ksplit):
     """gate rows [0, 3072), up rows [3072, 6144) of one layer's gate_up;
     SwiGLU with f16 rounding after each op (model/qwen3_full.mlir:829-839)."""
     N, K = 3072, 1024
     rng = np.random.default_rng(100 + B)
     w = _q8(O, rng, 2 * N, K, std=0.05)
     x = rng.standard_normal((B, K)).astype(np.float16)
-    y = _bgemm(gpu, w, 2 * N, 0, x, N, K, 2)
+    y = _bgemm(gpu, w, 2 * N, 0, x, N, K, 2, ksplit=ksplit)
     gu = (x.astype(np.float64) @ _w16(O, w, 2 * N, K).astype(np.float64).T).astype(np.float16)
     ref = np.stack([O.swiglu(gu[b]) for b in range(B)])
     assert rel_l2(y, ref) <= TOL
@@ -86,15 +94,20 @@ def test_bgemm_swiglu(gpu, O, B):
 
 def test_bgemm_rejects_bad_shapes(gpu):
     L = gpu.lib()
-    assert L.q3_bgemm_q8(None, 128, 0, None, None, None, 1, 128, 256, 0, None) != 0
+    assert L.q3_bgemm_q8(None, 128, 0, None, None, None, 1, 128, 256, 0, 1, None) != 0
     # B = 0 and B = 65 are outside [1, 64]; K not a multiple of 256; rows past the matrix
     dummy = gpu.DeviceArray((1 << 16,), np.uint8)
     p = dummy.ptr
-    assert L.q3_bgemm_q8(p, 128, 0, p, p, None, 0, 128, 256, 0, None) == 1
-    assert L.q3_bgemm_q8(p, 128, 0, p, p, None, 65, 128, 256, 0, None) == 1
-    assert L.q3_bgemm_q8(p, 128, 0, p, p, None, 1, 128, 320, 0, None) == 1
-    assert L.q3_bgemm_q8(p, 128, 1, p, p, None, 1, 128, 256, 0, None) == 1
-    assert L.q3_bgemm_q8(p, 256, 0, p, p, None, 1, 128, 256, 1, None) == 1  # resid without r
+    assert L.q3_bgemm_q8(p, 128, 0, p, p, None, 0, 128, 256, 0, 1, None) == 1
+    assert L.q3_bgemm_q8(p, 128, 0, p, p, None, 65, 128, 256, 0, 1, None) == 1
+    assert L.q3_bgemm_q8(p, 128, 0, p, p, None, 1, 128, 320, 0, 1, None) == 1
+    assert L.q3_bgemm_q8(p, 128, 1, p, p, None, 1, 128, 256, 0, 1, None) == 1
+    assert L.q3_bgemm_q8(p, 256, 0, p, p, None, 1, 128, 256, 1, 1, None) == 1  # no r
+    # ksplit must divide K/256, fit a cluster of 8 and leave <= 2 chunks per CTA
+    assert L.q3_bgemm_q8(p, 128, 0, p, p, None, 1, 128, 768, 0, 2, None) == 1
+    assert L.q3_bgemm_q8(p, 128, 0, p, p, None, 1, 128, 3072, 0, 2, None) == 1
+    assert L.q3_bgemm_q8(p, 128, 0, p, p, None, 1, 128, 3072, 0, 12, None) == 1
+    assert L.q3_bgemm_q8(p, 256, 0, p, p, None, 1, 128, 1024, 2, 2, None) == 1  # SwiGLU: 1 chunk
 
 
 @pytest.mark.parametrize("B,N", [(1, 151936), (16, 8192), (20, 151936), (64, 151936)])
