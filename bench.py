@@ -495,7 +495,8 @@ def measure_batched(q3b200, dw, d: Dist, key: str, seed: int, peak: float, warmu
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["achieved_gbs"],
                          "peak": peak, "unit": "GB/s",
-                         "frac": kern[dom]["achieved_gbs"] / peak},
+                         "frac": kern[dom]["achieved_gbs"] / peak,
+                         "traffic": load_traffic().get(f"b{B}_{dom}")},
             "kernels": kern,
             "l2": "inputs larger than L2 (779 MB of weights + the KV caches every step)"}
 
