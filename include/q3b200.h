@@ -313,6 +313,19 @@ size_t q3_bvocab_workspace_bytes(void);
 int q3_bvocab_argmax(const void* w, int N, const void* xn, int B, void* logits, int64_t* tokens,
                      void* ws, void* stream);
 
+/* Decode attention of one layer for B sequences, the batched decoder's
+ * kernel (model/qwen3_full.mlir:591-748 minus the projections, per sequence):
+ * QK-RMSNorm + RoPE, the new K/V row written at slot layer*S + pos[b], GQA
+ * attention over slots 0..pos[b], streamed by tensor TMA in segments of 512
+ * keys.  qkv [B][4096] raw projections; caches [B][28*S][8][128] f16; pos
+ * DEVICE int64[B]; out [B][2048].  ws: q3_batch_attention_workspace_bytes(S,
+ * B) bytes zero-filled once.  Tolerance-level parity (rel-L2 <= 1e-3). */
+size_t q3_batch_attention_workspace_bytes(int64_t S, int B);
+int q3_batch_attention(const void* qkv, const void* q_norm, const void* k_norm,
+                       const float* rope_cos, const float* rope_sin, int64_t rope_rows,
+                       void* k_cache, void* v_cache, int layer, int64_t S, int B,
+                       const int64_t* pos, void* out, void* ws, void* stream);
+
 /* Batched decoder: caches of max_batch sequences x max_seq_len positions. */
 typedef struct q3_batch q3_batch;
 int q3_batch_create(const q3_weights* w, int max_batch, int64_t max_seq_len, void* stream,

@@ -1312,4 +1312,5 @@ extern "C" int q3_model_trace_steps(q3_model* m, int64_t steps, int64_t trace_st
 // batched decoder (tcgen05 projections and vocab head)
 // ---------------------------------------------------------------------------
 #include "q3_batch.cuh"
+#include "q3_battn.cuh"
 #include "q3_batch_host.inc"

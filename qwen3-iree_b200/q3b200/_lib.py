@@ -105,6 +105,8 @@ SIGNATURES = {
     "q3_batch_steps": [P, I64],
     "q3_batch_read": [P, P, P, ctypes.POINTER(ctypes.c_int)],
     "q3_batch_read_argmax": [P, P],
+    "q3_batch_attention_workspace_bytes": [I64, I],
+    "q3_batch_attention": [P, P, P, P, P, I64, P, P, I, I64, I, P, P, P, P],
     "q3_batch_profile_steps": [P, I64, P, P, I64, PI64],
     "q3_batch_kernel_launches": [P, PI64],
     "q3_strerror": [I],
@@ -117,6 +119,7 @@ _RESTYPE = {
     "q3_attention_workspace_bytes": SZ,
     "q3_model_stream": P,
     "q3_bvocab_workspace_bytes": SZ,
+    "q3_batch_attention_workspace_bytes": SZ,
     "q3_batch_stream": P,
 }
 

@@ -148,6 +148,50 @@ def test_bvocab_ties_pick_lowest_index(gpu):
     assert (dt.download() == 3).all()
 
 
+def test_batch_attention_vs_oracle(gpu, O):
+    """The batched attention kernel against the oracle's attention, one
+    sequence per position class: single chunk, chunk boundaries, one and
+    several 512-key segments.  The new K/V rows must be written bit for bit."""
+    L = gpu.lib()
+    S, layer = 1800, 3
+    pos = np.array([0, 31, 32, 511, 512, 1000, 1700], np.int64)
+    B = pos.size
+    rng = np.random.default_rng(21)
+    kc = np.zeros((B, 28 * S, 8, 128), np.float16)  # only this layer's slots are read
+    vc = np.zeros((B, 28 * S, 8, 128), np.float16)
+    kc[:, layer * S:(layer + 1) * S] = rng.standard_normal((B, S, 8, 128), np.float32)
+    vc[:, layer * S:(layer + 1) * S] = rng.standard_normal((B, S, 8, 128), np.float32)
+    qkv = rng.standard_normal((B, 4096)).astype(np.float16)
+    qg = (1 + 0.1 * rng.standard_normal(128)).astype(np.float16)
+    kg = (1 + 0.1 * rng.standard_normal(128)).astype(np.float16)
+    cos, sin = O.rope_table(S)
+    dk, dv = _up(gpu, kc), _up(gpu, vc)
+    dq, dqg, dkg = _up(gpu, qkv), _up(gpu, qg), _up(gpu, kg)
+    dcos, dsin = _up(gpu, cos.astype(np.float32)), _up(gpu, sin.astype(np.float32))
+    dpos, dout = _up(gpu, pos), gpu.DeviceArray((B, 2048), np.float16)
+    ws = gpu.DeviceArray((L.q3_batch_attention_workspace_bytes(S, B),), np.uint8, zero=True)
+    for _ in range(2):  # the workspace re-arms itself
+        rc = L.q3_batch_attention(dq.ptr, dqg.ptr, dkg.ptr, dcos.ptr, dsin.ptr, S, dk.ptr, dv.ptr,
+                                  layer, S, B, dpos.ptr, dout.ptr, ws.ptr, None)
+        assert rc == 0, L.q3_last_error()
+        gpu.synchronize(None)
+    out = dout.download()
+    kg_out, vg_out = dk.download(), dv.download()
+    for b in range(B):
+        p = int(pos[b])
+        qn = O.qk_norm_rope(qkv[b, :2048], qg, p)
+        kn = O.qk_norm_rope(qkv[b, 2048:3072], kg, p)
+        slot = layer * S + p
+        assert np.array_equal(kg_out[b, slot].reshape(-1).view(np.uint16), kn.view(np.uint16)), b
+        assert np.array_equal(vg_out[b, slot].reshape(-1).view(np.uint16),
+                              qkv[b, 3072:].view(np.uint16)), b
+        kref, vref = kc[b].copy(), vc[b].copy()
+        kref[slot] = kn.reshape(8, 128)
+        vref[slot] = qkv[b, 3072:].reshape(8, 128)
+        ref = O.attention(qn, kref, vref, layer * S, p + 1)
+        assert rel_l2(out[b], ref) <= TOL, (b, p, rel_l2(out[b], ref))
+
+
 # ------------------------------------------------------------------ decoder
 @pytest.fixture(scope="module")
 def bmodels(gpu, O, model_weights):
@@ -156,9 +200,17 @@ def bmodels(gpu, O, model_weights):
     return gpu.DeviceWeights(model_weights), O.Model(to_oracle_dict(model_weights))
 
 
-def test_batch_decoder_teacher_forced_vs_oracle(gpu, O, bmodels):
-    """18 sequences (padded to 32) with prompts of 2..7 tokens, 8 steps: every
-    step's argmax agrees with the oracle's greedy token for the same history."""
+def _f16_ulp(v: float) -> float:
+    return 2.0 ** (np.floor(np.log2(max(abs(v), 2.0 ** -14))) - 10)
+
+
+def test_batch_decoder_teacher_forced_vs_oracle(gpu, O, bmodels, capsys):
+    """18 sequences (padded to 32) with prompts of 2..7 tokens, 8 steps,
+    teacher-forced: every step's argmax equals the oracle's greedy token for
+    the same history, except at a near-tie of the oracle's own f16 logits
+    (top-2 gap <= 4 f16 ulps; the batched path accumulates in the tensor
+    core's order, so it is held to a tolerance, not to bit-identity).  Flips
+    are logged and must stay rare."""
     dw, om = bmodels
     S, B, T = 16, 18, 8
     rng = np.random.default_rng(11)
@@ -169,7 +221,7 @@ def test_batch_decoder_teacher_forced_vs_oracle(gpu, O, bmodels):
     toks, pos = bd.read()
     amax = bd.read_argmax()
     assert (pos == T).all()
-    flips = 0
+    flips = []
     for b in range(B):
         assert toks[b, :len(prompts[b])].tolist() == prompts[b]
         kc, vc = om.new_cache(S)
@@ -178,11 +230,14 @@ def test_batch_decoder_teacher_forced_vs_oracle(gpu, O, bmodels):
             got = int(amax[b, p + 1])
             if got != otok:
                 lf = ologits.astype(np.float32)
-                assert lf[otok] - lf[got] <= 4e-3 * max(1.0, abs(lf[otok])), (b, p, got, otok)
-                flips += 1
+                gap = lf[otok] - lf[got]
+                assert gap <= 4 * _f16_ulp(lf[otok]), (b, p, got, otok, gap)
+                flips.append((b, p, got, otok, float(gap)))
             if p + 1 >= len(prompts[b]):
                 assert toks[b, p + 1] == got  # generated tokens are the argmax
-    assert flips <= 2
+    with capsys.disabled():
+        print(f"\nteacher-forced near-tie flips: {len(flips)} of {B * T} steps {flips}")
+    assert len(flips) <= 0.05 * B * T
     bd.close()
 
 
