@@ -141,42 +141,46 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- distributed plumbing
 class Dist:
-    """torch.distributed over NCCL for the barrier and the max-over-ranks of the
-    timings only; the decode itself has no collective (replicas)."""
+    """torch.distributed for the barrier and the max/sum over ranks of the
+    timings only; the decode itself has no collective (replicas).  NCCL on the
+    GPU box; "gloo" (CPU tensors) for the multi-rank tests of this logic."""
 
-    def __init__(self):
+    def __init__(self, backend: str = "nccl"):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.torch = None
+        self.device = "cpu"
         if self.world > 1:
             import datetime
 
             import torch
             import torch.distributed as dist
 
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                    device_id=torch.device("cuda", self.local))
+            timeout = datetime.timedelta(seconds=300)
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+                dist.init_process_group("nccl", timeout=timeout,
+                                        device_id=torch.device("cuda", self.local))
+                self.device = "cuda"
+            else:
+                dist.init_process_group(backend, timeout=timeout)
             self.torch, self.dist = torch, dist
 
     def barrier(self):
         if self.torch:
             self.dist.barrier()
 
-    def max(self, v: float) -> float:
-        if not self.torch:
-            return v
-        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
-        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+    def _reduce(self, v: float, op) -> float:
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=op)
         return float(t.item())
 
+    def max(self, v: float) -> float:
+        return self._reduce(v, self.dist.ReduceOp.MAX) if self.torch else v
+
     def sum(self, v: float) -> float:
-        if not self.torch:
-            return v
-        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
-        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
-        return float(t.item())
+        return self._reduce(v, self.dist.ReduceOp.SUM) if self.torch else v
 
     def close(self):
         if self.torch:

@@ -1,0 +1,71 @@
+"""bench.py's multi-rank plumbing (one process per GPU, replicas, no
+collective on the data path) on CPU: two gloo ranks on 127.0.0.1 take the
+same collective steps the GPU run takes -- barrier, max of the timings,
+sum of the units -- and rank 0's whole-job throughput is all units over the
+slowest rank's time."""
+import os
+import socket
+import sys
+
+import pytest
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, q) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    sys.path.insert(0, ROOT)
+    import bench
+
+    d = bench.Dist(backend="gloo")
+    try:
+        d.barrier()
+        ms = 100.0 * (rank + 1)        # rank 1 is the slow one
+        units = 1000.0 * (rank + 1)
+        t_max = d.max(ms)
+        total = d.sum(units)
+        q.put((rank, t_max, total, total / (t_max / 1e3)))
+    finally:
+        d.close()
+
+
+def test_two_gloo_ranks_aggregate_like_the_gpu_run():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    res = sorted(q.get(timeout=10) for _ in range(world))
+    for rank, t_max, total, value in res:
+        assert t_max == 200.0 and total == 3000.0
+        assert value == pytest.approx(3000.0 / 0.2)
+
+
+def test_aggregate_is_units_over_slowest_rank():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    v, t = bench.aggregate([100.0, 300.0], [50.0, 200.0])
+    assert t == 200.0 and v == pytest.approx(400.0 / 0.2)
+
+
+def test_single_process_dist_is_a_no_op():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    d = bench.Dist(backend="gloo")
+    assert d.world == 1 and d.max(3.0) == 3.0 and d.sum(4.0) == 4.0
+    d.barrier()
+    d.close()
