@@ -187,6 +187,24 @@ class Dist:
             self.dist.destroy_process_group()
 
 
+# The JSON line is the only thing on stdout: libraries that print there (NCCL
+# announces its version on rank 0) are routed to stderr by main().
+_JSON_OUT = sys.stdout
+
+
+def emit(line: dict) -> None:
+    _JSON_OUT.write(json.dumps(line) + "\n")
+    _JSON_OUT.flush()
+
+
+def route_stdout_to_stderr() -> None:
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
+
+
 def aggregate(units_per_rank: list[float], times_ms: list[float]) -> tuple[float, float]:
     """Whole-job throughput: all units over the slowest rank's time."""
     t = max(times_ms)
@@ -263,7 +281,7 @@ def run_reference(args, d: Dist) -> None:
         "e2e": {"value": r["e2e_tok_s"], "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def config_dict(args) -> dict:
@@ -417,7 +435,7 @@ def run_ours(args, d: Dist) -> None:
             "batched": batched,
             "device_error": err,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     dec.close()
 
 
@@ -550,6 +568,7 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the B=32 / B=64 legs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    route_stdout_to_stderr()
     d = Dist() if args.impl == "ours" else None
     if args.impl == "reference":
         class _D:
