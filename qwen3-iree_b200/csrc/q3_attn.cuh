@@ -169,7 +169,12 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
       vv[tt] = tt < nvalid ? __ldcg(reinterpret_cast<const uint2*>(vbase + (int64_t)tt * rowel))
                            : make_uint2(0u, 0u);
   };
-  if (EARLY && have) load_chunk();
+  if (EARLY) {
+    if (have) load_chunk();
+    // cache rows below pos were written by earlier launches: the loads above
+    // went out before the wait; q, k, v come from the previous kernel
+    pdl_wait();
+  }
 
   // 1) q heads 2h, 2h+1 and k head h: norm + rope into shared memory
   if (warp < 3) {
@@ -329,7 +334,9 @@ __global__ void __launch_bounds__(256, EARLY ? 1 : 2) k_attn_decode(const __grid
   __shared__ __align__(16) AttnSmem sm;
   const int h = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   pdl_launch_dependents();
-  pdl_wait();
+  // stop and pos change only in a decode step's last kernel: with EARLY they
+  // and the K/V loads go before the wait (inside attn_group)
+  if (!EARLY) pdl_wait();
   if (a.stop != nullptr && a.stop[(int64_t)b * a.stop_stride] != 0) return;
   const int64_t pos = a.pos[(int64_t)b * a.pos_stride];
   if (pos < 0 || pos >= a.S || pos >= a.rope_pos ||

@@ -157,6 +157,44 @@ __device__ __forceinline__ void cta_rmsnorm_to_smem(const uint16_t* x, const uin
   consumer_sync();
 }
 
+// The same RMSNorm with this thread's gamma values already in registers
+// (gr[i] = g[threadIdx.x + 256 i], loaded before the wait on the previous
+// kernel: gamma is a constant).  K <= 3072.
+constexpr int kGammaRegs = 12;
+__device__ __forceinline__ void load_gamma_regs(const uint16_t* g, int K,
+                                                uint16_t (&gr)[kGammaRegs]) {
+#pragma unroll
+  for (int i = 0; i < kGammaRegs; ++i) {
+    const int k = threadIdx.x + 256 * i;
+    gr[i] = k < K ? g[k] : (uint16_t)0;
+  }
+}
+__device__ __forceinline__ void cta_rmsnorm_to_smem_g(const uint16_t* x,
+                                                      const uint16_t (&gr)[kGammaRegs], int K,
+                                                      uint16_t* xs, float* rs) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < K / 8; i += 256)
+    reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(x)[i];
+  consumer_sync();
+  if (tid < 32) {
+    float ss = 0.0f;
+    for (int k = tid; k < K; k += 32) {
+      const float v = h2f(xs[k]);
+      ss = __fmaf_rn(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if (tid == 0) *rs = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), kEps));
+  }
+  consumer_sync();
+  const float r = *rs;
+#pragma unroll
+  for (int i = 0; i < kGammaRegs; ++i) {
+    const int k = tid + 256 * i;
+    if (k < K) xs[k] = rms_apply(xs[k], gr[i], r);
+  }
+  consumer_sync();
+}
+
 template <int G>
 __device__ __forceinline__ void h2_to_f32(const uint32_t (&xr)[G][16], float (&xf)[G][32]) {
 #pragma unroll
@@ -294,23 +332,30 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
   // ---------------- consumers ----------------
   __shared__ __align__(16) uint16_t xs[3072];
   __shared__ float rs;
-  pdl_wait();  // the previous kernel's outputs (activations, state) are visible
+  // The decode state (stop, pos, tokens) changes only in a step's last
+  // kernel, and gamma never: read them before waiting for the previous kernel.
   const bool stopped = a.seq != nullptr && a.seq->stop != 0;
-  uint32_t xr[G][16];
-  const uint16_t* xcur = nullptr;
-  if ((MODE == kModeNormIn || MODE == kModeSwiglu) && !stopped) {
-    const uint16_t* x = a.seg[0].x;
+  constexpr bool kNorm = MODE == kModeNormIn || MODE == kModeSwiglu;
+  uint16_t gr[kGammaRegs];
+  const uint16_t* xin = a.seg[0].x;
+  if (kNorm && !stopped) {
+    load_gamma_regs(a.norm_g, a.K, gr);
     if (a.tokens != nullptr) {
       int64_t tok = a.tokens[a.seq->pos];
       if (tok < 0 || tok >= kVocab) {
         if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
         tok = 0;
       }
-      x = a.embd + tok * (int64_t)kDim;
-      if (blockIdx.x == 0 && warp == 0 && a.embed_out != nullptr)
-        for (int k = lane; k < a.K; k += 32) a.embed_out[k] = x[k];
+      xin = a.embd + tok * (int64_t)kDim;
     }
-    cta_rmsnorm_to_smem(x, a.norm_g, a.K, xs, &rs);
+  }
+  pdl_wait();  // the previous kernel's outputs (activations) are visible
+  uint32_t xr[G][16];
+  const uint16_t* xcur = nullptr;
+  if (kNorm && !stopped) {
+    if (a.tokens != nullptr && blockIdx.x == 0 && warp == 0 && a.embed_out != nullptr)
+      for (int k = lane; k < a.K; k += 32) a.embed_out[k] = xin[k];
+    cta_rmsnorm_to_smem_g(xin, gr, a.K, xs, &rs);
     load_x_blocks<G>(xs, nb, lane, xr);
   }
 
@@ -325,17 +370,18 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
       }
     }
     const int s = i % ring.ns;
+    const int row = r0 + warp;
+    uint16_t rres = 0;  // the residual, fetched while the row dot runs
+    if (MODE == kModeResid && !stopped && lane == 0) rres = a.seg[seg].r[row];
     if (!mbar_wait(&ring.full[s], (uint32_t)((i / ring.ns) & 1), a.err, kErrTimeoutFull)) break;
     if (!stopped) {
       const uint32_t base = smem_u32(ring.buf + (size_t)s * ring.stage_bytes);
-      const int row = r0 + warp;
       const float d = q8_row_dot<G, ORDER>(base + rowbytes * warp, nb, lane, xr);
       if (MODE == kModeSwiglu) {
         const float u = q8_row_dot<G, ORDER>(base + rowbytes * (kTileRows + warp), nb, lane, xr);
         if (lane == 0) a.seg[seg].y[row] = swiglu_h(f2h(d), f2h(u));
       } else if (MODE == kModeResid) {
-        if (lane == 0)
-          a.seg[seg].y[row] = f2h(__fadd_rn(h2f(a.seg[seg].r[row]), h2f(f2h(d))));
+        if (lane == 0) a.seg[seg].y[row] = f2h(__fadd_rn(h2f(rres), h2f(f2h(d))));
       } else {
         if (lane == 0) a.seg[seg].y[row] = f2h(d);
       }
@@ -412,14 +458,17 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
       ring_drain(ring, i);
     }
   } else {
-    pdl_wait();
+    // stop changes only in this (the step's last) kernel; gamma never
     const bool stopped = a.seq != nullptr && a.seq->stop != 0;
+    uint16_t gr[kGammaRegs];
+    if (a.norm_g != nullptr && !stopped) load_gamma_regs(a.norm_g, a.K, gr);
+    pdl_wait();
     if (threadIdx.x == 0) stopped_s = stopped;
     // lane-strided inputs x[l + 32 i], normalised in f32 and rounded to f16
     uint16_t xh[kVocabK / 32];
     if (!stopped) {
       if (a.norm_g != nullptr) {
-        cta_rmsnorm_to_smem(a.x, a.norm_g, a.K, xs, &rs);
+        cta_rmsnorm_to_smem_g(a.x, gr, a.K, xs, &rs);
 #pragma unroll
         for (int i = 0; i < kVocabK / 32; ++i) xh[i] = xs[lane + 32 * i];
       } else {
