@@ -320,10 +320,21 @@ struct LaunchShape {
   size_t smem;
 };
 
+// Tiles at or below this many per SM run one tile per CTA (Q3_GEMV_ONE_TILE_PER_SM overrides).
+static int one_tile_threshold() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("Q3_GEMV_ONE_TILE_PER_SM");
+    const int x = e ? atoi(e) : 0;
+    v = (x >= 1 && x <= 16) ? x : 4;
+  }
+  return v;
+}
+
 static LaunchShape stream_shape(int ntiles, uint32_t tile_bytes, int ctas_per_sm_stream) {
   const int sms = current_sms();
   LaunchShape s;
-  if (ntiles <= 4 * sms) {
+  if (ntiles <= one_tile_threshold() * sms) {
     s.grid = ntiles > 0 ? ntiles : 1;
     s.nstages = 1;
   } else {

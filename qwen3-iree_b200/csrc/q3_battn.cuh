@@ -33,7 +33,7 @@ namespace q3 {
 constexpr int kBaWarps = 4;                       // consumer warps
 constexpr int kBaThreads = 32 * (kBaWarps + 1);   // + the producer warp
 constexpr int kBaStages = 6;                      // K+V tiles in flight per CTA
-constexpr int kBaSegChunks = 16;                  // 32-key chunks per CTA (512 keys)
+constexpr int kBaSegChunks = 16;                  // default 32-key chunks per CTA (512 keys)
 constexpr uint32_t kBaTileBytes = 32u * kHD * 2u; // one 32-key K (or V) tile
 
 struct BAttnArgs {
@@ -55,6 +55,7 @@ struct BAttnArgs {
   AttnPartial* part;       // [B][8][max_segs][2]
   unsigned int* counters;  // [B][8]
   int max_segs;
+  int seg_chunks;          // 32-key chunks per CTA
   int* err;
   int tag;
 };
@@ -72,9 +73,9 @@ __host__ __device__ constexpr size_t battn_smem_bytes() {
   return 1024 + (size_t)kBaStages * 2 * kBaTileBytes;
 }
 
-__device__ __forceinline__ int battn_nsegs(int64_t pos) {
+__device__ __forceinline__ int battn_nsegs(int64_t pos, int seg_chunks) {
   const int nch = (int)((pos + kAttChunk) / kAttChunk);
-  return (nch + kBaSegChunks - 1) / kBaSegChunks;
+  return (nch + seg_chunks - 1) / seg_chunks;
 }
 
 __device__ __forceinline__ void battn_named_sync() {
@@ -91,16 +92,17 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
 
   // positions were set by an earlier graph launch: readable before the wait
   const int64_t pos = a.pos[(int64_t)b * a.pos_stride];
-  const bool bad = pos < 0 || pos >= a.S || pos >= a.rope_rows || battn_nsegs(pos) > a.max_segs;
-  if (bad || seg >= battn_nsegs(pos)) {
+  const bool bad = pos < 0 || pos >= a.S || pos >= a.rope_rows ||
+                   battn_nsegs(pos, a.seg_chunks) > a.max_segs;
+  if (bad || seg >= battn_nsegs(pos, a.seg_chunks)) {
     pdl_launch_dependents();
     if (bad && seg == 0 && h == 0 && threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
     return;
   }
   const int nch_all = (int)((pos + kAttChunk) / kAttChunk);
-  const int c0 = seg * kBaSegChunks;
-  const int nch = nch_all - c0 < kBaSegChunks ? nch_all - c0 : kBaSegChunks;
-  const int nsegs = battn_nsegs(pos);
+  const int c0 = seg * a.seg_chunks;
+  const int nch = nch_all - c0 < a.seg_chunks ? nch_all - c0 : a.seg_chunks;
+  const int nsegs = battn_nsegs(pos, a.seg_chunks);
   const int64_t row0 = ((int64_t)b * kLayers + a.layer) * a.S;  // cache row of slot 0
 
   if (threadIdx.x == 0) {
