@@ -10,8 +10,9 @@ no PyTorch.
 
 Differences forced by this environment: there is no checkpoint or
 tokenizer.json here, so weights are the seeded random-init model of the
-benchmark configs and prompts are token-id lists -- seeded ones by default,
-one line of ids per prompt with --prompts-file, or text with --tokenizer.
+benchmark configs unless --gguf names a Q8_0 checkpoint, and prompts are
+token-id lists -- seeded ones by default, one line of ids per prompt with
+--prompts-file, or text with --tokenizer.
 
   python -m q3b200.benchmark [--max-tokens 128] [--json out.json]
   python -m q3b200.benchmark --batch 32 --context 128 2048 --steps 128
@@ -64,6 +65,17 @@ def load_tokenizer(path: str | None):
     return Tokenizer.from_file(path)
 
 
+def load_weights(args):
+    """The checkpoint given with --gguf, else the seeded random-init model."""
+    if getattr(args, "gguf", None):
+        from .gguf import load_qwen3_q8
+
+        return load_qwen3_q8(args.gguf)
+    from .weights import synthetic_weights
+
+    return synthetic_weights(seed=args.seed)
+
+
 def bench_one(dec, tokens: list[int], max_tokens: int, eos: int = EOS_TOKEN):
     """One @run call (scripts/benchmark.py:52-81): (n_in, n_out, seconds)."""
     t0 = time.perf_counter()
@@ -103,6 +115,7 @@ def main(argv=None) -> int:
     ap.add_argument("--tokenizer", default=None, help="tokenizer.json (text prompts)")
     ap.add_argument("--text", action="append", default=None, help="text prompt (with --tokenizer)")
     ap.add_argument("--seed", type=int, default=0, help="weights and synthetic prompts")
+    ap.add_argument("--gguf", default=None, help="Qwen3-0.6B Q8_0 GGUF checkpoint (else random init)")
     ap.add_argument("--engine", default="graph", choices=["graph", "persistent"])
     ap.add_argument("--max-seq-len", type=int, default=1024)
     ap.add_argument("--json", default=None, help="write results here")
@@ -113,10 +126,9 @@ def main(argv=None) -> int:
     args = ap.parse_args(argv)
 
     from . import DeviceWeights, Qwen3Decoder, set_device
-    from .weights import synthetic_weights
 
     set_device(args.device)
-    dw = DeviceWeights(synthetic_weights(seed=args.seed))
+    dw = DeviceWeights(load_weights(args))
 
     if args.batch:
         r = bench_batched(dw, args.batch, args.context[0], args.context[1], args.steps, args.seed)

@@ -8,7 +8,8 @@ does the same through libq3b200.so (q3_run).
 
 With --tokenizer PATH (a tokenizer.json; the `tokenizers` package) lines are
 text; without one (none ships here) a line is a list of token ids and the
-reply is printed as ids.  Weights are the seeded random-init model.
+reply is printed as ids.  Weights: a Q8_0 GGUF checkpoint with --gguf, else
+the seeded random-init model.
 
   python -m q3b200.chat [--max-tokens 256] [--tokenizer tokenizer.json]
 """
@@ -20,7 +21,7 @@ import time
 
 import numpy as np
 
-from .benchmark import CHAT_TEMPLATE, EOS_TOKEN, load_tokenizer, trim_eos
+from .benchmark import CHAT_TEMPLATE, EOS_TOKEN, load_tokenizer, load_weights, trim_eos
 
 QUIT_WORDS = ("quit", "exit", "q")
 
@@ -50,15 +51,15 @@ def main(argv=None) -> int:
     ap.add_argument("--max-tokens", type=int, default=256, help="max tokens to generate")
     ap.add_argument("--max-seq-len", type=int, default=1024)
     ap.add_argument("--seed", type=int, default=0, help="random-init weights")
+    ap.add_argument("--gguf", default=None, help="Qwen3-0.6B Q8_0 GGUF checkpoint (else random init)")
     ap.add_argument("--device", type=int, default=0)
     args = ap.parse_args(argv)
 
     from . import DeviceWeights, Qwen3Decoder, set_device
-    from .weights import synthetic_weights
 
     tokenizer = load_tokenizer(args.tokenizer)
     set_device(args.device)
-    dec = Qwen3Decoder(DeviceWeights(synthetic_weights(seed=args.seed)),
+    dec = Qwen3Decoder(DeviceWeights(load_weights(args)),
                        max_seq_len=args.max_seq_len)
     mode = "text" if tokenizer is not None else "token ids"
     print(f"Qwen3-0.6B Q8_0 on libq3b200.so ({mode}; type 'quit' to exit)\n", flush=True)
