@@ -279,6 +279,16 @@ int q3_model_kernel_launches(q3_model* m, int64_t* n);
 int q3_model_trace_steps(q3_model* m, int64_t steps, int64_t trace_step, long long* out,
                          int64_t cap, int* ctas, int* phases);
 
+/* Kernel timeline of the GRAPH engine: runs `steps` decode steps (which
+ * advance the sequence) from a copy of the step graph whose kernels record,
+ * with the GPU's global timer, their first CTA start, first and last release
+ * from the wait on the previous kernel, last CTA end, last CTA start and
+ * first CTA end: out[k][6] in ns from the step's first kernel start
+ * (averaged over steps),
+ * kinds[k] = Q3_KIND_*, *n_kernels = kernels per step.  For latency analysis. */
+int q3_model_trace_kernels(q3_model* m, int64_t steps, long long* out, int32_t* kinds,
+                           int64_t cap, int64_t* n_kernels);
+
 /* Kernel launches of one generation step of the GRAPH engine. */
 int q3_model_launches_per_step(q3_model* m, int64_t* n);
 /* Device error word of the last run (0: none; see q3_strerror(Q3_ERR_DEVICE)). */

@@ -726,6 +726,9 @@ struct q3_model {
   unsigned int* grid_ctr = nullptr;
   int64_t kernel_launches = 0;   // kernels launched by this model so far
   long long* trace_dev = nullptr; // persistent-kernel phase trace (when tracing)
+  cudaGraphExec_t g_ktrace = nullptr;     // graph-engine step with launch timing records
+  unsigned long long* ktrace_dev = nullptr;
+  std::vector<int32_t> ktrace_kinds;
   int trace_step = -1;
   bool chat_ready = false;
   int64_t chat_pos = 0, chat_max = 0;
@@ -736,7 +739,17 @@ struct q3_model {
 struct StepProbe {
   std::vector<cudaEvent_t>* events = nullptr;
   std::vector<int32_t>* kinds = nullptr;
+  unsigned long long* ktrace = nullptr;  // launch timing records, kTraceVals per kernel
+  int* slot = nullptr;                   // next record
+  std::vector<int32_t>* tkinds = nullptr;
 };
+
+// The next launch's timing record while capturing a traced graph, else null.
+static unsigned long long* probe_trace(const StepProbe* pr, int kind) {
+  if (!pr || !pr->ktrace) return nullptr;
+  pr->tkinds->push_back(kind);
+  return pr->ktrace + kTraceVals * (*pr->slot)++;
+}
 
 static int probe_mark(const StepProbe* pr, cudaStream_t st, int kind) {
   if (!pr || !pr->events) return Q3_OK;
@@ -780,6 +793,7 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
       a.embd = (const uint16_t*)m->w.token_embd;
       a.embed_out = m->x;
     }
+    a.trace = probe_trace(probe, Q3_KIND_QKV);
     int rc = launch_q8<kOrderMlir, kModeNormIn>(a, st, launches, true);
     if (rc) return rc;
     Q3_PROBE(Q3_KIND_QKV);
@@ -804,6 +818,7 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
     t.part = m->att_part;
     t.counters = m->att_counters;
     t.err = m->err;
+    t.trace = probe_trace(probe, Q3_KIND_ATTN);
     rc = launch_attn(t, 1, st, launches, true);
     if (rc) return rc;
     Q3_PROBE(Q3_KIND_ATTN);
@@ -812,6 +827,7 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
                        1024, 2048);
     a.seq = m->st;
     a.err = m->err;
+    a.trace = probe_trace(probe, Q3_KIND_O);
     rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches, true);
     if (rc) return rc;
     Q3_PROBE(Q3_KIND_O);
@@ -822,6 +838,7 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
     a.up_off_bytes = 3072 * rb;
     a.seq = m->st;
     a.err = m->err;
+    a.trace = probe_trace(probe, Q3_KIND_GATE_UP);
     rc = launch_q8<kOrderMlir, kModeSwiglu>(a, st, launches, true);
     if (rc) return rc;
     Q3_PROBE(Q3_KIND_GATE_UP);
@@ -831,6 +848,7 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
     a.seq = m->st;
     a.err = m->err;
     if (ingest && l == kLayers - 1) a.advance = m->st;
+    a.trace = probe_trace(probe, Q3_KIND_DOWN);
     rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches, true);
     if (rc) return rc;
     Q3_PROBE(Q3_KIND_DOWN);
@@ -853,6 +871,7 @@ static int enqueue_vocab(q3_model* m, int* launches, const StepProbe* probe) {
   v.seq = m->st;
   v.tokens = m->tokens;
   v.err = m->err;
+  v.trace = probe_trace(probe, Q3_KIND_VOCAB);
   int rc = launch_vocab(v, st, launches, true);
   if (rc) return rc;
   Q3_PROBE(Q3_KIND_VOCAB);
@@ -885,6 +904,8 @@ static void model_free(q3_model* m) {
   if (m->g_ingest) cudaGraphExecDestroy(m->g_ingest);
   if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
   if (m->g_prof) cudaGraphExecDestroy(m->g_prof);
+  if (m->g_ktrace) cudaGraphExecDestroy(m->g_ktrace);
+  if (m->ktrace_dev) cudaFree(m->ktrace_dev);
   for (cudaEvent_t e : m->prof_events) cudaEventDestroy(e);
   void* dev[] = {m->kc, m->vc, m->rope_cos, m->rope_sin, m->x, m->qkv, m->attn, m->h1, m->act,
                  m->logits, m->tokens, m->st, m->am_part, m->att_part, m->err, m->grid_ctr,
@@ -1288,6 +1309,55 @@ extern "C" int q3_model_profile_steps(q3_model* m, int64_t steps, float* times_u
   for (int64_t i = 0; i < nk; ++i) {
     times_us[i] = (float)(acc[(size_t)i] / (double)steps * 1000.0);
     kinds[i] = m->prof_kinds[(size_t)i + 1];
+  }
+  return Q3_OK;
+}
+
+// Timing of every kernel of `steps` graph-engine decode steps (which advance
+// the sequence): out[k][0..5] = first CTA start, first and last release from
+// the wait on the previous kernel, last CTA end, last CTA start, first CTA
+// end, in ns from the step's first kernel start, averaged over the steps;
+// kinds[k] = Q3_KIND_*.
+extern "C" int q3_model_trace_kernels(q3_model* m, int64_t steps, long long* out, int32_t* kinds,
+                                      int64_t cap, int64_t* n_kernels) {
+  Q3_REQUIRE(m && out && kinds && n_kernels && steps >= 1, "bad arguments");
+  if (!m->gen_active) return set_err(Q3_ERR_STATE, "no generation in progress");
+  constexpr int kMaxTraced = 512;
+  if (!m->g_ktrace) {
+    if (!m->ktrace_dev) Q3_CUDA(cudaMalloc((void**)&m->ktrace_dev, kMaxTraced * kTraceVals * 8));
+    int slot = 0, n = 0;
+    m->ktrace_kinds.clear();
+    StepProbe pr;
+    pr.ktrace = m->ktrace_dev;
+    pr.slot = &slot;
+    pr.tkinds = &m->ktrace_kinds;
+    int rc = capture(m, false, &m->g_ktrace, &n, &pr);
+    if (rc) return rc;
+  }
+  const int64_t nk = (int64_t)m->ktrace_kinds.size();
+  *n_kernels = nk;
+  Q3_REQUIRE(cap >= nk && nk <= kMaxTraced, "cap %lld below the %lld kernels of a step",
+             (long long)cap, (long long)nk);
+  constexpr int V = kTraceVals;
+  std::vector<unsigned long long> init((size_t)nk * V, 0ull), rec((size_t)nk * V);
+  for (int64_t k = 0; k < nk; ++k) init[k * V + 0] = init[k * V + 1] = init[k * V + 5] = ~0ull;
+  std::vector<double> acc((size_t)nk * V, 0.0);
+  for (int64_t s = 0; s < steps; ++s) {
+    Q3_CUDA(cudaMemcpyAsync(m->ktrace_dev, init.data(), init.size() * 8, cudaMemcpyHostToDevice,
+                            m->stream));
+    Q3_CUDA(cudaGraphLaunch(m->g_ktrace, m->stream));
+    Q3_CUDA(cudaMemcpyAsync(rec.data(), m->ktrace_dev, rec.size() * 8, cudaMemcpyDeviceToHost,
+                            m->stream));
+    Q3_CUDA(cudaStreamSynchronize(m->stream));
+    unsigned long long t0 = ~0ull;
+    for (int64_t k = 0; k < nk; ++k) t0 = std::min(t0, rec[k * V]);
+    for (size_t i = 0; i < rec.size(); ++i)
+      acc[i] += (rec[i] == ~0ull || rec[i] == 0) ? 0.0 : (double)(rec[i] - t0);
+  }
+  m->kernel_launches += steps * nk;
+  for (int64_t k = 0; k < nk; ++k) {
+    kinds[k] = m->ktrace_kinds[(size_t)k];
+    for (int j = 0; j < 6; ++j) out[k * 6 + j] = (long long)(acc[k * V + j] / (double)steps);
   }
   return Q3_OK;
 }

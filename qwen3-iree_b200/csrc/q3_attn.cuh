@@ -53,6 +53,7 @@ struct AttnArgs {
   unsigned int* counters;   // [B][8], zero between launches
   int max_chunks;           // >= ceil(S / 32)
   int* err;
+  unsigned long long* trace;  // optional launch timing record (4 values)
 };
 
 // Everything one group needs about one (sequence, layer).
@@ -70,6 +71,7 @@ struct AttnCtx {
   AttnPartial* part;      // [8][max_chunks][2]
   unsigned int* counters; // [8]
   int max_chunks;
+  unsigned long long* trace;  // optional launch timing record
 };
 
 struct AttnSmem {
@@ -101,6 +103,27 @@ __device__ __forceinline__ void head_norm_rope(const uint16_t* x, const uint16_t
 #pragma unroll
   for (int i = 0; i < 4; ++i) n[i] = h2f(f2h(__fmul_rn(__fdiv_rn(v[i], r), h2f(g[lane + 32 * i]))));
   // pairs (l, l+64) with angle index l, and (l+32, l+96) with angle index l+32
+  dst[lane] = f2h(__fsub_rn(__fmul_rn(n[0], c0), __fmul_rn(n[2], s0)));
+  dst[lane + 64] = f2h(__fadd_rn(__fmul_rn(n[0], s0), __fmul_rn(n[2], c0)));
+  dst[lane + 32] = f2h(__fsub_rn(__fmul_rn(n[1], c1), __fmul_rn(n[3], s1)));
+  dst[lane + 96] = f2h(__fadd_rn(__fmul_rn(n[1], s1), __fmul_rn(n[3], c1)));
+}
+
+// The same with this lane's gamma values g[lane + 32 i] already in registers.
+__device__ __forceinline__ void head_norm_rope_g(const uint16_t* x, const uint16_t (&gv)[4],
+                                                 float c0, float s0, float c1, float s1, int lane,
+                                                 uint16_t* dst) {
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = h2f(__ldcg(reinterpret_cast<const unsigned short*>(x) + lane + 32 * i));
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = __fmaf_rn(v[i], v[i], ss);
+  ss = warp_sum(ss);
+  const float r = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), kEps));
+  float n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = h2f(f2h(__fmul_rn(__fdiv_rn(v[i], r), h2f(gv[i]))));
   dst[lane] = f2h(__fsub_rn(__fmul_rn(n[0], c0), __fmul_rn(n[2], s0)));
   dst[lane + 64] = f2h(__fadd_rn(__fmul_rn(n[0], s0), __fmul_rn(n[2], c0)));
   dst[lane + 32] = f2h(__fsub_rn(__fmul_rn(n[1], c1), __fmul_rn(n[3], s1)));
@@ -169,20 +192,33 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
       vv[tt] = tt < nvalid ? __ldcg(reinterpret_cast<const uint2*>(vbase + (int64_t)tt * rowel))
                            : make_uint2(0u, 0u);
   };
+  // key pos of this chunk (if any) is taken from the projection, not the cache
+  const int tp = (have && pos < t0 + kAttChunk) ? (int)(pos - t0) : -1;
+  // RoPE angles and norm gammas are constants: read them with the K/V loads
+  float rc0 = 0.f, rs0 = 0.f, rc1 = 0.f, rs1 = 0.f;
+  uint16_t gv[4] = {0, 0, 0, 0};
+  if (warp < 3) {
+    rc0 = c.ct[lane], rs0 = c.sn[lane], rc1 = c.ct[lane + 32], rs1 = c.sn[lane + 32];
+    const uint16_t* g = warp < 2 ? c.q_norm : c.k_norm;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) gv[i] = g[lane + 32 * i];
+  }
   if (EARLY) {
     if (have) load_chunk();
     // cache rows below pos were written by earlier launches: the loads above
     // went out before the wait; q, k, v come from the previous kernel
     pdl_wait();
+    ktrace_release(c.trace);
   }
+  uint2 nv = make_uint2(0u, 0u);  // the new V row's dims 4 lane .. 4 lane + 3
+  if (tp >= 0) nv = __ldcg(reinterpret_cast<const uint2*>(c.qkv + 3072 + h * kHD + 4 * lane));
 
   // 1) q heads 2h, 2h+1 and k head h: norm + rope into shared memory
   if (warp < 3) {
-    const float c0 = c.ct[lane], s0 = c.sn[lane], c1 = c.ct[lane + 32], s1 = c.sn[lane + 32];
     if (warp < 2)
-      head_norm_rope(c.qkv + (2 * h + warp) * kHD, c.q_norm, c0, s0, c1, s1, lane, sm.qs[warp]);
+      head_norm_rope_g(c.qkv + (2 * h + warp) * kHD, gv, rc0, rs0, rc1, rs1, lane, sm.qs[warp]);
     else
-      head_norm_rope(c.qkv + 2048 + h * kHD, c.k_norm, c0, s0, c1, s1, lane, sm.ks);
+      head_norm_rope_g(c.qkv + 2048 + h * kHD, gv, rc0, rs0, rc1, rs1, lane, sm.ks);
   }
   consumer_sync();
   // 2) the group holding key pos writes the new K (normed, roped) and V rows,
@@ -193,14 +229,10 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
     c.vc[off] = __ldcg(reinterpret_cast<const unsigned short*>(c.qkv) + 3072 + h * kHD + threadIdx.x);
   }
   if (!EARLY && have) load_chunk();
-  // key pos of this chunk (if any) comes from shared memory / the projection
-  const int tp = (have && pos < t0 + kAttChunk) ? (int)(pos - t0) : -1;
   if (lane == tp) {
 #pragma unroll
     for (int v = 0; v < kHD / 8; ++v) kv[v] = reinterpret_cast<const uint4*>(sm.ks)[v];
   }
-  uint2 nv = make_uint2(0u, 0u);
-  if (tp >= 0) nv = __ldcg(reinterpret_cast<const uint2*>(c.qkv + 3072 + h * kHD + 4 * lane));
 
   // 3) one chunk of 32 keys per warp -> its partial in shared memory
   if (have) {
@@ -333,10 +365,14 @@ template <bool EARLY>
 __global__ void __launch_bounds__(256, EARLY ? 1 : 2) k_attn_decode(const __grid_constant__ AttnArgs a) {
   __shared__ __align__(16) AttnSmem sm;
   const int h = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  ktrace_start(a.trace);
   pdl_launch_dependents();
   // stop and pos change only in a decode step's last kernel: with EARLY they
   // and the K/V loads go before the wait (inside attn_group)
-  if (!EARLY) pdl_wait();
+  if (!EARLY) {
+    pdl_wait();
+    ktrace_release(a.trace);
+  }
   if (a.stop != nullptr && a.stop[(int64_t)b * a.stop_stride] != 0) return;
   const int64_t pos = a.pos[(int64_t)b * a.pos_stride];
   if (pos < 0 || pos >= a.S || pos >= a.rope_pos ||
@@ -359,7 +395,9 @@ __global__ void __launch_bounds__(256, EARLY ? 1 : 2) k_attn_decode(const __grid
   c.part = a.part + (int64_t)b * kNKV * a.max_chunks * 2;
   c.counters = a.counters + (int64_t)b * kNKV;
   c.max_chunks = a.max_chunks;
+  c.trace = a.trace;
   attn_group<EARLY>(c, h, g, sm);
+  ktrace_end(a.trace);
 }
 
 }  // namespace q3

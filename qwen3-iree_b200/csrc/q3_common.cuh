@@ -195,6 +195,39 @@ __device__ __forceinline__ bool mbar_wait_own(uint64_t* bar, uint32_t parity, in
   }
 }
 
+// Optional per-launch timing record (the graph engine's kernel trace), in ns
+// of %globaltimer, kept by thread 0 of every CTA: t[0] first CTA start,
+// t[1] first release from the wait on the previous kernel, t[2] last
+// release, t[3] last CTA end, t[4] last CTA start, t[5] first CTA end.  A
+// null pointer records nothing.
+constexpr int kTraceVals = 8;
+__device__ __forceinline__ unsigned long long gtimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void ktrace_start(unsigned long long* t) {
+  if (t != nullptr && threadIdx.x == 0) {
+    const unsigned long long n = gtimer_ns();
+    atomicMin(t, n);
+    atomicMax(t + 4, n);
+  }
+}
+__device__ __forceinline__ void ktrace_release(unsigned long long* t) {
+  if (t != nullptr && threadIdx.x == 0) {
+    const unsigned long long n = gtimer_ns();
+    atomicMin(t + 1, n);
+    atomicMax(t + 2, n);
+  }
+}
+__device__ __forceinline__ void ktrace_end(unsigned long long* t) {
+  if (t != nullptr && threadIdx.x == 0) {
+    const unsigned long long n = gtimer_ns();
+    atomicMax(t + 3, n);
+    atomicMin(t + 5, n);
+  }
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));

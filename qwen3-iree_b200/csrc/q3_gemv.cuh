@@ -64,6 +64,7 @@ struct Q8GemvArgs {
   SeqState* advance;     // if set, pos += 1 (the step's last kernel, prompt ingestion)
   int* err;
   int nstages;
+  unsigned long long* trace;  // optional launch timing record (4 values)
 };
 
 // --------------------------------------------------------------------------
@@ -159,18 +160,19 @@ __device__ __forceinline__ void cta_rmsnorm_to_smem(const uint16_t* x, const uin
 
 // The same RMSNorm with this thread's gamma values already in registers
 // (gr[i] = g[threadIdx.x + 256 i], loaded before the wait on the previous
-// kernel: gamma is a constant).  K <= 3072.
-constexpr int kGammaRegs = 12;
+// kernel: gamma is a constant).  KMAX bounds K (a multiple of 256).
+template <int KMAX>
 __device__ __forceinline__ void load_gamma_regs(const uint16_t* g, int K,
-                                                uint16_t (&gr)[kGammaRegs]) {
+                                                uint16_t (&gr)[KMAX / 256]) {
 #pragma unroll
-  for (int i = 0; i < kGammaRegs; ++i) {
+  for (int i = 0; i < KMAX / 256; ++i) {
     const int k = threadIdx.x + 256 * i;
     gr[i] = k < K ? g[k] : (uint16_t)0;
   }
 }
+template <int KMAX>
 __device__ __forceinline__ void cta_rmsnorm_to_smem_g(const uint16_t* x,
-                                                      const uint16_t (&gr)[kGammaRegs], int K,
+                                                      const uint16_t (&gr)[KMAX / 256], int K,
                                                       uint16_t* xs, float* rs) {
   const int tid = threadIdx.x;
   for (int i = tid; i < K / 8; i += 256)
@@ -188,7 +190,7 @@ __device__ __forceinline__ void cta_rmsnorm_to_smem_g(const uint16_t* x,
   consumer_sync();
   const float r = *rs;
 #pragma unroll
-  for (int i = 0; i < kGammaRegs; ++i) {
+  for (int i = 0; i < KMAX / 256; ++i) {
     const int k = tid + 256 * i;
     if (k < K) xs[k] = rms_apply(xs[k], gr[i], r);
   }
@@ -302,6 +304,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
   const int tiles_per_seg = a.seg_rows / kTileRows;
   const int ntiles = a.nseg * tiles_per_seg;
   Ring ring = ring_setup(smem, a.nstages, tile_bytes, kGemvConsumerWarps);
+  ktrace_start(a.trace);
   // Weights do not depend on the previous kernel: let the next kernel launch
   // and this one's copies start before the previous kernel has finished.
   pdl_launch_dependents();
@@ -336,10 +339,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
   // kernel, and gamma never: read them before waiting for the previous kernel.
   const bool stopped = a.seq != nullptr && a.seq->stop != 0;
   constexpr bool kNorm = MODE == kModeNormIn || MODE == kModeSwiglu;
-  uint16_t gr[kGammaRegs];
+  uint16_t gr[G * 4];
   const uint16_t* xin = a.seg[0].x;
   if (kNorm && !stopped) {
-    load_gamma_regs(a.norm_g, a.K, gr);
+    load_gamma_regs<G * 1024>(a.norm_g, a.K, gr);
     if (a.tokens != nullptr) {
       int64_t tok = a.tokens[a.seq->pos];
       if (tok < 0 || tok >= kVocab) {
@@ -350,12 +353,13 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
     }
   }
   pdl_wait();  // the previous kernel's outputs (activations) are visible
+  ktrace_release(a.trace);
   uint32_t xr[G][16];
   const uint16_t* xcur = nullptr;
   if (kNorm && !stopped) {
     if (a.tokens != nullptr && blockIdx.x == 0 && warp == 0 && a.embed_out != nullptr)
       for (int k = lane; k < a.K; k += 32) a.embed_out[k] = xin[k];
-    cta_rmsnorm_to_smem_g(xin, gr, a.K, xs, &rs);
+    cta_rmsnorm_to_smem_g<G * 1024>(xin, gr, a.K, xs, &rs);
     load_x_blocks<G>(xs, nb, lane, xr);
   }
 
@@ -391,6 +395,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
   }
   if (a.advance != nullptr && !stopped && blockIdx.x == 0 && threadIdx.x == 0)
     a.advance->pos += 1;
+  ktrace_end(a.trace);
 }
 
 // --------------------------------------------------------------------------
@@ -425,6 +430,7 @@ struct VocabArgs {
   int64_t* tokens;
   int* err;
   int nstages;
+  unsigned long long* trace;  // optional launch timing record (4 values)
 };
 
 constexpr int kVocabK = 1024;
@@ -438,6 +444,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
   const uint32_t tile_bytes = rowbytes * kTileRows;
   const int ntiles = a.N / kTileRows;
   Ring ring = ring_setup(smem, a.nstages, tile_bytes, kGemvConsumerWarps);
+  ktrace_start(a.trace);
   pdl_launch_dependents();
   __shared__ __align__(16) uint16_t xs[kVocabK];
   __shared__ float rs;
@@ -460,15 +467,16 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
   } else {
     // stop changes only in this (the step's last) kernel; gamma never
     const bool stopped = a.seq != nullptr && a.seq->stop != 0;
-    uint16_t gr[kGammaRegs];
-    if (a.norm_g != nullptr && !stopped) load_gamma_regs(a.norm_g, a.K, gr);
+    uint16_t gr[kVocabK / 256];
+    if (a.norm_g != nullptr && !stopped) load_gamma_regs<kVocabK>(a.norm_g, a.K, gr);
     pdl_wait();
+    ktrace_release(a.trace);
     if (threadIdx.x == 0) stopped_s = stopped;
     // lane-strided inputs x[l + 32 i], normalised in f32 and rounded to f16
     uint16_t xh[kVocabK / 32];
     if (!stopped) {
       if (a.norm_g != nullptr) {
-        cta_rmsnorm_to_smem_g(a.x, gr, a.K, xs, &rs);
+        cta_rmsnorm_to_smem_g<kVocabK>(a.x, gr, a.K, xs, &rs);
 #pragma unroll
         for (int i = 0; i < kVocabK / 32; ++i) xh[i] = xs[lane + 32 * i];
       } else {
@@ -525,6 +533,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
     is_last = (prev == gridDim.x - 1);
   }
   __syncthreads();
+  ktrace_end(a.trace);
   if (!is_last) return;
   __threadfence();
   // last CTA: reduce the per-CTA partials (any order: the rule is a total order)
@@ -574,6 +583,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
     }
     *a.counter = 0u;
   }
+  ktrace_end(a.trace);
 }
 
 }  // namespace q3

@@ -379,6 +379,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_decode_persistent(const __g
         c.part = a.att_part;
         c.counters = a.att_counters;
         c.max_chunks = a.max_chunks;
+        c.trace = nullptr;
         const int ntask = kNKV * attn_ngroups(pos);
         trace_mark(a, s, p, 2);
         for (int j = cta; j < ntask; j += G) attn_group<false>(c, j % kNKV, j / kNKV, asm_);

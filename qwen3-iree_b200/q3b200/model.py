@@ -143,6 +143,19 @@ class Qwen3Decoder:
         call("q3_model_kernel_launches", self.handle, ctypes.byref(n))
         return n.value
 
+    def trace_kernels(self, steps: int = 4):
+        """(times [n, 6] ns, kinds [n]): per kernel of a graph-engine step, its
+        first CTA start, first and last release from the wait on the previous
+        kernel, last CTA end, last CTA start and first CTA end, from the
+        step's first kernel start."""
+        cap = 512
+        out = np.zeros((cap, 6), np.int64)
+        kinds = np.zeros(cap, np.int32)
+        n = ctypes.c_int64(0)
+        call("q3_model_trace_kernels", self.handle, int(steps), out.ctypes.data, kinds.ctypes.data,
+             cap, ctypes.byref(n))
+        return out[:n.value].copy(), kinds[:n.value].copy()
+
     def launches_per_step(self) -> int:
         n = ctypes.c_int64(0)
         call("q3_model_launches_per_step", self.handle, ctypes.byref(n))
