@@ -367,6 +367,9 @@ int q3_batch_read_argmax(q3_batch* m, int64_t* out);
 int q3_batch_profile_steps(q3_batch* m, int64_t steps, float* times_us, int32_t* kinds,
                            int64_t cap, int64_t* n_kernels);
 int q3_batch_kernel_launches(q3_batch* m, int64_t* n);
+/* Kernel timeline of `steps` batched steps, as q3_model_trace_kernels. */
+int q3_batch_trace_kernels(q3_batch* m, int64_t steps, long long* out, int32_t* kinds,
+                           int64_t cap, int64_t* n_kernels);
 
 #ifdef __cplusplus
 }

@@ -76,6 +76,7 @@ struct BGemmArgs {
   int64_t up_rows;       // kBgSwiglu: offset (rows) from a gate row to its up row
   int* err;              // optional device error word (pipeline wait timed out)
   int tag;               // launch tag recorded with a timeout
+  unsigned long long* trace;  // optional launch timing record
 };
 
 // Weight stages (dequantised 64-wide K slices) between the dequantising warps
@@ -193,6 +194,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
   const int splits = (int)gridDim.y;
   const int cbase = (int)blockIdx.y * nchunk;              // first 256-wide chunk of this CTA
   const int tile = blockIdx.x, n0 = tile * 128;
+  ktrace_start(a.trace);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kBgMaxKc; ++i) mbar_init(&raw_full[i], 1);
@@ -237,6 +239,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
                       y0 + (int)(acc * a.up_rows), &raw_full[c]);
       }
       pdl_wait();  // activations come from the previous kernel
+      ktrace_release(a.trace);
       mbar_expect_tx(&x_full, (uint32_t)(nsub * NPAD * 128));
       for (int i = 0; i < nsub; ++i)
         tma_load_2d(gbase + (sX - base) + i * NPAD * 128, &a.xmap, (cbase * 4 + i) * 64, 0, &x_full);
@@ -397,6 +400,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
     tc_fence_after();
     tmem_dealloc(tmem, TCOLS);
   }
+  ktrace_end(a.trace);
 }
 
 // Per-sequence RMSNorm of model/qwen3_full.mlir:134-165 into the GEMM operand
@@ -415,14 +419,17 @@ struct BNormArgs {
   const BatchSeq* seq;
   const uint16_t* embd;
   int* err;
+  unsigned long long* trace;  // optional launch timing record
 };
 
 __global__ void __launch_bounds__(256) k_bnorm(const __grid_constant__ BNormArgs a) {
   __shared__ __align__(16) uint16_t xs[3072];
   __shared__ float rs;
   const int b = blockIdx.x;
+  ktrace_start(a.trace);
   pdl_launch_dependents();
   pdl_wait();
+  ktrace_release(a.trace);
   if (b >= a.B) return;
   const uint16_t* x = a.x + (int64_t)b * a.K;
   if (a.tokens != nullptr) {
@@ -444,6 +451,7 @@ __global__ void __launch_bounds__(256) k_bnorm(const __grid_constant__ BNormArgs
   cta_rmsnorm_to_smem(x, a.gamma, a.K, xs, &rs);
   for (int i = threadIdx.x; i < a.K / 8; i += 256)
     reinterpret_cast<uint4*>(a.xn + (int64_t)b * a.K)[i] = reinterpret_cast<const uint4*>(xs)[i];
+  ktrace_end(a.trace);
 }
 
 // ---------------------------------------------------------------- vocab head
@@ -463,6 +471,7 @@ struct BVocabArgs {
   int64_t* amax;         // optional [B][tok_stride]: argmax after every position, prompt included
   int* err;              // optional device error word
   int tag;               // launch tag recorded with a timeout
+  unsigned long long* trace;  // optional launch timing record
 };
 
 constexpr int kBvAStages = 4;
@@ -485,6 +494,7 @@ __global__ void __launch_bounds__(kBvThreads, 1) k_bvocab(const __grid_constant_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sX = base;                         // 16 atoms of [NPAD x 64]
+  ktrace_start(a.trace);
   const uint32_t sA = sX + 16 * NPAD * 128;         // [4][16 KB]
   uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
 
@@ -532,6 +542,7 @@ __global__ void __launch_bounds__(kBvThreads, 1) k_bvocab(const __grid_constant_
         i_done = i + 1;
         if (!x_issued && i == kBvAStages - 1) {
           pdl_wait();
+          ktrace_release(a.trace);
           mbar_expect_tx(&x_full, 16 * NPAD * 128);
           for (int q = 0; q < 16; ++q) tma_load_2d(gbase + q * NPAD * 128, &a.xmap, q * 64, 0, &x_full);
           x_issued = true;
@@ -539,6 +550,7 @@ __global__ void __launch_bounds__(kBvThreads, 1) k_bvocab(const __grid_constant_
       }
       if (!x_issued) {
         pdl_wait();
+        ktrace_release(a.trace);
         mbar_expect_tx(&x_full, 16 * NPAD * 128);
         for (int q = 0; q < 16; ++q) tma_load_2d(gbase + q * NPAD * 128, &a.xmap, q * 64, 0, &x_full);
       }
@@ -662,6 +674,7 @@ __global__ void __launch_bounds__(kBvThreads, 1) k_bvocab(const __grid_constant_
     if (is_last) *a.counter = 0u;
   }
   __syncthreads();
+  ktrace_end(a.trace);
   if (!is_last) return;
   __threadfence();
   if (threadIdx.x < a.B) {

@@ -58,6 +58,7 @@ struct BAttnArgs {
   int seg_chunks;          // 32-key chunks per CTA
   int* err;
   int tag;
+  unsigned long long* trace;  // optional launch timing record
 };
 
 struct BAttnSmem {
@@ -105,6 +106,7 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
   const int nsegs = battn_nsegs(pos, a.seg_chunks);
   const int64_t row0 = ((int64_t)b * kLayers + a.layer) * a.S;  // cache row of slot 0
 
+  ktrace_start(a.trace);
   if (threadIdx.x == 0) {
     for (int i = 0; i < kBaStages; ++i) {
       mbar_init(&sm.full[i], 1);
@@ -142,6 +144,7 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
 
   // ------------------------------------------------ consumers (warps 0-3)
   pdl_wait();  // q, k, v come from the previous kernel
+  ktrace_release(a.trace);
   const uint16_t* qkv = a.qkv + (int64_t)b * 4096;
   if (warp < 3) {
     const float* ct = a.rope_cos + pos * 64;
@@ -180,8 +183,9 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
     // q.k, lane = key
     float s[2] = {-__int_as_float(0x7f800000), -__int_as_float(0x7f800000)};
     if (lane < nvalid) {
-      float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll 4
+      // four independent accumulation chains per head (16 FMAs deep, not 128)
+      float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
       for (int j = 0; j < kHD / 8; ++j) {
         const int cidx = (j + lane) & 15;
         uint4 kk;
@@ -193,17 +197,17 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
                        : "r"(kt + (uint32_t)lane * 256u + (uint32_t)cidx * 16u));
         }
         const uint4 x0 = q0p[cidx], x1 = q1p[cidx];
-        a0 = fma_h2(x0.x, kk.x, a0);
-        a0 = fma_h2(x0.y, kk.y, a0);
-        a0 = fma_h2(x0.z, kk.z, a0);
-        a0 = fma_h2(x0.w, kk.w, a0);
-        a1 = fma_h2(x1.x, kk.x, a1);
-        a1 = fma_h2(x1.y, kk.y, a1);
-        a1 = fma_h2(x1.z, kk.z, a1);
-        a1 = fma_h2(x1.w, kk.w, a1);
+        a0[0] = fma_h2(x0.x, kk.x, a0[0]);
+        a0[1] = fma_h2(x0.y, kk.y, a0[1]);
+        a0[2] = fma_h2(x0.z, kk.z, a0[2]);
+        a0[3] = fma_h2(x0.w, kk.w, a0[3]);
+        a1[0] = fma_h2(x1.x, kk.x, a1[0]);
+        a1[1] = fma_h2(x1.y, kk.y, a1[1]);
+        a1[2] = fma_h2(x1.z, kk.z, a1[2]);
+        a1[3] = fma_h2(x1.w, kk.w, a1[3]);
       }
-      s[0] = __fmul_rn(a0, kAttnScale);
-      s[1] = __fmul_rn(a1, kAttnScale);
+      s[0] = __fmul_rn(__fadd_rn(__fadd_rn(a0[0], a0[1]), __fadd_rn(a0[2], a0[3])), kAttnScale);
+      s[1] = __fmul_rn(__fadd_rn(__fadd_rn(a1[0], a1[1]), __fadd_rn(a1[2], a1[3])), kAttnScale);
     }
     float p[2], scale[2];
 #pragma unroll
@@ -217,18 +221,11 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
 #pragma unroll
       for (int d = 0; d < 4; ++d) o[hh][d] = __fmul_rn(o[hh][d], scale[hh]);
     }
-    // p.v, lane = head dims 4*lane .. 4*lane+3
-    for (int tt = 0; tt < nvalid; ++tt) {
+    // p.v, lane = head dims 4*lane .. 4*lane+3; a full chunk without the new
+    // key (the common case) runs fully unrolled so its shuffles and loads overlap
+    auto pv_step = [&](int tt, uint2 vv) {
       const float p0 = __shfl_sync(0xffffffffu, p[0], tt);
       const float p1 = __shfl_sync(0xffffffffu, p[1], tt);
-      uint2 vv;
-      if (tt == tp) {
-        vv = vnew;
-      } else {
-        asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];"
-                     : "=r"(vv.x), "=r"(vv.y)
-                     : "r"(vt + (uint32_t)tt * 256u + (uint32_t)lane * 8u));
-      }
       const float v0 = h2f((uint16_t)(vv.x & 0xffffu)), v1 = h2f((uint16_t)(vv.x >> 16));
       const float v2 = h2f((uint16_t)(vv.y & 0xffffu)), v3 = h2f((uint16_t)(vv.y >> 16));
       o[0][0] = __fmaf_rn(p0, v0, o[0][0]);
@@ -239,6 +236,19 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
       o[1][1] = __fmaf_rn(p1, v1, o[1][1]);
       o[1][2] = __fmaf_rn(p1, v2, o[1][2]);
       o[1][3] = __fmaf_rn(p1, v3, o[1][3]);
+    };
+    auto ld_v = [&](int tt) {
+      uint2 vv;
+      asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];"
+                   : "=r"(vv.x), "=r"(vv.y)
+                   : "r"(vt + (uint32_t)tt * 256u + (uint32_t)lane * 8u));
+      return vv;
+    };
+    if (nvalid == kAttChunk && tp < 0) {
+#pragma unroll
+      for (int tt = 0; tt < kAttChunk; ++tt) pv_step(tt, ld_v(tt));
+    } else {
+      for (int tt = 0; tt < nvalid; ++tt) pv_step(tt, tt == tp ? vnew : ld_v(tt));
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[st]);  // the stage may be refilled
@@ -283,7 +293,10 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
       __threadfence();
     }
     asm volatile("bar.sync 2, 64;" ::: "memory");
-    if (!sm.last) return;
+    if (!sm.last) {
+      ktrace_end(a.trace);
+      return;
+    }
     const AttnPartial* pb = a.part + (((int64_t)b * kNKV + h) * a.max_segs) * 2 + hh;
     mm = __ldcg(&pb->m);
     ll = __ldcg(&pb->l);
@@ -317,6 +330,7 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
   pk.x = (uint32_t)f2h(__fdiv_rn(oo[0], ll)) | ((uint32_t)f2h(__fdiv_rn(oo[1], ll)) << 16);
   pk.y = (uint32_t)f2h(__fdiv_rn(oo[2], ll)) | ((uint32_t)f2h(__fdiv_rn(oo[3], ll)) << 16);
   *reinterpret_cast<uint2*>(outp) = pk;
+  ktrace_end(a.trace);
 }
 
 }  // namespace q3

@@ -106,6 +106,7 @@ SIGNATURES = {
     "q3_batch_read": [P, P, P, ctypes.POINTER(ctypes.c_int)],
     "q3_batch_read_argmax": [P, P],
     "q3_model_trace_kernels": [P, I64, P, P, I64, PI64],
+    "q3_batch_trace_kernels": [P, I64, P, P, I64, PI64],
     "q3_batch_attention_workspace_bytes": [I64, I],
     "q3_batch_attention": [P, P, P, P, P, I64, P, P, I, I64, I, P, P, P, P],
     "q3_batch_profile_steps": [P, I64, P, P, I64, PI64],

@@ -238,6 +238,17 @@ class BatchDecoder:
              ctypes.byref(n))
         return t[:n.value].copy(), k[:n.value].copy()
 
+    def trace_kernels(self, steps: int = 4):
+        """(times [n, 6] ns, kinds [n]) per kernel of a batched step, as
+        Qwen3Decoder.trace_kernels."""
+        cap = 512
+        out = np.zeros((cap, 6), np.int64)
+        kinds = np.zeros(cap, np.int32)
+        n = ctypes.c_int64(0)
+        call("q3_batch_trace_kernels", self.handle, int(steps), out.ctypes.data, kinds.ctypes.data,
+             cap, ctypes.byref(n))
+        return out[:n.value].copy(), kinds[:n.value].copy()
+
     def read_argmax(self) -> np.ndarray:
         """[B, S+1]: entry p+1 is the greedy token after feeding position p."""
         out = np.zeros((self.B, self.max_seq_len + 1), np.int64)
