@@ -605,7 +605,7 @@ __global__ void __launch_bounds__(kBvThreads, 1) k_bvocab(const __grid_constant_
       const int ab = k & 1;
       if (!Q3_BWAIT(&acc_full[ab], (k / 2) & 1, kErrTimeoutFull, 18)) break;
       tc_fence_after();
-      const int64_t n = (int64_t)t * 128 + 32 * q + lane;
+      const int64_t n = (int64_t)t * 128 + 32 * q + lane;  // this lane's vocabulary row
 #pragma unroll
       for (int col0 = 0; col0 < NPAD; col0 += 16) {
         uint32_t v[16];
@@ -616,21 +616,24 @@ __global__ void __launch_bounds__(kBvThreads, 1) k_bvocab(const __grid_constant_
           const int b = col0 + j;
           const uint16_t lh = f2h(__uint_as_float(v[j]));
           if (a.logits != nullptr && b < a.B) a.logits[(int64_t)b * a.ld_logits + n] = lh;
-          float lv = h2f(lh);
-          int64_t li = n;
-          // warp argmax over its 32 rows (a total order: any reduction order works)
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, lv, off);
-            const int64_t oi = __shfl_xor_sync(0xffffffffu, li, off);
-            if (am_better(ov, oi, lv, li)) {
-              lv = ov;
-              li = oi;
+          // warp argmax over its 32 rows in one reduction: the key orders as
+          // the f16 value (-0 taken as +0: they compare equal) and then by
+          // lower row; NaN and -inf never win (key 0), as in the strict ogt
+          // scan (model/qwen3_full.mlir:1482-1507)
+          const uint32_t hz = lh == 0x8000u ? 0u : (uint32_t)lh;
+          const bool nan_or_ninf = (hz & 0x7C00u) == 0x7C00u && ((hz & 0x03FFu) != 0u || (hz & 0x8000u));
+          const uint32_t ord = (hz & 0x8000u) ? (~hz & 0xFFFFu) : (hz | 0x8000u);
+          const uint32_t key = nan_or_ninf ? 0u : ((ord << 16) | (0xFFFFu - (uint32_t)lane));
+          const uint32_t best = __reduce_max_sync(0xffffffffu, key);
+          if (lane == (b & 31) && best != 0u) {
+            const uint32_t bo = best >> 16;
+            const uint16_t bh = (bo & 0x8000u) ? (uint16_t)(bo & 0x7FFFu) : (uint16_t)(~bo & 0xFFFFu);
+            const int64_t li = (int64_t)t * 128 + 32 * q + (int64_t)(0xFFFFu - (best & 0xFFFFu));
+            const float lv = h2f(bh);
+            if (am_better(lv, li, bv[b >> 5], bi[b >> 5])) {
+              bv[b >> 5] = lv;
+              bi[b >> 5] = li;
             }
-          }
-          if (lane == (b & 31) && am_better(lv, li, bv[b >> 5], bi[b >> 5])) {
-            bv[b >> 5] = lv;
-            bi[b >> 5] = li;
           }
         }
       }
