@@ -43,11 +43,12 @@ constexpr uint32_t kBgAtomA = 128u * 128u;     // 128 rows x 64 f16, SWIZZLE_128
 
 enum BGemmMode : int { kBgPlain = 0, kBgResid = 1, kBgSwiglu = 2 };
 
-// A pipeline wait of the batched kernels gives up after ~0.2 s (a whole
-// decode step takes milliseconds) and records in the error word
+// A pipeline wait of the batched kernels gives up after ~1 s of SM clock
+// (kSpinCycles, as every other wait here; a decode step takes milliseconds)
+// and records in the error word
 //   bits 0-3: kErrTimeout*, bits 4-7: wait site, bits 8-15: launch tag
 //   (layer * 8 + kernel), bits 16-27: CTA index.
-constexpr long long kBatchSpinCycles = 400000000ll;
+constexpr long long kBatchSpinCycles = kSpinCycles;
 __device__ __forceinline__ int bwait_code(int code, int site, int tag) {
   return code | (site << 4) | ((tag & 0xff) << 8) | (((int)blockIdx.x & 0xfff) << 16);
 }

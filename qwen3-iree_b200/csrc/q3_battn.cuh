@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
         const int st = i % kBaStages;
         if (i >= kBaStages &&
             !mbar_wait_own(&sm.empty[st], ((i / kBaStages) - 1) & 1, a.err,
-                           kErrTimeoutEmpty | (1 << 4) | ((a.tag & 0xff) << 8), 400000000ll))
+                           kErrTimeoutEmpty | (1 << 4) | ((a.tag & 0xff) << 8), kSpinCycles))
           break;
         mbar_expect_tx(&sm.full[st], 2 * kBaTileBytes);
         const int y = (int)(row0 + (int64_t)(c0 + i) * kAttChunk);
@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
       }
       for (int st = 0; st < kBaStages && st < issued; ++st)  // no copy in flight at exit
         mbar_wait_own(&sm.full[st], ((issued - 1 - st) / kBaStages) & 1, a.err,
-                      kErrTimeoutFull | (2 << 4) | ((a.tag & 0xff) << 8), 400000000ll);
+                      kErrTimeoutFull | (2 << 4) | ((a.tag & 0xff) << 8), kSpinCycles);
     }
     return;  // the producer warp takes no part in the consumers' barriers
   }
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
   for (int i = warp; i < nch; i += kBaWarps) {
     const int st = i % kBaStages;
     if (!mbar_wait_own(&sm.full[st], (i / kBaStages) & 1, a.err,
-                       kErrTimeoutFull | (3 << 4) | ((a.tag & 0xff) << 8), 400000000ll))
+                       kErrTimeoutFull | (3 << 4) | ((a.tag & 0xff) << 8), kSpinCycles))
       break;
     const int64_t t0 = (int64_t)(c0 + i) * kAttChunk;
     const int tp = pos < t0 + kAttChunk ? (int)(pos - t0) : -1;  // the new key in this chunk
