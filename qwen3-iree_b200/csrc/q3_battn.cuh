@@ -32,7 +32,10 @@ namespace q3 {
 
 constexpr int kBaWarps = 4;                       // consumer warps
 constexpr int kBaThreads = 32 * (kBaWarps + 1);   // + the producer warp
-constexpr int kBaStages = 6;                      // K+V tiles in flight per CTA
+#ifndef Q3_BA_STAGES
+#define Q3_BA_STAGES 6
+#endif
+constexpr int kBaStages = Q3_BA_STAGES;           // K+V tiles in flight per CTA
 constexpr int kBaSegChunks = 16;                  // default 32-key chunks per CTA (512 keys)
 constexpr uint32_t kBaTileBytes = 32u * kHD * 2u; // one 32-key K (or V) tile
 
