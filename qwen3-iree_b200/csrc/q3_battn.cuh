@@ -36,6 +36,16 @@ constexpr int kBaThreads = 32 * (kBaWarps + 1);   // + the producer warp
 #define Q3_BA_STAGES 6
 #endif
 constexpr int kBaStages = Q3_BA_STAGES;           // K+V tiles in flight per CTA
+// Full barriers, chunk i on full[i % kBaFullBars].  Consumer warps take chunks
+// round robin, so with one barrier per stage a warp would wait on phase k of a
+// stage whose phase k-1 (another warp's chunk) it never saw: TMA copies land
+// in any order, and while phase k-1 is still pending a parity wait for phase
+// k reads as complete.  A multiple of the warp count gives every warp its own
+// barriers (it saw their previous phases itself), and with at least kBaStages
+// of them chunk i - kBaFullBars was consumed, its phase closed, before the
+// producer arms chunk i.
+constexpr int kBaFullBars = ((kBaStages + kBaWarps - 1) / kBaWarps) * kBaWarps;
+static_assert(kBaFullBars % kBaWarps == 0 && kBaFullBars >= kBaStages, "full barrier count");
 constexpr int kBaSegChunks = 16;                  // default 32-key chunks per CTA (512 keys)
 constexpr uint32_t kBaTileBytes = 32u * kHD * 2u; // one 32-key K (or V) tile
 
@@ -65,7 +75,7 @@ struct BAttnArgs {
 };
 
 struct BAttnSmem {
-  uint64_t full[kBaStages], empty[kBaStages];
+  uint64_t full[kBaFullBars], empty[kBaStages];
   float wm[kBaWarps][2], wl[kBaWarps][2];
   float wo[kBaWarps][2][kHD];
   uint16_t qs[2][kHD];
@@ -111,10 +121,8 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
 
   ktrace_start(a.trace);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kBaStages; ++i) {
-      mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1);
-    }
+    for (int i = 0; i < kBaFullBars; ++i) mbar_init(&sm.full[i], 1);
+    for (int i = 0; i < kBaStages; ++i) mbar_init(&sm.empty[i], 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -132,14 +140,17 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
             !mbar_wait_own(&sm.empty[st], ((i / kBaStages) - 1) & 1, a.err,
                            kErrTimeoutEmpty | (1 << 4) | ((a.tag & 0xff) << 8), kSpinCycles))
           break;
-        mbar_expect_tx(&sm.full[st], 2 * kBaTileBytes);
+        uint64_t* const fb = &sm.full[i % kBaFullBars];
+        mbar_expect_tx(fb, 2 * kBaTileBytes);
         const int y = (int)(row0 + (int64_t)(c0 + i) * kAttChunk);
-        tma_load_2d(gbase + st * 2 * kBaTileBytes, &a.kmap, h * kHD, y, &sm.full[st]);
-        tma_load_2d(gbase + st * 2 * kBaTileBytes + kBaTileBytes, &a.vmap, h * kHD, y, &sm.full[st]);
+        tma_load_2d(gbase + st * 2 * kBaTileBytes, &a.kmap, h * kHD, y, fb);
+        tma_load_2d(gbase + st * 2 * kBaTileBytes + kBaTileBytes, &a.vmap, h * kHD, y, fb);
         issued = i + 1;
       }
-      for (int st = 0; st < kBaStages && st < issued; ++st)  // no copy in flight at exit
-        mbar_wait_own(&sm.full[st], ((issued - 1 - st) / kBaStages) & 1, a.err,
+      // no copy in flight at exit: every chunk before issued - kBaStages was
+      // consumed, so only the last kBaStages can still be landing
+      for (int i = issued > kBaStages ? issued - kBaStages : 0; i < issued; ++i)
+        mbar_wait_own(&sm.full[i % kBaFullBars], (i / kBaFullBars) & 1, a.err,
                       kErrTimeoutFull | (2 << 4) | ((a.tag & 0xff) << 8), kSpinCycles);
     }
     return;  // the producer warp takes no part in the consumers' barriers
@@ -176,7 +187,7 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
   float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   for (int i = warp; i < nch; i += kBaWarps) {
     const int st = i % kBaStages;
-    if (!mbar_wait_own(&sm.full[st], (i / kBaStages) & 1, a.err,
+    if (!mbar_wait_own(&sm.full[i % kBaFullBars], (i / kBaFullBars) & 1, a.err,
                        kErrTimeoutFull | (3 << 4) | ((a.tag & 0xff) << 8), kSpinCycles))
       break;
     const int64_t t0 = (int64_t)(c0 + i) * kAttChunk;
