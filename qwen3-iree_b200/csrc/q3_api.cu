@@ -331,7 +331,36 @@ static int one_tile_threshold() {
   return v;
 }
 
-static LaunchShape stream_shape(int ntiles, uint32_t tile_bytes, int ctas_per_sm_stream) {
+// CTAs per SM of a multi-tile Q8_0 GEMV launch: 3 (measured over 28-layer
+// launches: 2.2-3.2 TB/s against 2.0-3.0 at 2); Q3_GEMV_STREAM_CTAS overrides, 1..4.
+static int gemv_stream_ctas() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("Q3_GEMV_STREAM_CTAS");
+    const int x = e ? atoi(e) : 0;
+    v = (x >= 1 && x <= 4) ? x : 3;
+  }
+  return v;
+}
+
+// Shared memory of one SM and the part of it each CTA loses to the runtime.
+static void sm_smem_limits(size_t* per_sm, size_t* reserved) {
+  int dev = 0, v = 0, r = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess)
+    v = 0;
+  if (cudaDeviceGetAttribute(&r, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess)
+    r = 1024;
+  *per_sm = v > 0 ? (size_t)v : 228 * 1024;
+  *reserved = (size_t)r;
+}
+
+// Grid and ring depth: one tile per CTA for small launches, else
+// ctas_per_sm_stream CTAs on every SM, each ring as deep as the SM's shared
+// memory allows once every CTA's static shared memory (static_smem) and
+// reservation are counted.
+static LaunchShape stream_shape(int ntiles, uint32_t tile_bytes, int ctas_per_sm_stream,
+                                size_t static_smem = 0) {
   const int sms = current_sms();
   LaunchShape s;
   if (ntiles <= one_tile_threshold() * sms) {
@@ -340,7 +369,14 @@ static LaunchShape stream_shape(int ntiles, uint32_t tile_bytes, int ctas_per_sm
   } else {
     s.grid = ctas_per_sm_stream * sms;
     const int tpc = (ntiles + s.grid - 1) / s.grid;
-    const size_t budget = (size_t)(kMaxDynSmem / ctas_per_sm_stream) - 1024;
+    size_t budget = (size_t)(kMaxDynSmem / ctas_per_sm_stream) - 1024;
+    if (static_smem > 0) {
+      size_t per_sm = 0, reserved = 0;
+      sm_smem_limits(&per_sm, &reserved);
+      const size_t share = per_sm / ctas_per_sm_stream;
+      const size_t fit = share > reserved + static_smem + 256 ? share - reserved - static_smem - 256 : 0;
+      budget = std::min(budget, fit);
+    }
     int ns = (int)(budget / tile_bytes);
     if (ns < 1) ns = 1;
     if (ns > 16) ns = 16;
@@ -356,7 +392,14 @@ static int launch_q8_t(Q8GemvArgs a, cudaStream_t st, int* launches, bool pdl) {
   const uint32_t rowbytes = (uint32_t)(a.K / kQBlk) * kQBytes;
   const uint32_t tile_bytes = rowbytes * kTileRows * (MODE == kModeSwiglu ? 2u : 1u);
   const int ntiles = a.nseg * (a.seg_rows / kTileRows);
-  LaunchShape ls = stream_shape(ntiles, tile_bytes, 2);
+  static size_t static_smem = 0;
+  if (static_smem == 0) {
+    cudaFuncAttributes fa;
+    static_smem = cudaFuncGetAttributes(&fa, k_gemv_q8<G, ORDER, MODE>) == cudaSuccess
+                      ? fa.sharedSizeBytes + 16
+                      : 16 * 1024;
+  }
+  LaunchShape ls = stream_shape(ntiles, tile_bytes, gemv_stream_ctas(), static_smem);
   a.nstages = ls.nstages;
   int rc = ensure_smem_attr(k_gemv_q8<G, ORDER, MODE>, ls.smem);
   if (rc) return rc;

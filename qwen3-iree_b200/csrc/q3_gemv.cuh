@@ -242,6 +242,109 @@ __device__ __forceinline__ float q8_row_dot(uint32_t row, int nb, int lane,
 }
 
 // --------------------------------------------------------------------------
+// x staged once per CTA as f32 in shared memory (k_gemv_q8)
+// --------------------------------------------------------------------------
+// Block b's 32 values sit at floats [36 b, 36 b + 32) (144 bytes a block).
+// A lane reads its own block b = lane + 32 g as 8 float4; at float4 i that is
+// 16-byte bank group (9 b + i) mod 8, distinct across the 8 lanes of a
+// quarter warp, so the reads are conflict-free.  f16 -> f32 is exact, so the
+// row dots see the same operand values as with f16 x.
+constexpr int kXfStride = 36;
+
+__device__ __forceinline__ int xf_index(int k) { return (k >> 5) * kXfStride + (k & 31); }
+
+// x (f16, K a multiple of 8, 16-byte aligned) -> xf by the 256 consumer
+// threads; ends with a consumer barrier.
+__device__ __forceinline__ void stage_x_f32(const uint16_t* x, int K, float* xf) {
+  for (int i = threadIdx.x; i < K / 8; i += 256) {
+    const uint4 v = reinterpret_cast<const uint4*>(x)[i];
+    float* d = xf + xf_index(8 * i);
+    *reinterpret_cast<float4*>(d) =
+        make_float4(h2f((uint16_t)(v.x & 0xffffu)), h2f((uint16_t)(v.x >> 16)),
+                    h2f((uint16_t)(v.y & 0xffffu)), h2f((uint16_t)(v.y >> 16)));
+    *reinterpret_cast<float4*>(d + 4) =
+        make_float4(h2f((uint16_t)(v.z & 0xffffu)), h2f((uint16_t)(v.z >> 16)),
+                    h2f((uint16_t)(v.w & 0xffffu)), h2f((uint16_t)(v.w >> 16)));
+  }
+  consumer_sync();
+}
+
+// RMSNorm into xf: the same operations and order as cta_rmsnorm_to_smem_g
+// (sum of squares in warp 0's lane-strided order, x_k / r * g_k rounded to
+// f16), with the normalised f16 values stored as f32.
+template <int KMAX>
+__device__ __forceinline__ void cta_rmsnorm_to_xf(const uint16_t* x,
+                                                  const uint16_t (&gr)[KMAX / 256], int K,
+                                                  float* xf, float* rs) {
+  const int tid = threadIdx.x;
+  stage_x_f32(x, K, xf);
+  if (tid < 32) {
+    float ss = 0.0f;
+    for (int k = tid; k < K; k += 32) {
+      const float v = xf[xf_index(k)];
+      ss = __fmaf_rn(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if (tid == 0) *rs = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), kEps));
+  }
+  consumer_sync();
+  const float r = *rs;
+#pragma unroll
+  for (int i = 0; i < KMAX / 256; ++i) {
+    const int k = tid + 256 * i;
+    if (k < K) {
+      float* p = xf + xf_index(k);
+      *p = h2f(f2h(__fmul_rn(__fdiv_rn(*p, r), h2f(gr[i]))));
+    }
+  }
+  consumer_sync();
+}
+
+// Dot of one Q8_0 row (shared byte address `row`) with x staged in xf, in
+// the same per-block orders as q8_row_dot: MLIR, inner = fma chain of
+// q_j * x_j over j then acc = fma(scale, inner, acc); CUDA, acc = fma(scale *
+// q_j, x_j, acc) per element.  int8 -> f32 by the exact byte-perm offset.
+template <int G, int ORDER>
+__device__ __forceinline__ float q8_row_dot_xf(uint32_t row, int nb, int lane, const float* xf) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int b = lane + 32 * g;
+    if (b < nb) {
+      const Q8BlockWords bw = q8_load_block(row + (uint32_t)(kQBytes * b));
+      const float4* xb = reinterpret_cast<const float4*>(xf + b * kXfStride);
+      if constexpr (ORDER == kOrderMlir) {
+        float inner = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 xv = xb[i];
+          float f[4];
+          q8x4_to_f32(bw.q[i], f);
+          inner = __fmaf_rn(f[0], xv.x, inner);
+          inner = __fmaf_rn(f[1], xv.y, inner);
+          inner = __fmaf_rn(f[2], xv.z, inner);
+          inner = __fmaf_rn(f[3], xv.w, inner);
+        }
+        acc = __fmaf_rn(h2f((uint16_t)bw.scale16), inner, acc);
+      } else {
+        const float sc = h2f((uint16_t)bw.scale16);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 xv = xb[i];
+          float f[4];
+          q8x4_to_f32(bw.q[i], f);
+          acc = __fmaf_rn(__fmul_rn(sc, f[0]), xv.x, acc);
+          acc = __fmaf_rn(__fmul_rn(sc, f[1]), xv.y, acc);
+          acc = __fmaf_rn(__fmul_rn(sc, f[2]), xv.z, acc);
+          acc = __fmaf_rn(__fmul_rn(sc, f[3]), xv.w, acc);
+        }
+      }
+    }
+  }
+  return warp_sum(acc);
+}
+
+// --------------------------------------------------------------------------
 // Ring of shared-memory stages fed by the producer warp
 // --------------------------------------------------------------------------
 struct Ring {
@@ -295,7 +398,7 @@ __device__ __forceinline__ void ring_drain(const Ring& r, int issued) {
 // Q8_0 GEMV kernel
 // --------------------------------------------------------------------------
 template <int G, int ORDER, int MODE>
-__global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant__ Q8GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, 1) k_gemv_q8(const __grid_constant__ Q8GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = a.K / kQBlk;
@@ -303,6 +406,11 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
   const uint32_t tile_bytes = rowbytes * kTileRows * (MODE == kModeSwiglu ? 2u : 1u);
   const int tiles_per_seg = a.seg_rows / kTileRows;
   const int ntiles = a.nseg * tiles_per_seg;
+  // A contiguous run of tiles per CTA: with several segments (layers) in one
+  // launch a CTA crosses at most a few segment boundaries, so its x vector is
+  // reloaded that often rather than on every tile.
+  const int t_begin = (int)((int64_t)blockIdx.x * ntiles / gridDim.x);
+  const int t_end = (int)((int64_t)(blockIdx.x + 1) * ntiles / gridDim.x);
   Ring ring = ring_setup(smem, a.nstages, tile_bytes, kGemvConsumerWarps);
   ktrace_start(a.trace);
   // Weights do not depend on the previous kernel: let the next kernel launch
@@ -313,12 +421,13 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      int i = 0;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
-        if (!ring_acquire(ring, i, a.err)) break;
-        const int s = i % ring.ns;
-        const int seg = t / tiles_per_seg;
-        const int r0 = (t % tiles_per_seg) * kTileRows;
+      // tile t = t_begin + i sits in stage s = i % ns, round i / ns; segment
+      // and row are stepped along instead of divided out per tile
+      int i = 0, s = 0, seg = t_begin / tiles_per_seg, r0 = (t_begin % tiles_per_seg) * kTileRows;
+      uint32_t round_par = 0;
+      for (int t = t_begin; t < t_end; ++t, ++i) {
+        if (i >= ring.ns && !mbar_wait(&ring.empty[s], round_par ^ 1u, a.err, kErrTimeoutEmpty))
+          break;
         const uint8_t* src = a.seg[seg].w + (int64_t)r0 * rowbytes;
         uint8_t* dst = ring.buf + (size_t)s * ring.stage_bytes;
         mbar_expect_tx(&ring.full[s], tile_bytes);
@@ -326,6 +435,8 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
         if (MODE == kModeSwiglu)
           bulk_g2s(dst + rowbytes * kTileRows, src + a.up_off_bytes, rowbytes * kTileRows,
                    &ring.full[s], pol);
+        if (++s == ring.ns) s = 0, round_par ^= 1u;
+        if ((r0 += kTileRows) == a.seg_rows) r0 = 0, ++seg;
       }
       ring_drain(ring, i);
     }
@@ -333,7 +444,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
   }
 
   // ---------------- consumers ----------------
-  __shared__ __align__(16) uint16_t xs[3072];
+  __shared__ __align__(16) float xf[G * 32 * kXfStride];
   __shared__ float rs;
   // The decode state (stop, pos, tokens) changes only in a step's last
   // kernel, and gamma never: read them before waiting for the previous kernel.
@@ -354,35 +465,33 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
   }
   pdl_wait();  // the previous kernel's outputs (activations) are visible
   ktrace_release(a.trace);
-  uint32_t xr[G][16];
   const uint16_t* xcur = nullptr;
   if (kNorm && !stopped) {
     if (a.tokens != nullptr && blockIdx.x == 0 && warp == 0 && a.embed_out != nullptr)
       for (int k = lane; k < a.K; k += 32) a.embed_out[k] = xin[k];
-    cta_rmsnorm_to_smem_g<G * 1024>(xin, gr, a.K, xs, &rs);
-    load_x_blocks<G>(xs, nb, lane, xr);
+    cta_rmsnorm_to_xf<G * 1024>(xin, gr, a.K, xf, &rs);
   }
 
-  int i = 0;
-  for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
-    const int seg = t / tiles_per_seg;
-    const int r0 = (t % tiles_per_seg) * kTileRows;
-    if ((MODE == kModePlain || MODE == kModeResid) && !stopped) {
-      if (a.seg[seg].x != xcur) {
-        xcur = a.seg[seg].x;
-        load_x_blocks<G>(xcur, nb, lane, xr);
-      }
+  // A warp whose wait timed out keeps walking the tiles without computing,
+  // so that every consumer warp still reaches the barriers of an x reload.
+  bool live = true;
+  int s = 0, seg = t_begin / tiles_per_seg, r0 = (t_begin % tiles_per_seg) * kTileRows;
+  uint32_t round_par = 0;
+  for (int t = t_begin; t < t_end; ++t) {
+    if ((MODE == kModePlain || MODE == kModeResid) && !stopped && a.seg[seg].x != xcur) {
+      if (xcur != nullptr) consumer_sync();  // every warp is done with the previous x
+      xcur = a.seg[seg].x;
+      stage_x_f32(xcur, a.K, xf);
     }
-    const int s = i % ring.ns;
     const int row = r0 + warp;
     uint16_t rres = 0;  // the residual, fetched while the row dot runs
     if (MODE == kModeResid && !stopped && lane == 0) rres = a.seg[seg].r[row];
-    if (!mbar_wait(&ring.full[s], (uint32_t)((i / ring.ns) & 1), a.err, kErrTimeoutFull)) break;
-    if (!stopped) {
+    live = live && mbar_wait(&ring.full[s], round_par, a.err, kErrTimeoutFull);
+    if (live && !stopped) {
       const uint32_t base = smem_u32(ring.buf + (size_t)s * ring.stage_bytes);
-      const float d = q8_row_dot<G, ORDER>(base + rowbytes * warp, nb, lane, xr);
+      const float d = q8_row_dot_xf<G, ORDER>(base + rowbytes * warp, nb, lane, xf);
       if (MODE == kModeSwiglu) {
-        const float u = q8_row_dot<G, ORDER>(base + rowbytes * (kTileRows + warp), nb, lane, xr);
+        const float u = q8_row_dot_xf<G, ORDER>(base + rowbytes * (kTileRows + warp), nb, lane, xf);
         if (lane == 0) a.seg[seg].y[row] = swiglu_h(f2h(d), f2h(u));
       } else if (MODE == kModeResid) {
         if (lane == 0) a.seg[seg].y[row] = f2h(__fadd_rn(h2f(rres), h2f(f2h(d))));
@@ -391,7 +500,9 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q8(const __grid_constant_
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&ring.empty[s]);
+    if (live && lane == 0) mbar_arrive(&ring.empty[s]);
+    if (++s == ring.ns) s = 0, round_par ^= 1u;
+    if ((r0 += kTileRows) == a.seg_rows) r0 = 0, ++seg;
   }
   if (a.advance != nullptr && !stopped && blockIdx.x == 0 && threadIdx.x == 0)
     a.advance->pos += 1;
