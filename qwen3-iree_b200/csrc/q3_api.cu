@@ -392,6 +392,15 @@ static int launch_q8_t(Q8GemvArgs a, cudaStream_t st, int* launches, bool pdl) {
   const uint32_t rowbytes = (uint32_t)(a.K / kQBlk) * kQBytes;
   const uint32_t tile_bytes = rowbytes * kTileRows * (MODE == kModeSwiglu ? 2u : 1u);
   const int ntiles = a.nseg * (a.seg_rows / kTileRows);
+  if (ntiles <= one_tile_threshold() * current_sms()) {
+    // one tile per CTA: weights converted to registers before the dependency wait
+    int rc = ensure_smem_attr(k_gemv_q8_1t<G, ORDER, MODE>, tile_bytes);
+    if (rc) return rc;
+    Q3_CUDA(launch_ex(k_gemv_q8_1t<G, ORDER, MODE>, dim3(ntiles > 0 ? ntiles : 1),
+                      dim3(kGemv1tThreads), (size_t)tile_bytes, st, pdl, a));
+    if (launches) ++*launches;
+    return Q3_OK;
+  }
   static size_t static_smem = 0;
   if (static_smem == 0) {
     cudaFuncAttributes fa;

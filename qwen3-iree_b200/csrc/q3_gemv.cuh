@@ -510,6 +510,219 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv_q8(const __grid_consta
 }
 
 // --------------------------------------------------------------------------
+// Q8_0 GEMV, one tile per CTA (the batch-1 decode launches)
+// --------------------------------------------------------------------------
+// Weights do not depend on the previous kernel, so each warp's row (rows:
+// gate and up with SwiGLU) lands and is converted to f32 registers before the
+// wait; after it only x (RMSNorm included) and the FMA chains remain.  Same
+// operations and orders as k_gemv_q8: the MLIR order keeps q_j and the block
+// scale apart, the CUDA order's scale * q_j is formed early (exact in f32).
+constexpr int kGemv1tThreads = 32 * kTileRows;  // one warp per row of the tile
+
+template <int G, int ORDER>
+__device__ __forceinline__ void q8_row_to_regs(uint32_t row, int nb, int lane, float (&q)[G][32],
+                                               float (&sc)[G]) {
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int b = lane + 32 * g;
+    if (b < nb) {
+      const Q8BlockWords bw = q8_load_block(row + (uint32_t)(kQBytes * b));
+      sc[g] = h2f((uint16_t)bw.scale16);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float f[4];
+        q8x4_to_f32(bw.q[i], f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          q[g][4 * i + j] = ORDER == kOrderMlir ? f[j] : __fmul_rn(sc[g], f[j]);
+      }
+    } else {
+      sc[g] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) q[g][j] = 0.0f;
+    }
+  }
+}
+
+template <int G, int ORDER>
+__device__ __forceinline__ float q8_regs_dot_xf(const float (&q)[G][32], const float (&sc)[G],
+                                                int nb, int lane, const float* xf) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int b = lane + 32 * g;
+    if (b < nb) {
+      const float4* xb = reinterpret_cast<const float4*>(xf + b * kXfStride);
+      if constexpr (ORDER == kOrderMlir) {
+        float inner = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 xv = xb[i];
+          inner = __fmaf_rn(q[g][4 * i + 0], xv.x, inner);
+          inner = __fmaf_rn(q[g][4 * i + 1], xv.y, inner);
+          inner = __fmaf_rn(q[g][4 * i + 2], xv.z, inner);
+          inner = __fmaf_rn(q[g][4 * i + 3], xv.w, inner);
+        }
+        acc = __fmaf_rn(sc[g], inner, acc);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 xv = xb[i];
+          acc = __fmaf_rn(q[g][4 * i + 0], xv.x, acc);
+          acc = __fmaf_rn(q[g][4 * i + 1], xv.y, acc);
+          acc = __fmaf_rn(q[g][4 * i + 2], xv.z, acc);
+          acc = __fmaf_rn(q[g][4 * i + 3], xv.w, acc);
+        }
+      }
+    }
+  }
+  return warp_sum(acc);
+}
+
+// The same row kept as exact half2 pairs (16 registers a block instead of 32),
+// widened to f32 after the wait: the SwiGLU kernel's up row.
+template <int G>
+__device__ __forceinline__ void q8_row_to_h2regs(uint32_t row, int nb, int lane,
+                                                 uint32_t (&h)[G][16], float (&sc)[G]) {
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int b = lane + 32 * g;
+    if (b < nb) {
+      const Q8BlockWords bw = q8_load_block(row + (uint32_t)(kQBytes * b));
+      sc[g] = h2f((uint16_t)bw.scale16);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q8x4_to_h2(bw.q[i], h[g][2 * i], h[g][2 * i + 1]);
+    } else {
+      sc[g] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) h[g][j] = 0u;
+    }
+  }
+}
+
+template <int G, int ORDER>
+__device__ __forceinline__ float q8_h2regs_dot_xf(const uint32_t (&h)[G][16], const float (&sc)[G],
+                                                  int nb, int lane, const float* xf) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int b = lane + 32 * g;
+    if (b < nb) {
+      const float4* xb = reinterpret_cast<const float4*>(xf + b * kXfStride);
+      float inner = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 xv = xb[i];
+        const float xs4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t w = h[g][2 * i + (j >> 1)];
+          const float qj = h2f((uint16_t)((j & 1) ? (w >> 16) : (w & 0xffffu)));
+          if constexpr (ORDER == kOrderMlir)
+            inner = __fmaf_rn(qj, xs4[j], inner);
+          else
+            acc = __fmaf_rn(__fmul_rn(sc[g], qj), xs4[j], acc);
+        }
+      }
+      if constexpr (ORDER == kOrderMlir) acc = __fmaf_rn(sc[g], inner, acc);
+    }
+  }
+  return warp_sum(acc);
+}
+
+// Blocks per SM the launch must keep resident: 512 QKV tiles need 4, 384
+// gate/up tiles 3; the K = 2048 / 3072 launches have 128 tiles.
+template <int G, int MODE>
+constexpr int gemv1t_min_blocks() {
+  return G > 1 ? 1 : (MODE == kModeSwiglu ? 3 : 4);
+}
+
+template <int G, int ORDER, int MODE>
+__global__ void __launch_bounds__(kGemv1tThreads, gemv1t_min_blocks<G, MODE>())
+    k_gemv_q8_1t(const __grid_constant__ Q8GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];  // the tile (gate tile, then up tile)
+  __shared__ __align__(8) uint64_t full;
+  __shared__ __align__(16) float xf[G * 32 * kXfStride];
+  __shared__ float rs;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = a.K / kQBlk;
+  const uint32_t rowbytes = (uint32_t)(nb * kQBytes);
+  const uint32_t tile_bytes = rowbytes * kTileRows * (MODE == kModeSwiglu ? 2u : 1u);
+  const int tiles_per_seg = a.seg_rows / kTileRows;
+  const int seg = blockIdx.x / tiles_per_seg;
+  const int r0 = (blockIdx.x % tiles_per_seg) * kTileRows;
+  ktrace_start(a.trace);
+  if (threadIdx.x == 0) {
+    mbar_init(&full, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    const uint64_t pol = l2_policy_evict_first();
+    const uint8_t* src = a.seg[seg].w + (int64_t)r0 * rowbytes;
+    mbar_expect_tx(&full, tile_bytes);
+    bulk_g2s(smem, src, rowbytes * kTileRows, &full, pol);
+    if (MODE == kModeSwiglu)
+      bulk_g2s(smem + rowbytes * kTileRows, src + a.up_off_bytes, rowbytes * kTileRows, &full, pol);
+  }
+  // The decode state (stop, pos, tokens) changes only in a step's last
+  // kernel, and gamma never: read them before waiting for the previous kernel.
+  const bool stopped = a.seq != nullptr && a.seq->stop != 0;
+  constexpr bool kNorm = MODE == kModeNormIn || MODE == kModeSwiglu;
+  uint16_t gr[G * 4];
+  const uint16_t* xin = a.seg[seg].x;
+  if (kNorm && !stopped) {
+    load_gamma_regs<G * 1024>(a.norm_g, a.K, gr);
+    if (a.tokens != nullptr) {
+      int64_t tok = a.tokens[a.seq->pos];
+      if (tok < 0 || tok >= kVocab) {
+        if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
+        tok = 0;
+      }
+      xin = a.embd + tok * (int64_t)kDim;
+    }
+  }
+  float q[G][32], sc[G];
+  uint32_t qu[MODE == kModeSwiglu ? G : 1][16];
+  float scu[MODE == kModeSwiglu ? G : 1];
+  const bool landed = mbar_wait_own(&full, 0u, a.err, kErrTimeoutFull);
+  if (landed && !stopped) {
+    q8_row_to_regs<G, ORDER>(smem_u32(smem) + rowbytes * warp, nb, lane, q, sc);
+    if constexpr (MODE == kModeSwiglu)
+      q8_row_to_h2regs<G>(smem_u32(smem) + rowbytes * (kTileRows + warp), nb, lane, qu, scu);
+  }
+  // one decision for the whole CTA: the barriers below need every thread
+  const bool work = __syncthreads_and(landed && !stopped) != 0;
+  pdl_wait();  // the previous kernel's outputs (activations) are visible
+  ktrace_release(a.trace);
+  if (work) {
+    if (kNorm) {
+      if (a.tokens != nullptr && blockIdx.x == 0 && warp == 0 && a.embed_out != nullptr)
+        for (int k = lane; k < a.K; k += 32) a.embed_out[k] = xin[k];
+      cta_rmsnorm_to_xf<G * 1024>(xin, gr, a.K, xf, &rs);
+    } else {
+      stage_x_f32(xin, a.K, xf);
+    }
+    const int row = r0 + warp;
+    uint16_t rres = 0;
+    if (MODE == kModeResid && lane == 0) rres = a.seg[seg].r[row];
+    const float d = q8_regs_dot_xf<G, ORDER>(q, sc, nb, lane, xf);
+    if constexpr (MODE == kModeSwiglu) {
+      const float u = q8_h2regs_dot_xf<G, ORDER>(qu, scu, nb, lane, xf);
+      if (lane == 0) a.seg[seg].y[row] = swiglu_h(f2h(d), f2h(u));
+    } else if (MODE == kModeResid) {
+      if (lane == 0) a.seg[seg].y[row] = f2h(__fadd_rn(h2f(rres), h2f(f2h(d))));
+    } else {
+      if (lane == 0) a.seg[seg].y[row] = f2h(d);
+    }
+  }
+  if (a.advance != nullptr && !stopped && blockIdx.x == 0 && threadIdx.x == 0)
+    a.advance->pos += 1;
+  ktrace_end(a.trace);
+}
+
+// --------------------------------------------------------------------------
 // f16 vocab GEMV + argmax
 // --------------------------------------------------------------------------
 struct ArgmaxPartial {
