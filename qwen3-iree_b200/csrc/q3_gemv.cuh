@@ -253,35 +253,50 @@ constexpr int kXfStride = 36;
 
 __device__ __forceinline__ int xf_index(int k) { return (k >> 5) * kXfStride + (k & 31); }
 
-// x (f16, K a multiple of 8, 16-byte aligned) -> xf by the 256 consumer
-// threads; ends with a consumer barrier.
-__device__ __forceinline__ void stage_x_f32(const uint16_t* x, int K, float* xf) {
+// The f16 copy for rows kept as half2: block b's 32 values at halves
+// [40 b, 40 b + 32) (80 bytes a block), read as 4 uint4 per lane; at uint4 i
+// that is bank group (5 b + i) mod 8, again distinct across a quarter warp.
+constexpr int kXhStride = 40;
+
+__device__ __forceinline__ int xh_index(int k) { return (k >> 5) * kXhStride + (k & 31); }
+
+// x (f16, K a multiple of 8, 16-byte aligned) -> xf (F32) and/or xh (F16) by
+// the 256 consumer threads; ends with a consumer barrier.
+template <bool F32, bool F16>
+__device__ __forceinline__ void stage_x(const uint16_t* x, int K, float* xf, uint16_t* xh) {
   for (int i = threadIdx.x; i < K / 8; i += 256) {
     const uint4 v = reinterpret_cast<const uint4*>(x)[i];
-    float* d = xf + xf_index(8 * i);
-    *reinterpret_cast<float4*>(d) =
-        make_float4(h2f((uint16_t)(v.x & 0xffffu)), h2f((uint16_t)(v.x >> 16)),
-                    h2f((uint16_t)(v.y & 0xffffu)), h2f((uint16_t)(v.y >> 16)));
-    *reinterpret_cast<float4*>(d + 4) =
-        make_float4(h2f((uint16_t)(v.z & 0xffffu)), h2f((uint16_t)(v.z >> 16)),
-                    h2f((uint16_t)(v.w & 0xffffu)), h2f((uint16_t)(v.w >> 16)));
+    if constexpr (F32) {
+      float* d = xf + xf_index(8 * i);
+      *reinterpret_cast<float4*>(d) =
+          make_float4(h2f((uint16_t)(v.x & 0xffffu)), h2f((uint16_t)(v.x >> 16)),
+                      h2f((uint16_t)(v.y & 0xffffu)), h2f((uint16_t)(v.y >> 16)));
+      *reinterpret_cast<float4*>(d + 4) =
+          make_float4(h2f((uint16_t)(v.z & 0xffffu)), h2f((uint16_t)(v.z >> 16)),
+                      h2f((uint16_t)(v.w & 0xffffu)), h2f((uint16_t)(v.w >> 16)));
+    }
+    if constexpr (F16) *reinterpret_cast<uint4*>(xh + xh_index(8 * i)) = v;
   }
   consumer_sync();
 }
 
-// RMSNorm into xf: the same operations and order as cta_rmsnorm_to_smem_g
-// (sum of squares in warp 0's lane-strided order, x_k / r * g_k rounded to
-// f16), with the normalised f16 values stored as f32.
-template <int KMAX>
-__device__ __forceinline__ void cta_rmsnorm_to_xf(const uint16_t* x,
-                                                  const uint16_t (&gr)[KMAX / 256], int K,
-                                                  float* xf, float* rs) {
+__device__ __forceinline__ void stage_x_f32(const uint16_t* x, int K, float* xf) {
+  stage_x<true, false>(x, K, xf, nullptr);
+}
+
+// RMSNorm into xf and/or xh: the same operations and order as
+// cta_rmsnorm_to_smem_g (sum of squares in warp 0's lane-strided order,
+// x_k / r * g_k rounded to f16), the normalised values stored as f32 / f16.
+template <int KMAX, bool F32, bool F16>
+__device__ __forceinline__ void cta_rmsnorm_to_x(const uint16_t* x,
+                                                 const uint16_t (&gr)[KMAX / 256], int K,
+                                                 float* xf, uint16_t* xh, float* rs) {
   const int tid = threadIdx.x;
-  stage_x_f32(x, K, xf);
+  stage_x<F32, F16>(x, K, xf, xh);
   if (tid < 32) {
     float ss = 0.0f;
     for (int k = tid; k < K; k += 32) {
-      const float v = xf[xf_index(k)];
+      const float v = F32 ? xf[xf_index(k)] : h2f(xh[xh_index(k)]);
       ss = __fmaf_rn(v, v, ss);
     }
     ss = warp_sum(ss);
@@ -293,11 +308,20 @@ __device__ __forceinline__ void cta_rmsnorm_to_xf(const uint16_t* x,
   for (int i = 0; i < KMAX / 256; ++i) {
     const int k = tid + 256 * i;
     if (k < K) {
-      float* p = xf + xf_index(k);
-      *p = h2f(f2h(__fmul_rn(__fdiv_rn(*p, r), h2f(gr[i]))));
+      const float v = F32 ? xf[xf_index(k)] : h2f(xh[xh_index(k)]);
+      const uint16_t nh = f2h(__fmul_rn(__fdiv_rn(v, r), h2f(gr[i])));
+      if constexpr (F32) xf[xf_index(k)] = h2f(nh);
+      if constexpr (F16) xh[xh_index(k)] = nh;
     }
   }
   consumer_sync();
+}
+
+template <int KMAX>
+__device__ __forceinline__ void cta_rmsnorm_to_xf(const uint16_t* x,
+                                                  const uint16_t (&gr)[KMAX / 256], int K,
+                                                  float* xf, float* rs) {
+  cta_rmsnorm_to_x<KMAX, true, false>(x, gr, K, xf, nullptr, rs);
 }
 
 // Dot of one Q8_0 row (shared byte address `row`) with x staged in xf, in
@@ -513,10 +537,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv_q8(const __grid_consta
 // Q8_0 GEMV, one tile per CTA (the batch-1 decode launches)
 // --------------------------------------------------------------------------
 // Weights do not depend on the previous kernel, so each warp's row (rows:
-// gate and up with SwiGLU) lands and is converted to f32 registers before the
-// wait; after it only x (RMSNorm included) and the FMA chains remain.  Same
-// operations and orders as k_gemv_q8: the MLIR order keeps q_j and the block
-// scale apart, the CUDA order's scale * q_j is formed early (exact in f32).
+// gate and up with SwiGLU) lands and is converted to registers -- exact half2
+// in the MLIR order, f32 scale * q_j in the CUDA order -- before the wait;
+// after it only x (RMSNorm included) and the FMA chains remain.  Same
+// operations and orders as k_gemv_q8.
 constexpr int kGemv1tThreads = 32 * kTileRows;  // one warp per row of the tile
 
 template <int G, int ORDER>
@@ -600,49 +624,58 @@ __device__ __forceinline__ void q8_row_to_h2regs(uint32_t row, int nb, int lane,
   }
 }
 
-template <int G, int ORDER>
-__device__ __forceinline__ float q8_h2regs_dot_xf(const uint32_t (&h)[G][16], const float (&sc)[G],
-                                                  int nb, int lane, const float* xf) {
+// Dot of a half2-held row with the f16 copy of x in the MLIR order: the
+// inner chain of q_j * x_j (f16 operands, f32 accumulate, one rounding each,
+// the same as widening both first), then acc = fma(scale, inner, acc).
+template <int G>
+__device__ __forceinline__ float q8_h2regs_dot_xh(const uint32_t (&h)[G][16], const float (&sc)[G],
+                                                  int nb, int lane, const uint16_t* xh) {
   float acc = 0.0f;
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const int b = lane + 32 * g;
     if (b < nb) {
-      const float4* xb = reinterpret_cast<const float4*>(xf + b * kXfStride);
+      const uint4* xb = reinterpret_cast<const uint4*>(xh + b * kXhStride);
       float inner = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 xv = xb[i];
-        const float xs4[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t w = h[g][2 * i + (j >> 1)];
-          const float qj = h2f((uint16_t)((j & 1) ? (w >> 16) : (w & 0xffffu)));
-          if constexpr (ORDER == kOrderMlir)
-            inner = __fmaf_rn(qj, xs4[j], inner);
-          else
-            acc = __fmaf_rn(__fmul_rn(sc[g], qj), xs4[j], acc);
-        }
+      for (int i = 0; i < 4; ++i) {
+        const uint4 xv = xb[i];
+        inner = fma_h2(h[g][4 * i + 0], xv.x, inner);
+        inner = fma_h2(h[g][4 * i + 1], xv.y, inner);
+        inner = fma_h2(h[g][4 * i + 2], xv.z, inner);
+        inner = fma_h2(h[g][4 * i + 3], xv.w, inner);
       }
-      if constexpr (ORDER == kOrderMlir) acc = __fmaf_rn(sc[g], inner, acc);
+      acc = __fmaf_rn(sc[g], inner, acc);
     }
   }
   return warp_sum(acc);
 }
 
-// Blocks per SM the launch must keep resident: 512 QKV tiles need 4, 384
-// gate/up tiles 3; the K = 2048 / 3072 launches have 128 tiles.
+// Blocks per SM, which caps the registers: 512 QKV tiles need 4 resident,
+// 384 gate/up tiles 3; the K = 2048 / 3072 launches (128 tiles) take 3 so
+// that the next kernel's CTAs fit beside them (measured: 515 us per traced
+// step against 521 with 2 and 529 with 5 / 4 / 3).
 template <int G, int MODE>
 constexpr int gemv1t_min_blocks() {
-  return G > 1 ? 1 : (MODE == kModeSwiglu ? 3 : 4);
+  return G > 1 ? 3 : (MODE == kModeSwiglu ? 3 : 4);
 }
 
 template <int G, int ORDER, int MODE>
 __global__ void __launch_bounds__(kGemv1tThreads, gemv1t_min_blocks<G, MODE>())
     k_gemv_q8_1t(const __grid_constant__ Q8GemvArgs a) {
+  static_assert(ORDER == kOrderMlir || MODE != kModeSwiglu, "SwiGLU runs in the MLIR order");
+  // Rows are held as exact half2 and multiplied with an f16 copy of x by the
+  // mixed-precision FMA: half the registers of f32 rows, so every CTA of a
+  // launch, and the next launch's, can be resident before the release, and
+  // the f16-operand FMA runs faster here than widening either operand first.
+  // The CUDA order (scale * q_j formed first) keeps f32 rows and an f32 x.
+  constexpr bool kH2 = ORDER == kOrderMlir;
+  constexpr bool kXf = !kH2;
+  constexpr bool kXh = kH2 || MODE == kModeSwiglu;
   extern __shared__ __align__(128) uint8_t smem[];  // the tile (gate tile, then up tile)
   __shared__ __align__(8) uint64_t full;
-  __shared__ __align__(16) float xf[G * 32 * kXfStride];
+  __shared__ __align__(16) float xf[kXf ? G * 32 * kXfStride : 4];
+  __shared__ __align__(16) uint16_t xh[kXh ? G * 32 * kXhStride : 8];
   __shared__ float rs;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = a.K / kQBlk;
@@ -683,12 +716,16 @@ __global__ void __launch_bounds__(kGemv1tThreads, gemv1t_min_blocks<G, MODE>())
       xin = a.embd + tok * (int64_t)kDim;
     }
   }
-  float q[G][32], sc[G];
+  float q[kH2 ? 1 : G][32], sc[G];
+  uint32_t qh[kH2 ? G : 1][16];
   uint32_t qu[MODE == kModeSwiglu ? G : 1][16];
   float scu[MODE == kModeSwiglu ? G : 1];
   const bool landed = mbar_wait_own(&full, 0u, a.err, kErrTimeoutFull);
   if (landed && !stopped) {
-    q8_row_to_regs<G, ORDER>(smem_u32(smem) + rowbytes * warp, nb, lane, q, sc);
+    if constexpr (kH2)
+      q8_row_to_h2regs<G>(smem_u32(smem) + rowbytes * warp, nb, lane, qh, sc);
+    else
+      q8_row_to_regs<G, ORDER>(smem_u32(smem) + rowbytes * warp, nb, lane, q, sc);
     if constexpr (MODE == kModeSwiglu)
       q8_row_to_h2regs<G>(smem_u32(smem) + rowbytes * (kTileRows + warp), nb, lane, qu, scu);
   }
@@ -700,16 +737,20 @@ __global__ void __launch_bounds__(kGemv1tThreads, gemv1t_min_blocks<G, MODE>())
     if (kNorm) {
       if (a.tokens != nullptr && blockIdx.x == 0 && warp == 0 && a.embed_out != nullptr)
         for (int k = lane; k < a.K; k += 32) a.embed_out[k] = xin[k];
-      cta_rmsnorm_to_xf<G * 1024>(xin, gr, a.K, xf, &rs);
+      cta_rmsnorm_to_x<G * 1024, kXf, kXh>(xin, gr, a.K, xf, xh, &rs);
     } else {
-      stage_x_f32(xin, a.K, xf);
+      stage_x<kXf, kXh>(xin, a.K, xf, xh);
     }
     const int row = r0 + warp;
     uint16_t rres = 0;
     if (MODE == kModeResid && lane == 0) rres = a.seg[seg].r[row];
-    const float d = q8_regs_dot_xf<G, ORDER>(q, sc, nb, lane, xf);
+    float d;
+    if constexpr (kH2)
+      d = q8_h2regs_dot_xh<G>(qh, sc, nb, lane, xh);
+    else
+      d = q8_regs_dot_xf<G, ORDER>(q, sc, nb, lane, xf);
     if constexpr (MODE == kModeSwiglu) {
-      const float u = q8_h2regs_dot_xf<G, ORDER>(qu, scu, nb, lane, xf);
+      const float u = q8_h2regs_dot_xh<G>(qu, scu, nb, lane, xh);
       if (lane == 0) a.seg[seg].y[row] = swiglu_h(f2h(d), f2h(u));
     } else if (MODE == kModeResid) {
       if (lane == 0) a.seg[seg].y[row] = f2h(__fadd_rn(h2f(rres), h2f(f2h(d))));
