@@ -78,6 +78,7 @@ struct AttnSmem {
   AttnPartial part[kAttSplitChunks][2];  // this CTA's chunk partials when it holds every chunk
   uint16_t qs[2][kHD];
   uint16_t ks[kHD];
+  float2 pw[kAttSplitChunks][kAttChunk];  // each warp's softmax weights, both q heads
   int last;
 };
 
@@ -212,6 +213,12 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
   }
   uint2 nv = make_uint2(0u, 0u);  // the new V row's dims 4 lane .. 4 lane + 3
   if (tp >= 0) nv = __ldcg(reinterpret_cast<const uint2*>(c.qkv + 3072 + h * kHD + 4 * lane));
+  // the new V row for the cache write of step 2, fetched now so that its
+  // latency overlaps the norms instead of delaying warps 0-3 after them
+  const bool writes_row = g == ngroups - 1 && threadIdx.x < kHD;
+  unsigned short vrow = 0;
+  if (writes_row)
+    vrow = __ldcg(reinterpret_cast<const unsigned short*>(c.qkv) + 3072 + h * kHD + threadIdx.x);
 
   // 1) q heads 2h, 2h+1 and k head h: norm + rope into shared memory
   if (warp < 3) {
@@ -223,10 +230,10 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
   consumer_sync();
   // 2) the group holding key pos writes the new K (normed, roped) and V rows,
   //    and the warp holding it takes them from here instead of its stale loads
-  if (g == ngroups - 1 && threadIdx.x < kHD) {
+  if (writes_row) {
     const int64_t off = (c.slot0 + pos) * rowel + h * kHD + threadIdx.x;
     c.kc[off] = sm.ks[threadIdx.x];
-    c.vc[off] = __ldcg(reinterpret_cast<const unsigned short*>(c.qkv) + 3072 + h * kHD + threadIdx.x);
+    c.vc[off] = vrow;
   }
   if (!EARLY && have) load_chunk();
   if (lane == tp) {
@@ -259,28 +266,31 @@ __device__ __forceinline__ void attn_group(const AttnCtx& c, int h, int g, AttnS
     float m[2], p[2], l[2];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
-      m[hh] = warp_max(s[hh]);
+      m[hh] = warp_max_redux(s[hh]);
       p[hh] = valid ? q3_expf(__fsub_rn(s[hh], m[hh])) : 0.0f;
       l[hh] = warp_sum(p[hh]);
     }
+    // p.v, lane = 4 head dims, keys in order.  The weights go through shared
+    // memory (one broadcast load per key instead of two shuffles) and the
+    // loop has no branch, so its loads issue ahead of the FMA chains; keys
+    // past the chunk's end have p = 0 and V = 0 and add an exact +0.
+    sm.pw[warp][lane] = make_float2(p[0], p[1]);
+    __syncwarp();
     float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int tt = 0; tt < kAttChunk; ++tt) {
-      const float p0 = __shfl_sync(0xffffffffu, p[0], tt);
-      const float p1 = __shfl_sync(0xffffffffu, p[1], tt);
-      if (tt < nvalid) {
-        const uint2 vt = tt == tp ? nv : vv[tt];
-        const float v0 = h2f((uint16_t)(vt.x & 0xffffu)), v1 = h2f((uint16_t)(vt.x >> 16));
-        const float v2 = h2f((uint16_t)(vt.y & 0xffffu)), v3 = h2f((uint16_t)(vt.y >> 16));
-        o0[0] = __fmaf_rn(p0, v0, o0[0]);
-        o0[1] = __fmaf_rn(p0, v1, o0[1]);
-        o0[2] = __fmaf_rn(p0, v2, o0[2]);
-        o0[3] = __fmaf_rn(p0, v3, o0[3]);
-        o1[0] = __fmaf_rn(p1, v0, o1[0]);
-        o1[1] = __fmaf_rn(p1, v1, o1[1]);
-        o1[2] = __fmaf_rn(p1, v2, o1[2]);
-        o1[3] = __fmaf_rn(p1, v3, o1[3]);
-      }
+      const float2 pp = sm.pw[warp][tt];
+      const uint2 vt = tt == tp ? nv : vv[tt];
+      const float v0 = h2f((uint16_t)(vt.x & 0xffffu)), v1 = h2f((uint16_t)(vt.x >> 16));
+      const float v2 = h2f((uint16_t)(vt.y & 0xffffu)), v3 = h2f((uint16_t)(vt.y >> 16));
+      o0[0] = __fmaf_rn(pp.x, v0, o0[0]);
+      o0[1] = __fmaf_rn(pp.x, v1, o0[1]);
+      o0[2] = __fmaf_rn(pp.x, v2, o0[2]);
+      o0[3] = __fmaf_rn(pp.x, v3, o0[3]);
+      o1[0] = __fmaf_rn(pp.y, v0, o1[0]);
+      o1[1] = __fmaf_rn(pp.y, v1, o1[1]);
+      o1[2] = __fmaf_rn(pp.y, v2, o1[2]);
+      o1[3] = __fmaf_rn(pp.y, v3, o1[3]);
     }
     AttnPartial* gp = sm.part[warp];
     if (lane == 0) {

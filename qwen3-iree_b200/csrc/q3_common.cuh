@@ -116,6 +116,17 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// The same maximum (NaN-free inputs) in one redux.sync on order-preserving
+// keys: negative floats map to their complement, others get the sign bit set.
+// A max is exact, so only the sign of a zero result can differ from
+// warp_max, and a zero's sign does not survive the differences it enters.
+__device__ __forceinline__ float warp_max_redux(float v) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  const uint32_t m = __reduce_max_sync(0xffffffffu, key);
+  return __uint_as_float((m & 0x80000000u) ? (m & 0x7fffffffu) : ~m);
+}
+
 // f16 SwiGLU of model/qwen3_full.mlir:829-839, every op rounded to f16.
 __device__ __forceinline__ uint16_t swiglu_h(uint16_t gate, uint16_t up) {
   const float g = h2f(gate);
