@@ -819,6 +819,23 @@ static int probe_mark(const StepProbe* pr, cudaStream_t st, int kind) {
     if (rc_) return rc_;                        \
   } while (0)
 
+// Each Q8_0 launch of a step prefetches the next Q8_0 launch's weights into
+// L2 (Q3_GEMV_L2_PREFETCH=0 turns it off, for measurement).
+static bool gemv_l2_prefetch() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("Q3_GEMV_L2_PREFETCH");
+    v = (e && atoi(e) == 0) ? 0 : 1;
+  }
+  return v != 0;
+}
+
+static void set_prefetch(Q8GemvArgs& a, int r, const void* p, int64_t bytes) {
+  if (!gemv_l2_prefetch()) return;
+  a.pf_ptr[r] = (const uint8_t*)p;
+  a.pf_bytes[r] = (uint32_t)bytes;
+}
+
 static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepProbe* probe) {
   cudaStream_t st = m->stream;
   const int32_t* stop = &m->st->stop;
@@ -846,6 +863,7 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
       a.embed_out = m->x;
     }
     a.trace = probe_trace(probe, Q3_KIND_QKV);
+    set_prefetch(a, 0, (const uint8_t*)m->w.q8_attn_output + l * kBplO, kBplO);
     int rc = launch_q8<kOrderMlir, kModeNormIn>(a, st, launches, true);
     if (rc) return rc;
     Q3_PROBE(Q3_KIND_QKV);
@@ -880,6 +898,7 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
     a.seq = m->st;
     a.err = m->err;
     a.trace = probe_trace(probe, Q3_KIND_O);
+    set_prefetch(a, 0, (const uint8_t*)m->w.q8_ffn_gate_up + l * kBplGU, kBplGU);
     rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches, true);
     if (rc) return rc;
     Q3_PROBE(Q3_KIND_O);
@@ -891,6 +910,7 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
     a.seq = m->st;
     a.err = m->err;
     a.trace = probe_trace(probe, Q3_KIND_GATE_UP);
+    set_prefetch(a, 0, (const uint8_t*)m->w.q8_ffn_down + l * kBplD, kBplD);
     rc = launch_q8<kOrderMlir, kModeSwiglu>(a, st, launches, true);
     if (rc) return rc;
     Q3_PROBE(Q3_KIND_GATE_UP);
@@ -901,6 +921,11 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
     a.err = m->err;
     if (ingest && l == kLayers - 1) a.advance = m->st;
     a.trace = probe_trace(probe, Q3_KIND_DOWN);
+    if (l + 1 < kLayers) {
+      set_prefetch(a, 0, (const uint8_t*)m->w.q8_attn_q + (l + 1) * kBplQ, kBplQ);
+      set_prefetch(a, 1, (const uint8_t*)m->w.q8_attn_k + (l + 1) * kBplKV, kBplKV);
+      set_prefetch(a, 2, (const uint8_t*)m->w.q8_attn_v + (l + 1) * kBplKV, kBplKV);
+    }
     rc = launch_q8<kOrderMlir, kModeResid>(a, st, launches, true);
     if (rc) return rc;
     Q3_PROBE(Q3_KIND_DOWN);

@@ -65,7 +65,25 @@ struct Q8GemvArgs {
   int* err;
   int nstages;
   unsigned long long* trace;  // optional launch timing record (4 values)
+  // Optional L2 prefetch of the next launch's weights (up to 3 ranges, 16-byte
+  // aligned, sizes multiples of 16), split across this launch's CTAs and issued
+  // before the dependency wait, so that next launch's late-starting CTAs find
+  // their tiles in L2.
+  const uint8_t* pf_ptr[3];
+  uint32_t pf_bytes[3];
 };
+
+// This CTA's share of the L2 prefetch ranges.
+__device__ __forceinline__ void q8_prefetch_next(const Q8GemvArgs& a) {
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const uint32_t n = a.pf_bytes[r];
+    if (n == 0) continue;
+    const uint32_t share = ((n + gridDim.x - 1) / gridDim.x + 15u) & ~15u;
+    const uint32_t off = blockIdx.x * share;
+    if (off < n) bulk_prefetch_l2(a.pf_ptr[r] + off, n - off < share ? n - off : share);
+  }
+}
 
 // --------------------------------------------------------------------------
 // Input slices in registers
@@ -698,6 +716,7 @@ __global__ void __launch_bounds__(kGemv1tThreads, gemv1t_min_blocks<G, MODE>())
     bulk_g2s(smem, src, rowbytes * kTileRows, &full, pol);
     if (MODE == kModeSwiglu)
       bulk_g2s(smem + rowbytes * kTileRows, src + a.up_off_bytes, rowbytes * kTileRows, &full, pol);
+    q8_prefetch_next(a);
   }
   // The decode state (stop, pos, tokens) changes only in a step's last
   // kernel, and gamma never: read them before waiting for the previous kernel.
