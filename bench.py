@@ -524,39 +524,15 @@ def measure_batched(q3b200, dw, d: Dist, key: str, seed: int, peak: float, warmu
 
 
 def measure_gemv_stream(q3b200, dw, peak: float) -> dict:
-    """Each projection over all 28 layers in ONE launch (q3_gemv_q8_layers):
-    the streaming bandwidth of the GEMV kernel without launch gaps.  L2 is
-    flushed (a 256 MB write) before every timed launch, so the 62 MB pools of
-    attn_q and attn_o are read from HBM like the larger ones."""
-    L = q3b200.lib()
+    """Each projection over all 28 layers in ONE launch, L2 flushed before
+    every timed launch (q3b200.benchmark.gemv_stream)."""
+    from q3b200.benchmark import GEMV_STREAM_SHAPES, gemv_stream
+
     out = {}
-    flush = q3b200.DeviceArray((256 << 20,), np.uint8)
-    shapes = [("attn_q", "stacked.q8.attn_q.weight", 2048, 1024),
-              ("attn_o", "stacked.q8.attn_output.weight", 1024, 2048),
-              ("gate_up", "stacked.q8.ffn_gate_up.weight", 6144, 1024),
-              ("down", "stacked.q8.ffn_down.weight", 1024, 3072)]
-    ev = q3b200.Events()
-    for name, key, N, K in shapes:
-        w = dw.buffers[key]
-        bpl = N * (K // 32) * 34
-        x = q3b200.DeviceArray.from_host(
-            np.random.default_rng(1).standard_normal((28, K)).astype(np.float16))
-        y = q3b200.DeviceArray((28, N), np.float16)
-        for _ in range(3):
-            assert L.q3_gemv_q8_layers(w.ptr, bpl, x.ptr, y.ptr, N, K, 28, None) == 0
-        reps = 20
-        total_ms = 0.0
-        for r in range(reps):
-            flush.fill_bytes(r & 0xFF)
-            ev.record_start(None)
-            assert L.q3_gemv_q8_layers(w.ptr, bpl, x.ptr, y.ptr, N, K, 28, None) == 0
-            ev.record_end(None)
-            total_ms += ev.elapsed_ms()
-        us = total_ms * 1e3 / reps
-        b = 28 * (bpl + 2 * K + 2 * N)
-        out[name] = {"us_per_launch": us, "bytes": b, "gbs": b / (us * 1e-6) / 1e9,
-                     "frac_of_measured": b / (us * 1e-6) / 1e9 / peak, "l2": "flushed"}
-    flush.free()
+    for name in GEMV_STREAM_SHAPES:
+        r = gemv_stream(dw, name)
+        r["frac_of_measured"] = r["gbs"] / peak
+        out[name] = r
     return out
 
 

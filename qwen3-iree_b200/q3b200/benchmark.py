@@ -16,6 +16,9 @@ token-id lists -- seeded ones by default, one line of ids per prompt with
 
   python -m q3b200.benchmark [--max-tokens 128] [--json out.json]
   python -m q3b200.benchmark --batch 32 --context 128 2048 --steps 128
+  python -m q3b200.benchmark --num-prompts 1 --prompt-len 1 --max-tokens 3 --no-warmup
+      (the smallest whole decode: 4 steps of 141 launches, for profilers)
+  python -m q3b200.benchmark --gemv-stream gate_up   (GEMV HBM GB/s, 28 layers a launch)
 """
 from __future__ import annotations
 
@@ -39,11 +42,11 @@ def trim_eos(tokens, eos: int = EOS_TOKEN) -> list[int]:
     return tokens[:tokens.index(eos)] if eos in tokens else tokens
 
 
-def synthetic_prompts(n: int = 10, seed: int = 0) -> list[list[int]]:
-    """n seeded token-id prompts of increasing length (12..48 ids, the range
-    of short chat-formatted questions)."""
+def synthetic_prompts(n: int = 10, seed: int = 0, length: int = 0) -> list[list[int]]:
+    """n seeded token-id prompts: of increasing length (12..48 ids, the range
+    of short chat-formatted questions), or all `length` ids long."""
     rng = np.random.default_rng(seed)
-    lengths = np.linspace(12, 48, n).astype(int)
+    lengths = [length] * n if length > 0 else np.linspace(12, 48, n).astype(int)
     return [rng.integers(0, VOCAB, size=int(L)).tolist() for L in lengths]
 
 
@@ -108,6 +111,45 @@ def bench_batched(dw, B: int, lo: int, hi: int, steps: int, seed: int = 0) -> di
             "tok_s": B * steps / (ms / 1e3)}
 
 
+GEMV_STREAM_SHAPES = {  # projection: (stacked parameter, N, K)
+    "attn_q": ("stacked.q8.attn_q.weight", 2048, 1024),
+    "attn_o": ("stacked.q8.attn_output.weight", 1024, 2048),
+    "gate_up": ("stacked.q8.ffn_gate_up.weight", 6144, 1024),
+    "down": ("stacked.q8.ffn_down.weight", 1024, 3072),
+}
+
+
+def gemv_stream(dw, name: str, reps: int = 20, warmup: int = 3) -> dict:
+    """One projection over all 28 layers in ONE launch (q3_gemv_q8_layers):
+    the streaming bandwidth of the Q8_0 GEMV without launch gaps.  L2 is
+    flushed (a 256 MB write) before every timed launch, so the 62 MB pools
+    of attn_q and attn_o are read from HBM like the larger ones."""
+    from . import DeviceArray, Events
+    from ._lib import lib
+
+    key, N, K = GEMV_STREAM_SHAPES[name]
+    L = lib()
+    w = dw.buffers[key]
+    bpl = N * (K // 32) * 34
+    x = DeviceArray.from_host(np.random.default_rng(1).standard_normal((28, K)).astype(np.float16))
+    y = DeviceArray((28, N), np.float16)
+    flush = DeviceArray((256 << 20,), np.uint8)
+    ev = Events()
+    for _ in range(warmup):
+        assert L.q3_gemv_q8_layers(w.ptr, bpl, x.ptr, y.ptr, N, K, 28, None) == 0
+    total_ms = 0.0
+    for r in range(reps):
+        flush.fill_bytes(r & 0xFF)
+        ev.record_start(None)
+        assert L.q3_gemv_q8_layers(w.ptr, bpl, x.ptr, y.ptr, N, K, 28, None) == 0
+        ev.record_end(None)
+        total_ms += ev.elapsed_ms()
+    flush.free()
+    us = total_ms * 1e3 / reps
+    b = 28 * (bpl + 2 * K + 2 * N)
+    return {"us_per_launch": us, "bytes": b, "gbs": b / (us * 1e-6) / 1e9, "l2": "flushed"}
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description="Benchmark Qwen3-0.6B Q8_0 decode on libq3b200.so")
     ap.add_argument("--max-tokens", type=int, default=MAX_TOKENS)
@@ -123,12 +165,27 @@ def main(argv=None) -> int:
     ap.add_argument("--context", type=int, nargs=2, default=[128, 2048], metavar=("LO", "HI"))
     ap.add_argument("--steps", type=int, default=128, help="batched mode: decode steps")
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--num-prompts", type=int, default=10, help="synthetic prompts")
+    ap.add_argument("--prompt-len", type=int, default=0, help="synthetic prompt length (0: 12..48)")
+    ap.add_argument("--no-warmup", action="store_true", help="skip the untimed first call")
+    ap.add_argument("--gemv-stream", choices=sorted(GEMV_STREAM_SHAPES), default=None,
+                    help="time one projection over all 28 layers per launch")
+    ap.add_argument("--reps", type=int, default=20, help="with --gemv-stream: timed launches")
     args = ap.parse_args(argv)
 
     from . import DeviceWeights, Qwen3Decoder, set_device
 
     set_device(args.device)
     dw = DeviceWeights(load_weights(args))
+
+    if args.gemv_stream:
+        r = gemv_stream(dw, args.gemv_stream, args.reps, 0 if args.no_warmup else 3)
+        print(f"  {args.gemv_stream} x 28 layers: {r['us_per_launch']:.1f} us/launch, "
+              f"{r['gbs']:.0f} GB/s", flush=True)
+        if args.json:
+            with open(args.json, "w") as f:
+                json.dump(r, f, indent=2)
+        return 0
 
     if args.batch:
         r = bench_batched(dw, args.batch, args.context[0], args.context[1], args.steps, args.seed)
@@ -146,11 +203,12 @@ def main(argv=None) -> int:
         labels = [t[:40] for t in args.text]
     else:
         prompts = (read_prompts_file(args.prompts_file) if args.prompts_file
-                   else synthetic_prompts(seed=args.seed))
+                   else synthetic_prompts(args.num_prompts, args.seed, args.prompt_len))
         labels = [f"{len(p)} ids" for p in prompts]
 
     dec = Qwen3Decoder(dw, max_seq_len=args.max_seq_len, engine=args.engine)
-    bench_one(dec, prompts[0], 4)  # graph capture and first-call set-up
+    if not args.no_warmup:
+        bench_one(dec, prompts[0], 4)  # graph capture and first-call set-up
     tps = []
     for i, (p, label) in enumerate(zip(prompts, labels)):
         n_in, n_out, dt = bench_one(dec, p, args.max_tokens)

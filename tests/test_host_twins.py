@@ -23,6 +23,8 @@ def test_synthetic_prompts_seeded_and_in_vocab():
     assert [len(p) for p in a] == sorted(len(p) for p in a)
     assert all(0 <= t < bm.VOCAB for p in a for t in p)
     assert bm.synthetic_prompts(seed=4) != a
+    fixed = bm.synthetic_prompts(2, seed=3, length=5)
+    assert [len(p) for p in fixed] == [5, 5]
 
 
 def test_prompts_file_and_id_parsing(tmp_path):
