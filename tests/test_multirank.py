@@ -69,3 +69,21 @@ def test_single_process_dist_is_a_no_op():
     assert d.world == 1 and d.max(3.0) == 3.0 and d.sum(4.0) == 4.0
     d.barrier()
     d.close()
+
+
+def test_graph_roofline_reports_flushed_and_pipelined_traffic():
+    import bench
+
+    kern = {"qkv": {"total_us_per_step": 80.0, "achieved_gbs": 500.0, "launches_per_step": 28,
+                    "alg_bytes_per_launch": 4.5e6},
+            "vocab": {"total_us_per_step": 50.0, "achieved_gbs": 6000.0, "launches_per_step": 1,
+                      "alg_bytes_per_launch": 311e6}}
+    tr = bench.load_traffic()
+    r = bench.graph_roofline(kern, 6500.0, "measured", tr)
+    assert r["kernel"] == "qkv" and abs(r["frac"] - 500.0 / 6500.0) < 1e-12
+    assert r["traffic"] == tr["qkv"]
+    assert r["traffic_pipelined"] == tr["qkv_pipelined"]
+    assert r["traffic_pipelined_per_step"] == 28 * tr["qkv_pipelined"] + tr["vocab_pipelined"]
+    # without pipelined figures only the flushed capture is reported
+    r2 = bench.graph_roofline(kern, 6500.0, "measured", {"qkv": 1.0})
+    assert "traffic_pipelined" not in r2 and r2["traffic"] == 1.0
