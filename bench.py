@@ -239,10 +239,9 @@ def cpu_oracle_decode(steps: int, warmup: int, seed: int, budget_s: float) -> di
     steps, stopping early once `budget_s` of decode time is spent."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    from q3b200.weights import synthetic_weights, to_oracle_dict
 
-    w = synthetic_weights(seed=seed)
-    m = O.Model(to_oracle_dict(w))
+    # the oracle's own generator and quantizer: this leg never loads libq3b200.so
+    m = O.Model(O.synthetic_weights(seed=seed))
     prompt = np.random.default_rng(seed).integers(0, 151936, PROMPT_LEN, dtype=np.int64)
     kc, vc = m.new_cache(CACHE)
     t0 = time.perf_counter()

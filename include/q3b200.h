@@ -65,6 +65,12 @@ int q3_memset(void* dst, int value, size_t bytes, void* stream);
 int q3_stream_create(void** stream);
 int q3_stream_destroy(void* stream);
 int q3_stream_synchronize(void* stream);
+/* CUDA graphs: capture the calls enqueued on a created stream between begin
+ * and end, then replay them (exec is an opaque graph handle). */
+int q3_graph_capture_begin(void* stream);
+int q3_graph_capture_end(void* stream, void** exec);
+int q3_graph_launch(void* exec, void* stream);
+int q3_graph_destroy(void* exec);
 int q3_event_create(void** event);
 int q3_event_destroy(void* event);
 int q3_event_record(void* event, void* stream);
@@ -88,6 +94,12 @@ int q3_quantize_q8_0(const float* w, int64_t n, uint8_t* out);
  * Replaces q8_fused_gemv (model/qwen3_full.mlir:536-589).
  * K multiple of 256, K <= 3072; N multiple of 8; w, x 16-byte aligned. */
 int q3_gemv_q8(const void* w, const void* x, void* y, int N, int K, void* stream);
+/* The same GEMV launched with programmatic dependent launch: its weight rows
+ * are copied, and the next launch may begin, while the previous kernel in
+ * the stream is still running (x is read and y written only after that
+ * kernel has finished).  So w must not be written by the preceding kernel.
+ * Back-to-back calls over different weights then stream at HBM rate. */
+int q3_gemv_q8_overlapped(const void* w, const void* x, void* y, int N, int K, void* stream);
 
 /* Same, in the CUDA kernels' order (kernels/cuda/dispatch_3.cu:33-47;
  * per element acc += (scale*q)*x). */
@@ -200,6 +212,18 @@ typedef struct q3_weights {
   const void* q8_ffn_down;    /* Q8_0 [28, 3342336] */
 } q3_weights;
 
+/* One decoder layer (model/qwen3_full.mlir:751-864) as the fused engine
+ * computes it, on caller buffers: x_in f16[1024] -> x_out f16[1024]; the new
+ * K/V row is written at slot layer*S + pos of the flat caches and attention
+ * runs over slots layer*S + 0..pos.  w: the stacked weights (layer selects
+ * the slice); pos: DEVICE int64 (pos < S <= 4096); rope tables f32 [S, 64];
+ * workspace: q3_fused_layer_workspace_bytes() bytes.  Three kernels: the
+ * attention block, the feed-forward block and the residual rebuild. */
+size_t q3_fused_layer_workspace_bytes(void);
+int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, void* x_out, void* k_cache,
+                   void* v_cache, int64_t S, const int64_t* pos, const float* rope_cos,
+                   const float* rope_sin, void* workspace, void* stream);
+
 typedef struct q3_model q3_model;
 
 /* Creates a decoder bound to the current device and to `stream` (NULL: the
@@ -254,18 +278,26 @@ int q3_generate_end(q3_model* m, int64_t* out_tokens, int64_t* n_out);
 #define Q3_KIND_DOWN 4    /* down projection + residual */
 #define Q3_KIND_VOCAB 5   /* final RMSNorm + vocab GEMV + argmax */
 #define Q3_KIND_NORM 6    /* stand-alone RMSNorm (batched decoder only) */
+#define Q3_KIND_FUSED_ATTN 7 /* fused engine: RMSNorm + Q|K|V + QK-norm + RoPE + KV write +
+                                attention + split O projection */
+#define Q3_KIND_FUSED_FFN 8  /* fused engine: O reduction + residual + RMSNorm + gate|up +
+                                SwiGLU + split down projection */
 int q3_model_profile_steps(q3_model* m, int64_t steps, float* times_us, int32_t* kinds,
                            int64_t cap);
 
-/* Engines.  PERSISTENT: every decode
- * step of a call runs inside ONE cooperative kernel with one CTA per SM; a
- * producer warp per CTA streams weight tiles into shared memory ahead of the
- * grid barriers between phases.  GRAPH (default): the same arithmetic as 141
- * kernels per step replayed from CUDA graphs with programmatic dependent
- * launch.  Both give bit-identical results.  Q3_ENGINE=graph|persistent in
- * the environment selects the engine at creation. */
+/* Engines.  FUSED (default where available): two cluster kernels per layer
+ * (attention block; feed-forward block) with the O and down projections split
+ * along K into 8 slices whose f32 partials are summed in slice order -- 57
+ * kernels per step; needs max_seq_len <= 4096.  GRAPH: the reference kernels'
+ * per-projection orders, five kernels per layer (141 per step).  Both replay
+ * CUDA graphs with programmatic dependent launch.  PERSISTENT: the GRAPH
+ * engine's arithmetic inside ONE cooperative kernel with grid barriers
+ * between phases.  GRAPH and PERSISTENT give identical bits; FUSED differs
+ * from them only by its stated summation orders.  Q3_ENGINE=fused|graph|
+ * persistent in the environment selects the engine at creation. */
 #define Q3_ENGINE_GRAPH 0
 #define Q3_ENGINE_PERSISTENT 1
+#define Q3_ENGINE_FUSED 2
 int q3_model_set_engine(q3_model* m, int engine);
 int q3_model_engine(q3_model* m, int* engine);
 /* Kernels this model has launched so far (all engines). */
@@ -278,6 +310,13 @@ int q3_model_kernel_launches(q3_model* m, int64_t* n);
  * out[ctas][phases][4] (host; cap entries).  For latency analysis. */
 int q3_model_trace_steps(q3_model* m, int64_t steps, int64_t trace_step, long long* out,
                          int64_t cap, int* ctas, int* phases);
+
+/* Phase stamps of the FUSED engine: runs `steps` generation steps from a copy
+ * of the step graph whose cluster kernels record, per CTA, the global timer
+ * (ns) after each numbered step of the kernel: out[56 launches][128 CTAs]
+ * [phases] for the last step.  For latency analysis. */
+int q3_model_trace_phases(q3_model* m, int64_t steps, long long* out, int64_t cap,
+                          int64_t* n_launches, int* ctas, int* phases);
 
 /* Kernel timeline of the GRAPH engine: runs `steps` decode steps (which
  * advance the sequence) from a copy of the step graph whose kernels record,

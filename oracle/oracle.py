@@ -78,7 +78,12 @@ def lib() -> ctypes.CDLL:
 class Weights(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "token_embd", "output_norm", "output_T", "attn_norm", "ffn_norm", "q_norm", "k_norm",
-        "q8_q", "q8_k", "q8_v", "q8_o", "q8_gate_up", "q8_down")] + [("n_layers", ctypes.c_int)]
+        "q8_q", "q8_k", "q8_v", "q8_o", "q8_gate_up", "q8_down")] + [("n_layers", ctypes.c_int),
+                                                                    ("order", ctypes.c_int)]
+
+# summation orders of the C oracle (q3_oracle.h): the exact engine's, or the
+# fused engine's (split O / down projections, cluster attention fold)
+ORDER_EXACT, ORDER_FUSED = 0, 1
 
 
 def _declare(L: ctypes.CDLL) -> None:
@@ -99,6 +104,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "q3o_swiglu": (None, [P, P, I]),
         "q3o_add_f16": (None, [P, P, P, I]),
         "q3o_attention": (None, [P, P, P, I64, I64, P]),
+        "q3o_attention_fused": (None, [P, P, P, I64, I64, P]),
+        "q3o_gemv_q8_split": (None, [P, P, P, I, I, I]),
         "q3o_layer": (None, [ctypes.POINTER(Weights), I, P, I64, P, P, I64]),
         "q3o_decode_step": (I64, [ctypes.POINTER(Weights), I64, I64, P, P, I64, P, I]),
         "q3o_generate": (I64, [ctypes.POINTER(Weights), P, I64, I64, I64, P, P, I64, P, P]),
@@ -201,18 +208,30 @@ def add_f16(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return y
 
 
-def attention(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, slot0: int, T: int) -> np.ndarray:
+def attention(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, slot0: int, T: int,
+              order: int = ORDER_EXACT) -> np.ndarray:
     """q: f16[16*128] (normed+roped); kc/vc: f16 [slots, 8, 128]."""
     q, kc, vc = _h(q), _h(kc), _h(vc)
     out = np.empty(NQ * HD, dtype=np.float16)
-    lib().q3o_attention(_p(q), _p(kc), _p(vc), slot0, T, _p(out))
+    fn = lib().q3o_attention_fused if order == ORDER_FUSED else lib().q3o_attention
+    fn(_p(q), _p(kc), _p(vc), slot0, T, _p(out))
     return out
+
+
+def gemv_q8_split(w: np.ndarray, x: np.ndarray, N: int, K: int, nparts: int = 8) -> np.ndarray:
+    """The fused engine's K-split Q8_0 GEMV (O and down projections)."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    assert w.size >= N * (K // QBLK) * QBYTES
+    x = _h(x)
+    y = np.empty(N, dtype=np.float16)
+    lib().q3o_gemv_q8_split(_p(w), _p(x), _p(y), N, K, nparts)
+    return y
 
 
 class Model:
     """Keeps numpy weight arrays alive and exposes the C layer/step/generate."""
 
-    def __init__(self, w: dict[str, np.ndarray], n_layers: int = LAYERS):
+    def __init__(self, w: dict[str, np.ndarray], n_layers: int = LAYERS, order: int = ORDER_EXACT):
         self.arrays = {k: np.ascontiguousarray(v) for k, v in w.items()}
         a = self.arrays
         self.c = Weights(
@@ -222,8 +241,9 @@ class Model:
             k_norm=a["k_norm"].ctypes.data, q8_q=a["q8_q"].ctypes.data,
             q8_k=a["q8_k"].ctypes.data, q8_v=a["q8_v"].ctypes.data, q8_o=a["q8_o"].ctypes.data,
             q8_gate_up=a["q8_gate_up"].ctypes.data, q8_down=a["q8_down"].ctypes.data,
-            n_layers=n_layers)
+            n_layers=n_layers, order=order)
         self.n_layers = n_layers
+        self.order = order
 
     def new_cache(self, S: int) -> tuple[np.ndarray, np.ndarray]:
         return (np.zeros((LAYERS * S, NKV, HD), np.float16),
@@ -256,3 +276,71 @@ def num_threads() -> int:
 
 def set_num_threads(n: int) -> None:
     lib().q3o_set_num_threads(n)
+
+
+# --------------------------------------------------------------------------
+# Seeded synthetic weights for the CPU legs (the oracle's own quantizer)
+# --------------------------------------------------------------------------
+# The benchmark configurations' weights: every matrix f32 N(0, 0.02)
+# quantised Q8_0, gammas 1 + N(0, 0.1) as f16, a tied f16 embedding / vocab
+# N(0, 0.02).  Each tensor draws from its own PCG64 stream spawned from
+# SeedSequence(seed) in a fixed order -- the same streams, in the same order,
+# as the library's host generator, so both produce the same bytes (a test
+# checks that) while bench.py's CPU legs never load the product library.
+Q8_SHAPES = [("q8_q", 2048, 1024), ("q8_k", 1024, 1024), ("q8_v", 1024, 1024),
+             ("q8_o", 1024, 2048), ("q8_gate_up", 6144, 1024), ("q8_down", 1024, 3072)]
+EMB_CHUNKS = 16
+
+
+def _normal_f32(rng: np.random.Generator, shape, std: float) -> np.ndarray:
+    out = np.empty(shape, dtype=np.float32)
+    rng.standard_normal(out=out, dtype=np.float32)
+    out *= np.float32(std)
+    return out
+
+
+def _gamma_f16(rng: np.random.Generator, shape) -> np.ndarray:
+    return (np.float32(1.0) + _normal_f32(rng, shape, 0.1)).astype(np.float16)
+
+
+def synthetic_weights(seed: int = 0, layers: int = LAYERS, threads: int | None = None
+                      ) -> dict[str, np.ndarray]:
+    """The decode path's parameters under the oracle's field names (Model()).
+    Layers beyond `layers` stay zero."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    streams = iter(np.random.SeedSequence(seed).spawn(16 + EMB_CHUNKS + len(Q8_SHAPES) * LAYERS))
+    gen = lambda: np.random.Generator(np.random.PCG64(next(streams)))
+    w: dict[str, np.ndarray] = {}
+    jobs = []
+    emb = np.empty((VOCAB, DIM), dtype=np.float16)
+    rows = VOCAB // EMB_CHUNKS
+
+    def emb_chunk(c, g):
+        emb[c * rows:(c + 1) * rows] = _normal_f32(g, (rows, DIM), 0.02).astype(np.float16)
+
+    for c in range(EMB_CHUNKS):
+        jobs.append((emb_chunk, c, gen()))
+    w["token_embd"] = emb
+    w["output_T"] = emb
+    w["output_norm"] = _gamma_f16(gen(), (DIM,))
+    w["attn_norm"] = _gamma_f16(gen(), (LAYERS, DIM))
+    w["ffn_norm"] = _gamma_f16(gen(), (LAYERS, DIM))
+    w["q_norm"] = _gamma_f16(gen(), (LAYERS, HD))
+    w["k_norm"] = _gamma_f16(gen(), (LAYERS, HD))
+    for name, N, K in Q8_SHAPES:
+        st = np.zeros((LAYERS, N * (K // QBLK) * QBYTES), dtype=np.uint8)
+        w[name] = st
+
+        def q8_layer(l, g, st=st, N=N, K=K):
+            st[l] = quantize_q8_0_c(_normal_f32(g, (N, K), 0.02))
+
+        for l in range(LAYERS):
+            g = gen()
+            if l < layers:
+                jobs.append((q8_layer, l, g))
+    nt = threads or min(32, os.cpu_count() or 1)
+    with ThreadPoolExecutor(nt) as ex:
+        for f in [ex.submit(fn, a, g) for fn, a, g in jobs]:
+            f.result()
+    return w

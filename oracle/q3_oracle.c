@@ -85,7 +85,20 @@ static void pool_start(void) {
   g_pool.started = 1;
 }
 
+/* One pool_for at a time: the pool has a single task slot, and callers may
+ * come from several host threads (the weight generator quantises layers from
+ * a thread pool). */
+static pthread_mutex_t g_pool_call_mu = PTHREAD_MUTEX_INITIALIZER;
+
+static void pool_for_locked(int64_t total, task_fn fn, void* ctx);
+
 static void pool_for(int64_t total, task_fn fn, void* ctx) {
+  pthread_mutex_lock(&g_pool_call_mu);
+  pool_for_locked(total, fn, ctx);
+  pthread_mutex_unlock(&g_pool_call_mu);
+}
+
+static void pool_for_locked(int64_t total, task_fn fn, void* ctx) {
   pool_start();
   const int n = g_pool.nthreads;
   if (n == 1 || total < 2) {
@@ -509,40 +522,47 @@ static void att_merge(att_part* a, const att_part* b) {
   a->m = m;
 }
 
+/* One chunk of 32 keys (c*32 .. c*32+31, those < T) of kv head kvh: the
+ * partial (m, l, o) of the q head held in qf (f32 of the f16 values). */
+static void att_chunk(const float* qf, const uint16_t* kc, const uint16_t* vc, int64_t slot0,
+                      int kvh, int64_t c, int64_t T, att_part* out) {
+  const int64_t row = (int64_t)Q3O_NKV * Q3O_HD;
+  float s[32], p[32];
+  int valid = 0;
+  for (int l = 0; l < 32; ++l) {
+    const int64_t t = c * 32 + l;
+    if (t < T) {
+      const uint16_t* k = kc + (slot0 + t) * row + kvh * Q3O_HD;
+      float a = 0.0f;
+      for (int d = 0; d < Q3O_HD; ++d) a = fmaf(qf[d], q3o_h2f(k[d]), a);
+      s[l] = a * kAttnScale;
+      ++valid;
+    } else {
+      s[l] = -INFINITY;
+    }
+  }
+  float m = -INFINITY;
+  for (int l = 0; l < 32; ++l) m = fmaxf(m, s[l]);
+  for (int l = 0; l < 32; ++l) p[l] = (l < valid) ? q3o_expf(s[l] - m) : 0.0f;
+  out->m = m;
+  out->l = butterfly_sum(p);
+  for (int d = 0; d < Q3O_HD; ++d) out->o[d] = 0.0f;
+  for (int l = 0; l < valid; ++l) {
+    const uint16_t* v = vc + (slot0 + c * 32 + l) * row + kvh * Q3O_HD;
+    for (int d = 0; d < Q3O_HD; ++d) out->o[d] = fmaf(p[l], q3o_h2f(v[d]), out->o[d]);
+  }
+}
+
 void q3o_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int64_t slot0,
                    int64_t T, uint16_t* out) {
   const int64_t nchunks = (T + Q3O_ATT_CHUNK - 1) / Q3O_ATT_CHUNK;
-  const int64_t row = (int64_t)Q3O_NKV * Q3O_HD;
   for (int h = 0; h < Q3O_NQ; ++h) {
     const int kvh = h / 2;
     float qf[Q3O_HD];
     x_to_f32(q + h * Q3O_HD, qf, Q3O_HD);
     att_part total, group, chunk;
     for (int64_t c = 0; c < nchunks; ++c) {
-      float s[32], p[32];
-      int valid = 0;
-      for (int l = 0; l < 32; ++l) {
-        const int64_t t = c * 32 + l;
-        if (t < T) {
-          const uint16_t* k = kc + (slot0 + t) * row + kvh * Q3O_HD;
-          float a = 0.0f;
-          for (int d = 0; d < Q3O_HD; ++d) a = fmaf(qf[d], q3o_h2f(k[d]), a);
-          s[l] = a * kAttnScale;
-          ++valid;
-        } else {
-          s[l] = -INFINITY;
-        }
-      }
-      float m = -INFINITY;
-      for (int l = 0; l < 32; ++l) m = fmaxf(m, s[l]);
-      for (int l = 0; l < 32; ++l) p[l] = (l < valid) ? q3o_expf(s[l] - m) : 0.0f;
-      chunk.m = m;
-      chunk.l = butterfly_sum(p);
-      for (int d = 0; d < Q3O_HD; ++d) chunk.o[d] = 0.0f;
-      for (int l = 0; l < valid; ++l) {
-        const uint16_t* v = vc + (slot0 + c * 32 + l) * row + kvh * Q3O_HD;
-        for (int d = 0; d < Q3O_HD; ++d) chunk.o[d] = fmaf(p[l], q3o_h2f(v[d]), chunk.o[d]);
-      }
+      att_chunk(qf, kc, vc, slot0, kvh, c, T, &chunk);
       if (c % Q3O_ATT_GROUP == 0)
         group = chunk;
       else
@@ -556,6 +576,96 @@ void q3o_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, in
     }
     for (int d = 0; d < Q3O_HD; ++d) out[h * Q3O_HD + d] = q3o_f2h(total.o[d] / total.l);
   }
+}
+
+/* The fused engine's attention (k_fused_attn): the same chunk partials;
+ * chunk c belongs to cluster rank c % 16.  Rank r folds its chunks
+ * (ascending c):  M_r = max m_c,  e_c = exp(m_c - M_r),  l_r = fma chain of
+ * l_c * e_c,  o_r = fma chain of o_c * e_c  (a rank without chunks has
+ * M_r = -inf, l_r = o_r = 0).  The cluster folds the ranks the same way
+ * (M = max M_r, E_r = exp(M_r - M), chains over r = 0..15); out = f16(O / L). */
+void q3o_attention_fused(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                         int64_t slot0, int64_t T, uint16_t* out) {
+  const int64_t nchunks = (T + Q3O_ATT_CHUNK - 1) / Q3O_ATT_CHUNK;
+  att_part* ch = (att_part*)malloc(sizeof(att_part) * (size_t)nchunks);
+  for (int h = 0; h < Q3O_NQ; ++h) {
+    const int kvh = h / 2;
+    float qf[Q3O_HD];
+    x_to_f32(q + h * Q3O_HD, qf, Q3O_HD);
+    for (int64_t c = 0; c < nchunks; ++c) att_chunk(qf, kc, vc, slot0, kvh, c, T, &ch[c]);
+    att_part rk[Q3O_FUSED_CLUSTER];
+    for (int r = 0; r < Q3O_FUSED_CLUSTER; ++r) {
+      att_part* p = &rk[r];
+      p->m = -INFINITY;
+      p->l = 0.0f;
+      for (int d = 0; d < Q3O_HD; ++d) p->o[d] = 0.0f;
+      for (int64_t c = r; c < nchunks; c += Q3O_FUSED_CLUSTER) p->m = fmaxf(p->m, ch[c].m);
+      for (int64_t c = r; c < nchunks; c += Q3O_FUSED_CLUSTER) {
+        const float e = q3o_expf(ch[c].m - p->m);
+        p->l = fmaf(ch[c].l, e, p->l);
+        for (int d = 0; d < Q3O_HD; ++d) p->o[d] = fmaf(ch[c].o[d], e, p->o[d]);
+      }
+    }
+    float M = -INFINITY, L = 0.0f, O[Q3O_HD];
+    for (int r = 0; r < Q3O_FUSED_CLUSTER; ++r) M = fmaxf(M, rk[r].m);
+    for (int d = 0; d < Q3O_HD; ++d) O[d] = 0.0f;
+    for (int r = 0; r < Q3O_FUSED_CLUSTER; ++r) {
+      const float E = q3o_expf(rk[r].m - M);
+      L = fmaf(rk[r].l, E, L);
+      for (int d = 0; d < Q3O_HD; ++d) O[d] = fmaf(rk[r].o[d], E, O[d]);
+    }
+    for (int d = 0; d < Q3O_HD; ++d) out[h * Q3O_HD + d] = q3o_f2h(O[d] / L);
+  }
+  free(ch);
+}
+
+/* The fused engine's split GEMV (k_fused_attn's W_o slice, k_fused_ffn's
+ * W_down slice): K is cut into nparts slices of bpp = K/32/nparts blocks;
+ * in slice p, lane sub (0..3) accumulates blocks p*bpp + sub*bpp/4 + i
+ * (i < bpp/4) as acc = fma(scale, inner, acc) with inner the fma chain of
+ * q_j * x_j over j; the slice partial is (a0 + a1) + (a2 + a3); the row is
+ * f16 of the partials summed in slice order. */
+typedef struct {
+  const uint8_t* w;
+  const float* xf;
+  uint16_t* y;
+  int nb, nparts;
+} split_ctx;
+
+static void gemv_q8_split_task(void* vctx, int64_t n0, int64_t n1) {
+  const split_ctx* c = (const split_ctx*)vctx;
+  const int bpp = c->nb / c->nparts, bps = bpp / 4;
+  for (int64_t n = n0; n < n1; ++n) {
+    const uint8_t* row = c->w + n * (int64_t)c->nb * Q3O_QBYTES;
+    float total = 0.0f;
+    for (int p = 0; p < c->nparts; ++p) {
+      float a[4];
+      for (int sub = 0; sub < 4; ++sub) {
+        float acc = 0.0f;
+        for (int i = 0; i < bps; ++i) {
+          const int b = p * bpp + sub * bps + i;
+          const uint8_t* blk = row + (int64_t)b * Q3O_QBYTES;
+          const float sc = q3o_h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+          float inner = 0.0f;
+          for (int j = 0; j < 32; ++j) inner = fmaf((float)(int8_t)blk[2 + j], c->xf[b * 32 + j], inner);
+          acc = fmaf(sc, inner, acc);
+        }
+        a[sub] = acc;
+      }
+      const float part = (a[0] + a[1]) + (a[2] + a[3]);
+      total = p == 0 ? part : total + part;
+    }
+    c->y[n] = q3o_f2h(total);
+  }
+}
+
+void q3o_gemv_q8_split(const uint8_t* w, const uint16_t* x, uint16_t* y, int N, int K,
+                       int nparts) {
+  float* xf = (float*)malloc(sizeof(float) * (size_t)K);
+  x_to_f32(x, xf, K);
+  split_ctx c = {w, xf, y, K / Q3O_QBLK, nparts};
+  pool_for(N, gemv_q8_split_task, &c);
+  free(xf);
 }
 
 /* ---------------------------------------------------------------------- */
@@ -583,13 +693,23 @@ void q3o_layer(const q3o_weights* w, int layer, uint16_t* x, int64_t pos, uint16
   const int64_t slot = (int64_t)layer * S + pos;
   memcpy(kc + slot * 1024, kn, sizeof(kn));
   memcpy(vc + slot * 1024, v, sizeof(v));
-  q3o_attention(qn, kc, vc, (int64_t)layer * S, pos + 1, att);
-  q3o_gemv_q8_mlir(w->q8_o + layer * kBplO, att, o, 1024, 2048);
+  const int fused = w->order == Q3O_ORDER_FUSED;
+  if (fused)
+    q3o_attention_fused(qn, kc, vc, (int64_t)layer * S, pos + 1, att);
+  else
+    q3o_attention(qn, kc, vc, (int64_t)layer * S, pos + 1, att);
+  if (fused)
+    q3o_gemv_q8_split(w->q8_o + layer * kBplO, att, o, 1024, 2048, 8);
+  else
+    q3o_gemv_q8_mlir(w->q8_o + layer * kBplO, att, o, 1024, 2048);
   q3o_add_f16(x, o, h1, Q3O_DIM);
   q3o_rmsnorm(h1, w->ffn_norm + layer * Q3O_DIM, hn, Q3O_DIM);
   q3o_gemv_q8_mlir(w->q8_gate_up + layer * kBplGU, hn, gu, 6144, 1024);
   q3o_swiglu(gu, act, Q3O_FFN);
-  q3o_gemv_q8_mlir(w->q8_down + layer * kBplD, act, d, 1024, 3072);
+  if (fused)
+    q3o_gemv_q8_split(w->q8_down + layer * kBplD, act, d, 1024, 3072, 8);
+  else
+    q3o_gemv_q8_mlir(w->q8_down + layer * kBplD, act, d, 1024, 3072);
   q3o_add_f16(h1, d, x, Q3O_DIM);
 }
 

@@ -57,6 +57,15 @@ void q3o_add_f16(const uint16_t* a, const uint16_t* b, uint16_t* y, int n);
 void q3o_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int64_t slot0,
                    int64_t T, uint16_t* out);
 
+/* The fused engine's orders (the CUDA kernels k_fused_attn / k_fused_ffn):
+ * a Q8_0 GEMV split along K into nparts slices whose f32 partials are summed
+ * in slice order, and the attention folded over a 16-CTA cluster. */
+#define Q3O_FUSED_CLUSTER 16
+void q3o_gemv_q8_split(const uint8_t* w, const uint16_t* x, uint16_t* y, int N, int K,
+                       int nparts);
+void q3o_attention_fused(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                         int64_t slot0, int64_t T, uint16_t* out);
+
 /* model -- weights in the reference's parameter layout (tools/create_q8_irpa.py:146-224) */
 typedef struct q3o_weights {
   const uint16_t* token_embd;   /* [151936,1024] f16 */
@@ -73,7 +82,14 @@ typedef struct q3o_weights {
   const uint8_t* q8_gate_up;    /* [28, 6684672] */
   const uint8_t* q8_down;       /* [28, 3342336] */
   int n_layers;                 /* <= 28; configs run all 28 */
+  int order;                    /* Q3O_ORDER_*: which engine's summation orders */
 } q3o_weights;
+
+/* Q3O_ORDER_EXACT: the per-projection orders of the reference kernels (the
+ * exact engine).  Q3O_ORDER_FUSED: the O and down projections split along K
+ * into 8 slices and the cluster attention fold (the fused engine). */
+#define Q3O_ORDER_EXACT 0
+#define Q3O_ORDER_FUSED 1
 
 void q3o_layer(const q3o_weights* w, int layer, uint16_t* x, int64_t pos, uint16_t* kc,
                uint16_t* vc, int64_t S);

@@ -18,6 +18,7 @@
 
 #include "q3_attn.cuh"
 #include "q3_common.cuh"
+#include "q3_fused.cuh"
 #include "q3_gemv.cuh"
 #include "q3_iree.cuh"
 #include "q3_persist.cuh"
@@ -156,6 +157,33 @@ extern "C" int q3_stream_destroy(void* s) {
 }
 extern "C" int q3_stream_synchronize(void* s) {
   Q3_CUDA(cudaStreamSynchronize((cudaStream_t)s));
+  return Q3_OK;
+}
+// CUDA graphs of work enqueued on a (non-default) stream, for hosts without
+// a CUDA binding that want to replay a sequence of calls.
+extern "C" int q3_graph_capture_begin(void* s) {
+  Q3_REQUIRE(s, "capture needs a created stream");
+  Q3_CUDA(cudaStreamBeginCapture((cudaStream_t)s, cudaStreamCaptureModeThreadLocal));
+  return Q3_OK;
+}
+extern "C" int q3_graph_capture_end(void* s, void** exec) {
+  Q3_REQUIRE(s && exec, "null pointer");
+  cudaGraph_t g = nullptr;
+  Q3_CUDA(cudaStreamEndCapture((cudaStream_t)s, &g));
+  cudaGraphExec_t ge = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  Q3_CUDA(e);
+  *exec = ge;
+  return Q3_OK;
+}
+extern "C" int q3_graph_launch(void* exec, void* s) {
+  Q3_REQUIRE(exec, "null graph");
+  Q3_CUDA(cudaGraphLaunch((cudaGraphExec_t)exec, (cudaStream_t)s));
+  return Q3_OK;
+}
+extern "C" int q3_graph_destroy(void* exec) {
+  if (exec) Q3_CUDA(cudaGraphExecDestroy((cudaGraphExec_t)exec));
   return Q3_OK;
 }
 extern "C" int q3_event_create(void** e) {
@@ -315,6 +343,33 @@ static cudaError_t launch_cluster(void (*k)(KArgs...), dim3 grid, dim3 block, si
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+// The same with clusters of cluster_x CTAs along x (sizes above 8 need the
+// kernel's non-portable cluster attribute).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_cluster_x(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t st, bool pdl, int cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = (unsigned)cluster_x;
+  attr[n].val.clusterDim.y = 1;
+  attr[n].val.clusterDim.z = 1;
+  ++n;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 struct LaunchShape {
   int grid, nstages;
   size_t smem;
@@ -457,6 +512,14 @@ extern "C" int q3_gemv_q8(const void* w, const void* x, void* y, int N, int K, v
                                           (cudaStream_t)stream, nullptr);
 }
 
+extern "C" int q3_gemv_q8_overlapped(const void* w, const void* x, void* y, int N, int K,
+                                     void* stream) {
+  int rc = check_q8_shape(w, x, y, N, K);
+  if (rc) return rc;
+  return launch_q8<kOrderMlir, kModePlain>(q8_args_single(w, x, y, nullptr, N, K),
+                                          (cudaStream_t)stream, nullptr, true);
+}
+
 extern "C" int q3_gemv_q8_cuda_order(const void* w, const void* x, void* y, int N, int K,
                                      void* stream) {
   int rc = check_q8_shape(w, x, y, N, K);
@@ -573,9 +636,12 @@ static bool attn_early_loads(int batch) {
   return batch == 1;
 }
 
+// groups > 0 sizes the grid's group dimension below the partial stride
+// (a.max_chunks), for a scratch laid out for longer caches than this launch's.
 static int launch_attn(const AttnArgs& a, int batch, cudaStream_t st, int* launches,
-                       bool pdl = false) {
-  dim3 grid(kNKV, (unsigned)max_groups_for((int64_t)a.max_chunks * kAttChunk), batch);
+                       bool pdl = false, int groups = 0) {
+  if (groups <= 0) groups = max_groups_for((int64_t)a.max_chunks * kAttChunk);
+  dim3 grid(kNKV, (unsigned)groups, batch);
   if (attn_early_loads(batch))
     Q3_CUDA(launch_ex(k_attn_decode<true>, grid, dim3(256), 0, st, pdl, a));
   else
@@ -593,6 +659,7 @@ extern "C" int q3_decode_attention(const void* qkv, const void* q_norm, const vo
   Q3_REQUIRE(S >= 1 && slot0 >= 0 && rope_rows >= 1, "bad S / slot0 / rope_rows");
   Q3_REQUIRE(aligned16(qkv) && aligned16(kc) && aligned16(vc) && aligned16(ws),
              "qkv, caches and workspace must be 16-byte aligned");
+  Q3_REQUIRE(((uintptr_t)out & 7u) == 0, "out must be 8-byte aligned (stored as 4 f16 at a time)");
   AttnArgs a;
   memset(&a, 0, sizeof(a));
   a.qkv = (const uint16_t*)qkv;
@@ -648,6 +715,7 @@ extern "C" int q3_decode_attention_noalloc(const void* qkv, const void* q_norm, 
              (long long)S, (long long)kNoAllocMaxPositions);
   Q3_REQUIRE(aligned16(qkv) && aligned16(kc) && aligned16(vc),
              "qkv and caches must be 16-byte aligned");
+  Q3_REQUIRE(((uintptr_t)out & 7u) == 0, "out must be 8-byte aligned (stored as 4 f16 at a time)");
   int dev = 0;
   Q3_CUDA(cudaGetDevice(&dev));
   Q3_REQUIRE(dev >= 0 && dev < 64, "device ordinal %d out of range", dev);
@@ -682,7 +750,97 @@ extern "C" int q3_decode_attention_noalloc(const void* qkv, const void* q_norm, 
   a.max_chunks = kNoAllocChunks;
   a.part = (AttnPartial*)scratch;
   a.counters = counters;
-  return launch_attn(a, 1, (cudaStream_t)stream, nullptr);
+  // partials keep the scratch's stride; the grid covers only this cache's groups
+  return launch_attn(a, 1, (cudaStream_t)stream, nullptr, false, max_groups_for(S));
+}
+
+// One layer of the fused engine on caller buffers ------------------------------
+// The fused kernels' attributes (dynamic shared memory above 48 KB, 16-CTA
+// clusters), set once per device.
+static int fused_attrs() {
+  static std::mutex mu;
+  static std::set<int> done;
+  int dev = 0;
+  Q3_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count(dev)) return Q3_OK;
+  Q3_CUDA(cudaFuncSetAttribute(k_fused_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaSmem));
+  Q3_CUDA(cudaFuncSetAttribute(k_fused_attn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  Q3_CUDA(cudaFuncSetAttribute(k_fused_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFbSmem));
+  Q3_CUDA(cudaFuncSetAttribute(k_fused_ffn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  done.insert(dev);
+  return Q3_OK;
+}
+
+// Workspace: the O and down partials, h1, the intermediate x and a sequence
+// state holding pos (copied from the caller's device pos).
+struct FusedLayerWs {
+  float opart[kFParts * kDim];
+  float dpart[kFParts * kDim];
+  uint16_t x[kDim];
+  uint16_t h1[kDim];
+  SeqState seq;
+};
+
+extern "C" size_t q3_fused_layer_workspace_bytes(void) { return sizeof(FusedLayerWs) + 256; }
+
+extern "C" int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, void* x_out,
+                              void* kc, void* vc, int64_t S, const int64_t* pos,
+                              const float* rope_cos, const float* rope_sin, void* ws,
+                              void* stream) {
+  Q3_REQUIRE(w && x_in && x_out && kc && vc && pos && rope_cos && rope_sin && ws, "null pointer");
+  Q3_REQUIRE(layer >= 0 && layer < kLayers, "layer %d out of range", layer);
+  Q3_REQUIRE(S >= 1 && S <= kFusedMaxPositions, "S=%lld outside [1, %lld]", (long long)S,
+             (long long)kFusedMaxPositions);
+  Q3_REQUIRE(aligned16(x_in) && aligned16(x_out) && aligned16(kc) && aligned16(vc) && aligned16(ws),
+             "x, caches and workspace must be 16-byte aligned");
+  const void* req[] = {w->attn_norm, w->ffn_norm, w->attn_q_norm, w->attn_k_norm, w->q8_attn_q,
+                       w->q8_attn_k, w->q8_attn_v, w->q8_attn_output, w->q8_ffn_gate_up,
+                       w->q8_ffn_down};
+  for (const void* p : req) Q3_REQUIRE(p != nullptr && aligned16(p), "weights: null or unaligned");
+  int rc_ = Q3_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  FusedLayerWs* f = (FusedLayerWs*)ws;
+  Q3_CUDA(cudaMemsetAsync(&f->seq, 0, sizeof(SeqState), st));
+  Q3_CUDA(cudaMemcpyAsync(&f->seq.pos, pos, sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
+  rc_ = fused_attrs();
+  if (rc_) return rc_;
+  FaArgs fa;
+  memset(&fa, 0, sizeof(fa));
+  fa.wq = (const uint8_t*)w->q8_attn_q + layer * kBplQ;
+  fa.wk = (const uint8_t*)w->q8_attn_k + layer * kBplKV;
+  fa.wv = (const uint8_t*)w->q8_attn_v + layer * kBplKV;
+  fa.wo = (const uint8_t*)w->q8_attn_output + layer * kBplO;
+  fa.attn_norm = (const uint16_t*)w->attn_norm + layer * kDim;
+  fa.q_norm = (const uint16_t*)w->attn_q_norm + layer * kHD;
+  fa.k_norm = (const uint16_t*)w->attn_k_norm + layer * kHD;
+  fa.h1 = (const uint16_t*)x_in;  // no dpart: x = x_in
+  fa.x_out = f->x;
+  fa.opart = f->opart;
+  fa.kc = (uint16_t*)kc;
+  fa.vc = (uint16_t*)vc;
+  fa.rope_cos = rope_cos;
+  fa.rope_sin = rope_sin;
+  fa.slot0 = (int64_t)layer * S;
+  fa.S = S;
+  fa.seq = &f->seq;
+  Q3_CUDA(launch_cluster_x(k_fused_attn, dim3(kFParts * kFC), dim3(kFaThreads), kFaSmem, st, false,
+                           kFC, fa));
+  FbArgs fb;
+  memset(&fb, 0, sizeof(fb));
+  fb.wgu = (const uint8_t*)w->q8_ffn_gate_up + layer * kBplGU;
+  fb.wd = (const uint8_t*)w->q8_ffn_down + layer * kBplD;
+  fb.ffn_norm = (const uint16_t*)w->ffn_norm + layer * kDim;
+  fb.x = f->x;
+  fb.opart = f->opart;
+  fb.h1_out = f->h1;
+  fb.dpart = f->dpart;
+  fb.seq = &f->seq;
+  Q3_CUDA(launch_cluster_x(k_fused_ffn, dim3(kFParts * kFC), dim3(kFbThreads), kFbSmem, st, true,
+                           kFC, fb));
+  Q3_CUDA(launch_ex(k_resid_parts, dim3(1), dim3(256), 0, st, true, (const uint16_t*)f->h1,
+                    (const float*)f->dpart, (uint16_t*)x_out));
+  return Q3_OK;
 }
 
 // IREE-ABI dispatch launchers --------------------------------------------------
@@ -772,8 +930,14 @@ struct q3_model {
   int64_t gen_n_prompt = 0, gen_pos0 = 0, gen_max = 0;
   bool gen_active = false;
   // chat
-  // engines: CUDA graphs of per-phase kernels, or one persistent kernel
-  int engine = Q3_ENGINE_GRAPH;  // measured faster at batch 1 for now
+  // engines: CUDA graphs of per-phase kernels (exact: 5 per layer; fused: 2
+  // cluster kernels per layer), or one persistent kernel
+  int engine = Q3_ENGINE_GRAPH;
+  float *opart = nullptr, *dpart = nullptr;  // fused engine: split O / down partials [8][1024]
+  cudaGraphExec_t g_ingest_f = nullptr, g_gen_f = nullptr;
+  int launches_gen_f = 0, launches_ingest_f = 0;
+  int fused_clusters = 0;        // co-resident 16-CTA clusters of the fused kernels (0: unavailable)
+  int prof_engine = -1, ktrace_engine = -1;  // engine the profiling graphs were captured for
   int persist_grid = 0;          // CTAs of the persistent kernel (one per SM)
   unsigned int* grid_ctr = nullptr;
   int64_t kernel_launches = 0;   // kernels launched by this model so far
@@ -794,7 +958,15 @@ struct StepProbe {
   unsigned long long* ktrace = nullptr;  // launch timing records, kTraceVals per kernel
   int* slot = nullptr;                   // next record
   std::vector<int32_t>* tkinds = nullptr;
+  long long* phase = nullptr;            // fused kernels' per-CTA phase stamps, per launch
+  int* pslot = nullptr;
 };
+
+// The next fused launch's phase-stamp block while capturing a phase-traced graph.
+static long long* probe_phase(const StepProbe* pr) {
+  if (!pr || !pr->phase) return nullptr;
+  return pr->phase + (int64_t)kFParts * kFC * kFPhases * (*pr->pslot)++;
+}
 
 // The next launch's timing record while capturing a traced graph, else null.
 static unsigned long long* probe_trace(const StepProbe* pr, int kind) {
@@ -933,12 +1105,75 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
   return Q3_OK;
 }
 
-static int enqueue_vocab(q3_model* m, int* launches, const StepProbe* probe) {
+// The fused engine: per layer k_fused_attn then k_fused_ffn (q3_fused.cuh),
+// each a grid of 8 clusters of 16 CTAs with programmatic dependent launch.
+static int enqueue_layers_fused(q3_model* m, bool ingest, int* launches, const StepProbe* probe) {
+  cudaStream_t st = m->stream;
+  for (int l = 0; l < kLayers; ++l) {
+    FaArgs fa;
+    memset(&fa, 0, sizeof(fa));
+    fa.wq = (const uint8_t*)m->w.q8_attn_q + l * kBplQ;
+    fa.wk = (const uint8_t*)m->w.q8_attn_k + l * kBplKV;
+    fa.wv = (const uint8_t*)m->w.q8_attn_v + l * kBplKV;
+    fa.wo = (const uint8_t*)m->w.q8_attn_output + l * kBplO;
+    fa.attn_norm = (const uint16_t*)m->w.attn_norm + l * kDim;
+    fa.q_norm = (const uint16_t*)m->w.attn_q_norm + l * kHD;
+    fa.k_norm = (const uint16_t*)m->w.attn_k_norm + l * kHD;
+    if (l == 0) {
+      fa.tokens = m->tokens;
+      fa.embd = (const uint16_t*)m->w.token_embd;
+    } else {
+      fa.h1 = m->h1;
+      fa.dpart = m->dpart;
+    }
+    fa.x_out = m->x;
+    fa.opart = m->opart;
+    fa.kc = m->kc;
+    fa.vc = m->vc;
+    fa.rope_cos = m->rope_cos;
+    fa.rope_sin = m->rope_sin;
+    fa.slot0 = (int64_t)l * m->S;
+    fa.S = m->S;
+    fa.seq = m->st;
+    fa.err = m->err;
+    fa.trace = probe_trace(probe, Q3_KIND_FUSED_ATTN);
+    fa.phase = probe_phase(probe);
+    Q3_CUDA(launch_cluster_x(k_fused_attn, dim3(kFParts * kFC), dim3(kFaThreads), kFaSmem, st,
+                             true, kFC, fa));
+    ++*launches;
+    Q3_PROBE(Q3_KIND_FUSED_ATTN);
+    FbArgs fb;
+    memset(&fb, 0, sizeof(fb));
+    fb.wgu = (const uint8_t*)m->w.q8_ffn_gate_up + l * kBplGU;
+    fb.wd = (const uint8_t*)m->w.q8_ffn_down + l * kBplD;
+    fb.ffn_norm = (const uint16_t*)m->w.ffn_norm + l * kDim;
+    fb.x = m->x;
+    fb.opart = m->opart;
+    fb.h1_out = m->h1;
+    fb.dpart = m->dpart;
+    fb.seq = m->st;
+    if (ingest && l == kLayers - 1) fb.advance = m->st;
+    fb.err = m->err;
+    fb.trace = probe_trace(probe, Q3_KIND_FUSED_FFN);
+    fb.phase = probe_phase(probe);
+    Q3_CUDA(launch_cluster_x(k_fused_ffn, dim3(kFParts * kFC), dim3(kFbThreads), kFbSmem, st,
+                             true, kFC, fb));
+    ++*launches;
+    Q3_PROBE(Q3_KIND_FUSED_FFN);
+  }
+  return Q3_OK;
+}
+
+static int enqueue_vocab(q3_model* m, int* launches, const StepProbe* probe, int engine) {
   cudaStream_t st = m->stream;
   VocabArgs v;
   memset(&v, 0, sizeof(v));
   v.w = (const uint16_t*)m->w.output_T;
   v.x = m->x;
+  if (engine == Q3_ENGINE_FUSED) {  // x = f16(h1 + f16(sum of the last layer's down partials))
+    v.xres = m->h1;
+    v.xpart = m->dpart;
+  }
   v.norm_g = (const uint16_t*)m->w.output_norm;
   v.logits = m->logits;
   v.N = kVocab;
@@ -956,13 +1191,15 @@ static int enqueue_vocab(q3_model* m, int* launches, const StepProbe* probe) {
 }
 
 static int capture(q3_model* m, bool ingest, cudaGraphExec_t* out, int* launches,
-                   const StepProbe* probe = nullptr) {
+                   const StepProbe* probe = nullptr, int engine = Q3_ENGINE_GRAPH) {
   cudaGraph_t g = nullptr;
   Q3_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
   int n = 0;
   int rc = probe_mark(probe, m->stream, -1);
-  if (rc == Q3_OK) rc = enqueue_layers(m, ingest, &n, probe);
-  if (rc == Q3_OK && !ingest) rc = enqueue_vocab(m, &n, probe);
+  if (rc == Q3_OK)
+    rc = engine == Q3_ENGINE_FUSED ? enqueue_layers_fused(m, ingest, &n, probe)
+                                   : enqueue_layers(m, ingest, &n, probe);
+  if (rc == Q3_OK && !ingest) rc = enqueue_vocab(m, &n, probe, engine);
   cudaError_t e = cudaStreamEndCapture(m->stream, &g);
   if (rc) {
     if (g) cudaGraphDestroy(g);
@@ -982,11 +1219,13 @@ static void model_free(q3_model* m) {
   if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
   if (m->g_prof) cudaGraphExecDestroy(m->g_prof);
   if (m->g_ktrace) cudaGraphExecDestroy(m->g_ktrace);
+  if (m->g_ingest_f) cudaGraphExecDestroy(m->g_ingest_f);
+  if (m->g_gen_f) cudaGraphExecDestroy(m->g_gen_f);
   if (m->ktrace_dev) cudaFree(m->ktrace_dev);
   for (cudaEvent_t e : m->prof_events) cudaEventDestroy(e);
   void* dev[] = {m->kc, m->vc, m->rope_cos, m->rope_sin, m->x, m->qkv, m->attn, m->h1, m->act,
                  m->logits, m->tokens, m->st, m->am_part, m->att_part, m->err, m->grid_ctr,
-                 m->trace_dev};
+                 m->trace_dev, m->opart, m->dpart};
   for (void* p : dev)
     if (p) cudaFree(p);
   if (m->h_st) cudaFreeHost(m->h_st);
@@ -1019,6 +1258,44 @@ static int persist_setup(q3_model* m) {
   if (m->persist_grid > kArgmaxMaxGrid) m->persist_grid = 0;
   Q3_CUDA(cudaMalloc((void**)&m->grid_ctr, 256));
   Q3_CUDA(cudaMemset(m->grid_ctr, 0, 256));
+  return Q3_OK;
+}
+
+// The fused engine needs caches of at most kFusedMaxPositions positions and
+// 16-CTA clusters of both of its kernels resident (non-portable size).
+static int fused_setup(q3_model* m) {
+  m->fused_clusters = 0;
+  if (m->S > kFusedMaxPositions) return Q3_OK;
+  int rc = fused_attrs();
+  if (rc) return rc;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = kFC;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kFParts * kFC);
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int na = 0, nb = 0;
+  cfg.blockDim = dim3(kFaThreads);
+  cfg.dynamicSmemBytes = kFaSmem;
+  if (cudaOccupancyMaxActiveClusters(&na, (void*)k_fused_attn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    na = 0;
+  }
+  cfg.blockDim = dim3(kFbThreads);
+  cfg.dynamicSmemBytes = kFbSmem;
+  if (cudaOccupancyMaxActiveClusters(&nb, (void*)k_fused_ffn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    nb = 0;
+  }
+  m->fused_clusters = na < nb ? na : nb;
+  if (m->fused_clusters < 1) return Q3_OK;
+  Q3_CUDA(cudaMalloc((void**)&m->opart, kFParts * kDim * sizeof(float)));
+  Q3_CUDA(cudaMalloc((void**)&m->dpart, kFParts * kDim * sizeof(float)));
+  Q3_CUDA(cudaMemset(m->opart, 0, kFParts * kDim * sizeof(float)));
+  Q3_CUDA(cudaMemset(m->dpart, 0, kFParts * kDim * sizeof(float)));
   return Q3_OK;
 }
 
@@ -1094,24 +1371,36 @@ extern "C" int q3_model_create(const q3_weights* w, int64_t S, void* stream, q3_
   if (rc == Q3_OK) rc = capture(m, true, &m->g_ingest, &m->launches_ingest);
   if (rc == Q3_OK) rc = capture(m, false, &m->g_gen, &m->launches_gen);
   if (rc == Q3_OK) rc = persist_setup(m);
+  if (rc == Q3_OK) rc = fused_setup(m);
+  if (rc == Q3_OK && m->fused_clusters > 0)
+    rc = capture(m, true, &m->g_ingest_f, &m->launches_ingest_f, nullptr, Q3_ENGINE_FUSED);
+  if (rc == Q3_OK && m->fused_clusters > 0)
+    rc = capture(m, false, &m->g_gen_f, &m->launches_gen_f, nullptr, Q3_ENGINE_FUSED);
   if (rc != Q3_OK) {
     model_free(m);
     return rc;
   }
+  // default: the fused engine where it is available
+  m->engine = m->fused_clusters > 0 ? Q3_ENGINE_FUSED : Q3_ENGINE_GRAPH;
   const char* env = getenv("Q3_ENGINE");
   if (env && strcmp(env, "graph") == 0) m->engine = Q3_ENGINE_GRAPH;
+  if (env && strcmp(env, "fused") == 0 && m->fused_clusters > 0) m->engine = Q3_ENGINE_FUSED;
   if (env && strcmp(env, "persistent") == 0 && m->persist_grid > 0) m->engine = Q3_ENGINE_PERSISTENT;
-  if (m->persist_grid == 0) m->engine = Q3_ENGINE_GRAPH;
   *out = m;
   return Q3_OK;
 }
 
 extern "C" int q3_model_set_engine(q3_model* m, int engine) {
   Q3_REQUIRE(m, "null model");
-  Q3_REQUIRE(engine == Q3_ENGINE_GRAPH || engine == Q3_ENGINE_PERSISTENT, "unknown engine %d",
-             engine);
+  Q3_REQUIRE(engine == Q3_ENGINE_GRAPH || engine == Q3_ENGINE_PERSISTENT ||
+                 engine == Q3_ENGINE_FUSED,
+             "unknown engine %d", engine);
   if (engine == Q3_ENGINE_PERSISTENT && m->persist_grid == 0)
     return set_err(Q3_ERR_UNSUPPORTED, "the persistent kernel cannot be co-resident here");
+  if (engine == Q3_ENGINE_FUSED && m->fused_clusters == 0)
+    return set_err(Q3_ERR_UNSUPPORTED,
+                   "the fused engine needs max_seq_len <= %lld and resident 16-CTA clusters",
+                   (long long)kFusedMaxPositions);
   m->engine = engine;
   return Q3_OK;
 }
@@ -1140,7 +1429,8 @@ extern "C" void* q3_model_stream(q3_model* m) { return m ? (void*)m->stream : nu
 
 extern "C" int q3_model_launches_per_step(q3_model* m, int64_t* n) {
   Q3_REQUIRE(m && n, "null pointer");
-  *n = m->launches_gen;
+  *n = m->engine == Q3_ENGINE_FUSED ? m->launches_gen_f : m->engine == Q3_ENGINE_PERSISTENT ? 1
+                                                                                          : m->launches_gen;
   return Q3_OK;
 }
 
@@ -1232,9 +1522,12 @@ static int launch_graphs(q3_model* m, int64_t n_ingest, int64_t n_gen) {
     m->kernel_launches += 1;
     return Q3_OK;
   }
-  for (int64_t i = 0; i < n_ingest; ++i) Q3_CUDA(cudaGraphLaunch(m->g_ingest, m->stream));
-  for (int64_t i = 0; i < n_gen; ++i) Q3_CUDA(cudaGraphLaunch(m->g_gen, m->stream));
-  m->kernel_launches += n_ingest * m->launches_ingest + n_gen * m->launches_gen;
+  const bool f = m->engine == Q3_ENGINE_FUSED;
+  cudaGraphExec_t gi = f ? m->g_ingest_f : m->g_ingest, gg = f ? m->g_gen_f : m->g_gen;
+  for (int64_t i = 0; i < n_ingest; ++i) Q3_CUDA(cudaGraphLaunch(gi, m->stream));
+  for (int64_t i = 0; i < n_gen; ++i) Q3_CUDA(cudaGraphLaunch(gg, m->stream));
+  m->kernel_launches += n_ingest * (f ? m->launches_ingest_f : m->launches_ingest) +
+                        n_gen * (f ? m->launches_gen_f : m->launches_gen);
   return Q3_OK;
 }
 
@@ -1365,11 +1658,20 @@ extern "C" int q3_model_profile_steps(q3_model* m, int64_t steps, float* times_u
                                       int64_t cap) {
   Q3_REQUIRE(m && times_us && kinds && steps >= 1, "bad arguments");
   if (!m->gen_active) return set_err(Q3_ERR_STATE, "no generation in progress");
+  const int eng = m->engine == Q3_ENGINE_FUSED ? Q3_ENGINE_FUSED : Q3_ENGINE_GRAPH;
+  if (m->g_prof && m->prof_engine != eng) {
+    cudaGraphExecDestroy(m->g_prof);
+    m->g_prof = nullptr;
+    for (cudaEvent_t e : m->prof_events) cudaEventDestroy(e);
+    m->prof_events.clear();
+    m->prof_kinds.clear();
+  }
   if (!m->g_prof) {
     StepProbe pr{&m->prof_events, &m->prof_kinds};
     int n = 0;
-    int rc = capture(m, false, &m->g_prof, &n, &pr);
+    int rc = capture(m, false, &m->g_prof, &n, &pr, eng);
     if (rc) return rc;
+    m->prof_engine = eng;
   }
   const int64_t nk = (int64_t)m->prof_events.size() - 1;
   Q3_REQUIRE(cap >= nk, "cap %lld below the %lld kernels of a step", (long long)cap, (long long)nk);
@@ -1400,6 +1702,11 @@ extern "C" int q3_model_trace_kernels(q3_model* m, int64_t steps, long long* out
   Q3_REQUIRE(m && out && kinds && n_kernels && steps >= 1, "bad arguments");
   if (!m->gen_active) return set_err(Q3_ERR_STATE, "no generation in progress");
   constexpr int kMaxTraced = 512;
+  const int eng = m->engine == Q3_ENGINE_FUSED ? Q3_ENGINE_FUSED : Q3_ENGINE_GRAPH;
+  if (m->g_ktrace && m->ktrace_engine != eng) {
+    cudaGraphExecDestroy(m->g_ktrace);
+    m->g_ktrace = nullptr;
+  }
   if (!m->g_ktrace) {
     if (!m->ktrace_dev) Q3_CUDA(cudaMalloc((void**)&m->ktrace_dev, kMaxTraced * kTraceVals * 8));
     int slot = 0, n = 0;
@@ -1408,8 +1715,9 @@ extern "C" int q3_model_trace_kernels(q3_model* m, int64_t steps, long long* out
     pr.ktrace = m->ktrace_dev;
     pr.slot = &slot;
     pr.tkinds = &m->ktrace_kinds;
-    int rc = capture(m, false, &m->g_ktrace, &n, &pr);
+    int rc = capture(m, false, &m->g_ktrace, &n, &pr, eng);
     if (rc) return rc;
+    m->ktrace_engine = eng;
   }
   const int64_t nk = (int64_t)m->ktrace_kinds.size();
   *n_kernels = nk;
@@ -1437,6 +1745,43 @@ extern "C" int q3_model_trace_kernels(q3_model* m, int64_t steps, long long* out
     for (int j = 0; j < 6; ++j) out[k * 6 + j] = (long long)(acc[k * V + j] / (double)steps);
   }
   return Q3_OK;
+}
+
+// Per-CTA phase stamps of the fused engine's kernels during the last of
+// `steps` decode steps (which advance the sequence): out[launch][cta][phase]
+// in ns of %globaltimer, 2 x 28 launches of 128 CTAs x kFPhases each.
+extern "C" int q3_model_trace_phases(q3_model* m, int64_t steps, long long* out, int64_t cap,
+                                     int64_t* n_launches, int* ctas, int* phases) {
+  Q3_REQUIRE(m && out && n_launches && ctas && phases && steps >= 1, "bad arguments");
+  if (!m->gen_active) return set_err(Q3_ERR_STATE, "no generation in progress");
+  if (m->engine != Q3_ENGINE_FUSED) return set_err(Q3_ERR_STATE, "phase tracing needs the fused engine");
+  const int64_t nl = 2 * kLayers, per = (int64_t)kFParts * kFC * kFPhases;
+  Q3_REQUIRE(cap >= nl * per, "cap %lld below %lld", (long long)cap, (long long)(nl * per));
+  long long* dev = nullptr;
+  Q3_CUDA(cudaMalloc((void**)&dev, (size_t)(nl * per) * sizeof(long long)));
+  cudaGraphExec_t g = nullptr;
+  int n = 0, ps = 0;
+  StepProbe pr;
+  pr.phase = dev;
+  pr.pslot = &ps;
+  int rc = capture(m, false, &g, &n, &pr, Q3_ENGINE_FUSED);
+  for (int64_t i = 0; rc == Q3_OK && i < steps; ++i) {
+    const cudaError_t e = cudaGraphLaunch(g, m->stream);
+    if (e != cudaSuccess) rc = set_err(Q3_ERR_CUDA, "trace launch: %s", cudaGetErrorString(e));
+  }
+  if (rc == Q3_OK) {
+    cudaError_t e = cudaMemcpyAsync(out, dev, (size_t)(nl * per) * sizeof(long long),
+                                    cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) rc = set_err(Q3_ERR_CUDA, "trace copy: %s", cudaGetErrorString(e));
+  }
+  if (g) cudaGraphExecDestroy(g);
+  cudaFree(dev);
+  m->kernel_launches += steps * n;
+  *n_launches = nl;
+  *ctas = kFParts * kFC;
+  *phases = kFPhases;
+  return rc;
 }
 
 extern "C" int q3_model_trace_steps(q3_model* m, int64_t steps, int64_t trace_step,

@@ -147,22 +147,6 @@ __device__ __forceinline__ void dequant_block_j(int blk, uint32_t stage, uint32_
 }
 
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
-  uint32_t remote;
-  float v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
-}
-
 // Batched Q8_0 GEMM.  Grid (row tiles, S splits), clusters of the S CTAs of
 // a tile: CTA (t, s) owns output rows 128t .. 128t+127 (kBgSwiglu: those gate
 // rows and their up rows) over 256-wide K chunks [s*kc, (s+1)*kc).  With

@@ -359,4 +359,38 @@ __device__ __forceinline__ float q8_block_dot_cuda(const Q8BlockWords& b, const 
   return acc;
 }
 
+// ---------------------------------------------------------------------------
+// Thread-block clusters: barrier and distributed shared memory (DSMEM)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of `local_addr` (a shared::cta address) in CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  return remote;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(dsmem_map(local_addr, rank)) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint16_t ld_dsmem_u16(uint32_t local_addr, uint32_t rank) {
+  uint16_t v;
+  asm volatile("ld.shared::cluster.u16 %0, [%1];" : "=h"(v) : "r"(dsmem_map(local_addr, rank)) : "memory");
+  return v;
+}
+
 }  // namespace q3

@@ -188,13 +188,15 @@ __device__ __forceinline__ void load_gamma_regs(const uint16_t* g, int K,
     gr[i] = k < K ? g[k] : (uint16_t)0;
   }
 }
+// x == nullptr: xs already holds the input (staged by the caller).
 template <int KMAX>
 __device__ __forceinline__ void cta_rmsnorm_to_smem_g(const uint16_t* x,
                                                       const uint16_t (&gr)[KMAX / 256], int K,
                                                       uint16_t* xs, float* rs) {
   const int tid = threadIdx.x;
-  for (int i = tid; i < K / 8; i += 256)
-    reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(x)[i];
+  if (x != nullptr)
+    for (int i = tid; i < K / 8; i += 256)
+      reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(x)[i];
   consumer_sync();
   if (tid < 32) {
     float ss = 0.0f;
@@ -783,6 +785,32 @@ __global__ void __launch_bounds__(kGemv1tThreads, gemv1t_min_blocks<G, MODE>())
 }
 
 // --------------------------------------------------------------------------
+// Residual stream from split projections (the fused engine)
+// --------------------------------------------------------------------------
+// The fused engine splits the O and down projections along K into kFParts
+// f32 partial vectors; a consumer rebuilds the residual stream, 4 elements
+// per thread: y = f16(res + f16(((p0 + p1) + p2) + ... + p7)).
+constexpr int kFParts = 8;
+
+__device__ __forceinline__ uint2 resid_plus_parts(const uint16_t* res, const float* parts, int k0) {
+  const uint2 rv = __ldcg(reinterpret_cast<const uint2*>(res + k0));
+  float4 s = __ldcg(reinterpret_cast<const float4*>(parts + k0));
+#pragma unroll
+  for (int c = 1; c < kFParts; ++c) {
+    const float4 t = __ldcg(reinterpret_cast<const float4*>(parts + c * kDim + k0));
+    s.x = __fadd_rn(s.x, t.x);
+    s.y = __fadd_rn(s.y, t.y);
+    s.z = __fadd_rn(s.z, t.z);
+    s.w = __fadd_rn(s.w, t.w);
+  }
+  auto add = [](uint16_t r, float p) { return f2h(__fadd_rn(h2f(r), h2f(f2h(p)))); };
+  uint2 y;
+  y.x = (uint32_t)add((uint16_t)(rv.x & 0xffffu), s.x) | ((uint32_t)add((uint16_t)(rv.x >> 16), s.y) << 16);
+  y.y = (uint32_t)add((uint16_t)(rv.y & 0xffffu), s.z) | ((uint32_t)add((uint16_t)(rv.y >> 16), s.w) << 16);
+  return y;
+}
+
+// --------------------------------------------------------------------------
 // f16 vocab GEMV + argmax
 // --------------------------------------------------------------------------
 struct ArgmaxPartial {
@@ -804,6 +832,10 @@ struct VocabArgs {
   const uint16_t* w;       // [N, K] f16 rows
   const uint16_t* x;       // input (f16); normalised with norm_g if non-null
   const uint16_t* norm_g;
+  // Fused engine (with norm_g): x = f16(xres + f16(sum of the kFParts
+  // vectors of xpart)) instead of x.
+  const float* xpart;
+  const uint16_t* xres;
   uint16_t* logits;        // optional [N] f16
   int N, K;                // N multiple of 8, K == 1024 (lane holds K/32 inputs)
   ArgmaxPartial* partial;  // [gridDim.x]
@@ -860,7 +892,9 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
     uint16_t xh[kVocabK / 32];
     if (!stopped) {
       if (a.norm_g != nullptr) {
-        cta_rmsnorm_to_smem_g<kVocabK>(a.x, gr, a.K, xs, &rs);
+        if (a.xpart != nullptr)
+          *reinterpret_cast<uint2*>(xs + 4 * threadIdx.x) = resid_plus_parts(a.xres, a.xpart, 4 * threadIdx.x);
+        cta_rmsnorm_to_smem_g<kVocabK>(a.xpart != nullptr ? nullptr : a.x, gr, a.K, xs, &rs);
 #pragma unroll
         for (int i = 0; i < kVocabK / 32; ++i) xh[i] = xs[lane + 32 * i];
       } else {

@@ -52,6 +52,10 @@ SIGNATURES = {
     "q3_stream_create": [PP],
     "q3_stream_destroy": [P],
     "q3_stream_synchronize": [P],
+    "q3_graph_capture_begin": [P],
+    "q3_graph_capture_end": [P, PP],
+    "q3_graph_launch": [P, P],
+    "q3_graph_destroy": [P],
     "q3_event_create": [PP],
     "q3_event_destroy": [P],
     "q3_event_record": [P, P],
@@ -61,6 +65,7 @@ SIGNATURES = {
     "q3_quantize_q8_0": [P, I64, P],
     "q3_gemv_q8": [P, P, P, I, I, P],
     "q3_gemv_q8_cuda_order": [P, P, P, I, I, P],
+    "q3_gemv_q8_overlapped": [P, P, P, I, I, P],
     "q3_gemv_q8_layers": [P, I64, P, P, I, I, I, P],
     "q3_gemv_q8_norm": [P, P, P, P, I, I, P],
     "q3_gemv_q8_resid": [P, P, P, P, I, I, P],
@@ -76,6 +81,8 @@ SIGNATURES = {
     "q3_iree_dispatch_18": [P, P, P, U32, U32, P],
     "q3_iree_dispatch_20": [P, P, P, U32, U32, P],
     "q3_iree_dispatch_24": [P, P, P, U32, P],
+    "q3_fused_layer_workspace_bytes": [],
+    "q3_fused_layer": [ctypes.POINTER(Weights), I, P, P, P, P, I64, P, P, P, P, P],
     "q3_model_create": [ctypes.POINTER(Weights), I64, P, PP],
     "q3_model_destroy": [P],
     "q3_model_stream": [P],
@@ -106,6 +113,8 @@ SIGNATURES = {
     "q3_batch_read": [P, P, P, ctypes.POINTER(ctypes.c_int)],
     "q3_batch_read_argmax": [P, P],
     "q3_model_trace_kernels": [P, I64, P, P, I64, PI64],
+    "q3_model_trace_phases": [P, I64, P, I64, PI64, ctypes.POINTER(ctypes.c_int),
+                              ctypes.POINTER(ctypes.c_int)],
     "q3_batch_trace_kernels": [P, I64, P, P, I64, PI64],
     "q3_batch_attention_workspace_bytes": [I64, I],
     "q3_batch_attention": [P, P, P, P, P, I64, P, P, I, I64, I, P, P, P, P],
@@ -119,6 +128,7 @@ _RESTYPE = {
     "q3_last_error": ctypes.c_char_p,
     "q3_vocab_argmax_workspace_bytes": SZ,
     "q3_attention_workspace_bytes": SZ,
+    "q3_fused_layer_workspace_bytes": SZ,
     "q3_model_stream": P,
     "q3_bvocab_workspace_bytes": SZ,
     "q3_batch_attention_workspace_bytes": SZ,

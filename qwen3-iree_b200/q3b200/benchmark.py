@@ -150,6 +150,152 @@ def gemv_stream(dw, name: str, reps: int = 20, warmup: int = 3) -> dict:
     return {"us_per_launch": us, "bytes": b, "gbs": b / (us * 1e-6) / 1e9, "l2": "flushed"}
 
 
+class _Graph:
+    """A CUDA graph of the calls made inside `with` on a created stream."""
+
+    def __init__(self, stream):
+        self.stream, self.exec = stream, None
+
+    def __enter__(self):
+        from ._lib import call
+
+        call("q3_graph_capture_begin", self.stream)
+        return self
+
+    def __exit__(self, *exc):
+        import ctypes
+
+        from ._lib import call
+
+        e = ctypes.c_void_p()
+        call("q3_graph_capture_end", self.stream, ctypes.byref(e))
+        self.exec = e.value
+        return False
+
+    def launch(self):
+        from ._lib import call
+
+        call("q3_graph_launch", self.exec, self.stream)
+
+    def close(self):
+        from ._lib import lib
+
+        if self.exec:
+            lib().q3_graph_destroy(self.exec)
+            self.exec = None
+
+
+def _stream():
+    import ctypes
+
+    from ._lib import call
+
+    s = ctypes.c_void_p()
+    call("q3_stream_create", ctypes.byref(s))
+    return s.value
+
+
+# BASELINE configs[0]: one attn_q-shaped Q8_0 GEMV [2048, 1024]
+GEMV_POOL = 64            # distinct weight matrices (143 MB, larger than the 126 MB L2)
+GEMV_N, GEMV_K = 2048, 1024
+GEMV_ALG_BYTES = GEMV_N * (GEMV_K // 32) * 34 + 2 * GEMV_K + 2 * GEMV_N
+
+
+def gemv_pool(seed: int = 0, reps: int = 20, warmup: int = 3) -> dict:
+    """the attn_q GEMV over a rotating pool of 64 seeded matrices
+    (W N(0,0.02) quantised Q8_0, x N(0,1) f16), larger than L2, so every call
+    reads its weights from HBM.  One CUDA graph holds a call per matrix:
+    q3_gemv_q8_overlapped (each call's weight copies start while the previous
+    call runs) and, for comparison, q3_gemv_q8 (each call after the previous
+    one).  Device time of whole replays / calls."""
+    from . import DeviceArray, Events
+    from ._lib import call
+    from .weights import make_q8_matrix
+
+    rng = np.random.default_rng(seed)
+    mats = [make_q8_matrix(rng, GEMV_N, GEMV_K) for _ in range(GEMV_POOL)]
+    w = DeviceArray.from_host(np.stack(mats))
+    x = DeviceArray.from_host(rng.standard_normal(GEMV_K).astype(np.float16))
+    y = DeviceArray((GEMV_POOL, GEMV_N), np.float16)
+    bpm = mats[0].nbytes
+    st = _stream()
+    ev = Events()
+    out = {"workload": f"configs[0]: Q8_0 GEMV [{GEMV_N},{GEMV_K}], a rotating pool of "
+                       f"{GEMV_POOL} matrices ({GEMV_POOL * bpm / 1e6:.0f} MB > L2)",
+           "alg_bytes_per_call": GEMV_ALG_BYTES}
+    for name in ("q3_gemv_q8_overlapped", "q3_gemv_q8"):
+        g = _Graph(st)
+        with g:
+            for i in range(GEMV_POOL):
+                call(name, w.ptr + i * bpm, x.ptr, y.ptr + i * GEMV_N * 2, GEMV_N, GEMV_K, st)
+        for _ in range(warmup):
+            g.launch()
+        ev.record_start(st)
+        for _ in range(reps):
+            g.launch()
+        ev.record_end(st)
+        us = ev.elapsed_ms() * 1e3 / (reps * GEMV_POOL)
+        g.close()
+        out[name] = {"us_per_call": us, "gbs": GEMV_ALG_BYTES / (us * 1e-6) / 1e9}
+    from ._lib import lib
+
+    lib().q3_stream_destroy(st)
+    return out
+
+
+# BASELINE configs[1]: one decoder layer at position 511 over a 512-position cache
+LAYER_S, LAYER_POS = 512, 511
+LAYER_ALG_BYTES = (2228224 + 2 * 1114112 + 2228224 + 6684672 + 3342336  # Q8_0 weights
+                   + 4 * 1024 * 2 + 2 * 128 * 2                          # gammas
+                   + 2 * (LAYER_POS + 1) * 8 * 128 * 2                   # K and V read
+                   + 2 * 8 * 128 * 2                                     # new K/V row written
+                   + 2 * 1024 * 2)                                       # x in, x out
+
+
+def layer_bench(dw, seed: int = 0, reps: int = 10, warmup: int = 3) -> dict:
+    """q3_fused_layer at position 511 over a cache of 512
+    positions (511 cached N(0,1) rows).  One CUDA graph runs the layer once
+    for each of the 28 layers' weights (468 MB, larger than L2), each over its
+    own cache slice; device time per layer call."""
+    import ctypes
+
+    from . import DeviceArray, Events
+    from ._lib import call, lib
+
+    rng = np.random.default_rng(seed)
+    S, pos = LAYER_S, LAYER_POS
+    kv = rng.standard_normal((28 * S, 8, 128)).astype(np.float16)
+    kc, vc = DeviceArray.from_host(kv), DeviceArray.from_host(kv[::-1].copy())
+    xs = [DeviceArray.from_host(rng.standard_normal(1024).astype(np.float16)) for _ in range(2)]
+    dpos = DeviceArray.from_host(np.array([pos], np.int64))
+    c = np.empty((S, 64), np.float32)
+    sn = np.empty((S, 64), np.float32)
+    call("q3_rope_table", S, c.ctypes.data, sn.ctypes.data)
+    dc, ds = DeviceArray.from_host(c), DeviceArray.from_host(sn)
+    ws = DeviceArray((lib().q3_fused_layer_workspace_bytes(),), np.uint8, zero=True)
+    st = _stream()
+    g = _Graph(st)
+    with g:
+        for l in range(28):
+            call("q3_fused_layer", ctypes.byref(dw.struct), l, xs[l % 2].ptr, xs[(l + 1) % 2].ptr,
+                 kc.ptr, vc.ptr, S, dpos.ptr, dc.ptr, ds.ptr, ws.ptr, st)
+    ev = Events()
+    for _ in range(warmup):
+        g.launch()
+    ev.record_start(st)
+    for _ in range(reps):
+        g.launch()
+    ev.record_end(st)
+    us = ev.elapsed_ms() * 1e3 / (reps * 28)
+    g.close()
+    lib().q3_stream_destroy(st)
+    return {"workload": "configs[1]: one decoder layer at position 511, cache of 512 positions, "
+                        "the 28 layers' weights in turn (468 MB > L2)",
+            "call": "q3_fused_layer (attention block, feed-forward block, residual rebuild)",
+            "us_per_layer": us, "alg_bytes_per_layer": LAYER_ALG_BYTES,
+            "gbs": LAYER_ALG_BYTES / (us * 1e-6) / 1e9}
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description="Benchmark Qwen3-0.6B Q8_0 decode on libq3b200.so")
     ap.add_argument("--max-tokens", type=int, default=MAX_TOKENS)

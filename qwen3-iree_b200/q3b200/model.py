@@ -118,7 +118,7 @@ class Qwen3Decoder:
         n = self.launches_per_step()
         return t[:n].copy(), k[:n].copy()
 
-    ENGINES = {"graph": 0, "persistent": 1}
+    ENGINES = {"graph": 0, "persistent": 1, "fused": 2}
 
     def set_engine(self, name: str) -> None:
         call("q3_model_set_engine", self.handle, self.ENGINES[name])
@@ -137,6 +137,16 @@ class Qwen3Decoder:
         call("q3_model_trace_steps", self.handle, int(steps), int(trace_step), out.ctypes.data,
              cap, ctypes.byref(c), ctypes.byref(p))
         return out[:c.value * p.value * 4].reshape(c.value, p.value, 4)
+
+    def trace_phases(self, steps: int = 4) -> np.ndarray:
+        """Fused engine: [56 launches, 128 CTAs, phases] global-timer stamps (ns)
+        of the last of `steps` steps."""
+        cap = 56 * 128 * 16
+        out = np.zeros(cap, np.int64)
+        nl, c, p = ctypes.c_int64(), ctypes.c_int(), ctypes.c_int()
+        call("q3_model_trace_phases", self.handle, int(steps), out.ctypes.data, cap,
+             ctypes.byref(nl), ctypes.byref(c), ctypes.byref(p))
+        return out[:nl.value * c.value * p.value].reshape(nl.value, c.value, p.value)
 
     def kernel_launches(self) -> int:
         n = ctypes.c_int64(0)
@@ -254,6 +264,16 @@ class BatchDecoder:
         out = np.zeros((self.B, self.max_seq_len + 1), np.int64)
         call("q3_batch_read_argmax", self.handle, out.ctypes.data)
         return out
+
+    def trace_phases(self, steps: int = 4) -> np.ndarray:
+        """Fused engine: [56 launches, 128 CTAs, phases] global-timer stamps (ns)
+        of the last of `steps` steps."""
+        cap = 56 * 128 * 16
+        out = np.zeros(cap, np.int64)
+        nl, c, p = ctypes.c_int64(), ctypes.c_int(), ctypes.c_int()
+        call("q3_model_trace_phases", self.handle, int(steps), out.ctypes.data, cap,
+             ctypes.byref(nl), ctypes.byref(c), ctypes.byref(p))
+        return out[:nl.value * c.value * p.value].reshape(nl.value, c.value, p.value)
 
     def kernel_launches(self) -> int:
         n = ctypes.c_int64(0)

@@ -1,5 +1,6 @@
 """The whole decode path (28 layers, vocab head, argmax, generate loop)
-through the C ABI vs the CPU oracle: logits bit for bit, greedy tokens
+through the C ABI vs the CPU oracle, for each engine against the oracle in
+that engine's summation orders: logits bit for bit, greedy tokens
 identical over 256 steps, the reference's end-of-text
 rule, and the chat state machine."""
 import numpy as np
@@ -11,18 +12,25 @@ pytestmark = pytest.mark.gpu
 EOS = 151645
 
 
-@pytest.fixture(params=["persistent", "graph"])
+@pytest.fixture(params=["persistent", "graph", "fused"])
 def engine(request):
     return request.param
 
 
 @pytest.fixture(scope="module")
-def models(gpu, O, model_weights):
+def oracles(gpu, O, model_weights):
     from q3b200.weights import to_oracle_dict
 
     dw = gpu.DeviceWeights(model_weights)
-    om = O.Model(to_oracle_dict(model_weights))
-    return dw, om
+    od = to_oracle_dict(model_weights)
+    return dw, {"exact": O.Model(od, order=O.ORDER_EXACT), "fused": O.Model(od, order=O.ORDER_FUSED)}
+
+
+@pytest.fixture
+def models(oracles, engine):
+    """(device weights, the oracle in the engine's summation orders)"""
+    dw, oms = oracles
+    return dw, oms["fused" if engine == "fused" else "exact"]
 
 
 def test_decode_steps_bit_exact(gpu, O, models, engine):

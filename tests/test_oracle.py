@@ -197,3 +197,17 @@ def test_attention_vs_float64(O, T):
     q = rng.standard_normal(2048).astype(np.float16)
     got = O.attention(q, kc, vc, slot0, T)
     assert rel_l2(got, _attn_ref(q, kc, vc, slot0, T)) < 1e-3
+
+
+def test_oracle_weight_generator_matches_library(O, q3):
+    """bench.py's CPU legs build their weights with the oracle's generator and
+    quantizer (never the product library); both generators must give the same
+    bytes for the same seed."""
+    from q3b200.weights import synthetic_weights, to_oracle_dict
+
+    a = O.synthetic_weights(seed=5, layers=2)
+    b = to_oracle_dict(synthetic_weights(seed=5, layers=2))
+    assert set(a) == set(b)
+    for k in a:
+        assert a[k].shape == b[k].shape, k
+        assert np.array_equal(a[k].view(np.uint8), b[k].view(np.uint8)), k

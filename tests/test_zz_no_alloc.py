@@ -36,7 +36,7 @@ def _setup(q3, seed):
     return dict(kc=kc, vc=vc, c=c, s=s, gq=gq, gk=gk, qkv=qkv)
 
 
-def _run(q3, d, positions, noalloc):
+def _run(q3, d, positions, noalloc, stream=None):
     L = q3.lib()
     kc, vc = _up(q3, d["kc"]), _up(q3, d["vc"])
     c, s, gq, gk = _up(q3, d["c"]), _up(q3, d["s"]), _up(q3, d["gq"]), _up(q3, d["gk"])
@@ -49,11 +49,13 @@ def _run(q3, d, positions, noalloc):
         out.fill_bytes(0xFF)
         if noalloc:
             rc = L.q3_decode_attention_noalloc(qkv.ptr, gq.ptr, gk.ptr, c.ptr, s.ptr, S, kc.ptr,
-                                               vc.ptr, LAYER * S, S, p.ptr, out.ptr, None)
+                                               vc.ptr, LAYER * S, S, p.ptr, out.ptr, stream)
         else:
             rc = L.q3_decode_attention(qkv.ptr, gq.ptr, gk.ptr, c.ptr, s.ptr, S, kc.ptr, vc.ptr,
-                                       LAYER * S, S, p.ptr, out.ptr, ws.ptr, None)
+                                       LAYER * S, S, p.ptr, out.ptr, ws.ptr, stream)
         assert rc == 0, L.q3_last_error()
+        if stream is not None:
+            assert L.q3_stream_synchronize(stream) == 0
         outs.append(out.download())
     return outs, kc.download(), vc.download()
 
@@ -76,3 +78,31 @@ def test_noalloc_attention_rejects_contexts_beyond_its_scratch(gpu):
     rc = L.q3_decode_attention_noalloc(p, p, p, p, p, 8192, p, p, 0, 8192, p, p, None)
     assert rc == 1
     assert b"4096" in L.q3_last_error()
+
+
+def test_noalloc_attention_on_a_created_stream(gpu):
+    """Two calls in a row on a non-default stream: the counter clear of each
+    call is ordered on that stream before its kernel."""
+    L = gpu.lib()
+    st = ctypes.c_void_p()
+    assert L.q3_stream_create(ctypes.byref(st)) == 0
+    try:
+        d = _setup(gpu, 77)
+        want, wk, wv = _run(gpu, d, (700, 701), noalloc=False, stream=st)
+        got, gk, gv = _run(gpu, d, (700, 701), noalloc=True, stream=st)
+    finally:
+        L.q3_stream_destroy(st)
+    for w, g in zip(want, got):
+        assert np.array_equal(w.view(np.uint16), g.view(np.uint16))
+    assert np.array_equal(wk.view(np.uint16), gk.view(np.uint16))
+
+
+def test_noalloc_attention_rejects_a_misaligned_output(gpu):
+    """out is stored 4 f16 at a time: a buffer off an 8-byte boundary is
+    refused on the host before anything is launched."""
+    L = gpu.lib()
+    buf = gpu.DeviceArray((64,), np.uint8, zero=True)
+    p = buf.ptr
+    rc = L.q3_decode_attention_noalloc(p, p, p, p, p, 16, p, p, 0, 16, p, p + 2, None)
+    assert rc == 1
+    assert b"8-byte" in L.q3_last_error()
