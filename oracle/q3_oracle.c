@@ -578,45 +578,126 @@ void q3o_attention(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, in
   }
 }
 
-/* The fused engine's attention (k_fused_attn): the same chunk partials;
- * chunk c belongs to cluster rank c % 16.  Rank r folds its chunks
- * (ascending c):  M_r = max m_c,  e_c = exp(m_c - M_r),  l_r = fma chain of
- * l_c * e_c,  o_r = fma chain of o_c * e_c  (a rank without chunks has
- * M_r = -inf, l_r = o_r = 0).  The cluster folds the ranks the same way
- * (M = max M_r, E_r = exp(M_r - M), chains over r = 0..15); out = f16(O / L). */
+/* The fused engine's attention (k_fused_attn).  Chunks of 8 keys; key t's
+ * dot is split in four quarters of 32 dims (fma chains), combined as
+ * (a0 + a1) + (a2 + a3), times rsqrt(128); per chunk m = max s_t,
+ * p_t = exp(s_t - m) (0 past the end), l = ((p0 + p1) + (p2 + p3)) +
+ * ((p4 + p5) + (p6 + p7)), o_d = fma chain of p_t * v_td over t.  Chunk c
+ * belongs to cluster rank c % 16 as local chunk j = c / 16, handled by warp
+ * j % 8 in pass j / 8; a warp folds its chunks in pass order with the
+ * pairwise merge of q3o_attention (att_merge); rank r folds its 8 warps
+ * (M_r = max m_w, e_w = exp(m_w - M_r), fma chains of l_w * e_w and
+ * o_w * e_w over w, warps without chunks skipped), the cluster folds the
+ * ranks the same way (ranks without chunks skipped) and out = f16(O / L). */
+static void att_chunk8(const float* qf, const uint16_t* kc, const uint16_t* vc, int64_t slot0,
+                       int kvh, int64_t c, int64_t T, att_part* out) {
+  const int64_t row = (int64_t)Q3O_NKV * Q3O_HD;
+  float s[8], p[8];
+  for (int l = 0; l < 8; ++l) {
+    const int64_t t = c * 8 + l;
+    if (t < T) {
+      const uint16_t* k = kc + (slot0 + t) * row + kvh * Q3O_HD;
+      float a[4];
+      for (int q = 0; q < 4; ++q) {
+        float acc = 0.0f;
+        for (int d = 32 * q; d < 32 * q + 32; ++d) acc = fmaf(qf[d], q3o_h2f(k[d]), acc);
+        a[q] = acc;
+      }
+      s[l] = ((a[0] + a[1]) + (a[2] + a[3])) * kAttnScale;
+    } else {
+      s[l] = -INFINITY;
+    }
+  }
+  float m = -INFINITY;
+  for (int l = 0; l < 8; ++l) m = fmaxf(m, s[l]);
+  for (int l = 0; l < 8; ++l) p[l] = (c * 8 + l < T) ? q3o_expf(s[l] - m) : 0.0f;
+  out->m = m;
+  out->l = ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
+  for (int d = 0; d < Q3O_HD; ++d) out->o[d] = 0.0f;
+  for (int l = 0; l < 8 && c * 8 + l < T; ++l) {
+    const uint16_t* v = vc + (slot0 + c * 8 + l) * row + kvh * Q3O_HD;
+    for (int d = 0; d < Q3O_HD; ++d) out->o[d] = fmaf(p[l], q3o_h2f(v[d]), out->o[d]);
+  }
+}
+
+/* max-first fold of n partials (those with have[i]) into *out */
+static void att_fold_maxfirst(const att_part* p, const int* have, int n, att_part* out) {
+  out->m = -INFINITY;
+  out->l = 0.0f;
+  for (int d = 0; d < Q3O_HD; ++d) out->o[d] = 0.0f;
+  for (int i = 0; i < n; ++i)
+    if (have[i]) out->m = fmaxf(out->m, p[i].m);
+  for (int i = 0; i < n; ++i) {
+    if (!have[i]) continue;
+    const float e = q3o_expf(p[i].m - out->m);
+    out->l = fmaf(p[i].l, e, out->l);
+    for (int d = 0; d < Q3O_HD; ++d) out->o[d] = fmaf(p[i].o[d], e, out->o[d]);
+  }
+}
+
 void q3o_attention_fused(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
                          int64_t slot0, int64_t T, uint16_t* out) {
-  const int64_t nchunks = (T + Q3O_ATT_CHUNK - 1) / Q3O_ATT_CHUNK;
-  att_part* ch = (att_part*)malloc(sizeof(att_part) * (size_t)nchunks);
+  enum { R = Q3O_FUSED_CLUSTER, W = 8 };
+  const int64_t nchunks = (T + 7) / 8;
   for (int h = 0; h < Q3O_NQ; ++h) {
     const int kvh = h / 2;
     float qf[Q3O_HD];
     x_to_f32(q + h * Q3O_HD, qf, Q3O_HD);
-    for (int64_t c = 0; c < nchunks; ++c) att_chunk(qf, kc, vc, slot0, kvh, c, T, &ch[c]);
-    att_part rk[Q3O_FUSED_CLUSTER];
-    for (int r = 0; r < Q3O_FUSED_CLUSTER; ++r) {
-      att_part* p = &rk[r];
-      p->m = -INFINITY;
-      p->l = 0.0f;
-      for (int d = 0; d < Q3O_HD; ++d) p->o[d] = 0.0f;
-      for (int64_t c = r; c < nchunks; c += Q3O_FUSED_CLUSTER) p->m = fmaxf(p->m, ch[c].m);
-      for (int64_t c = r; c < nchunks; c += Q3O_FUSED_CLUSTER) {
-        const float e = q3o_expf(ch[c].m - p->m);
-        p->l = fmaf(ch[c].l, e, p->l);
-        for (int d = 0; d < Q3O_HD; ++d) p->o[d] = fmaf(ch[c].o[d], e, p->o[d]);
+    att_part rk[R];
+    int rk_have[R];
+    for (int r = 0; r < R; ++r) {
+      att_part wp[W];
+      int w_have[W];
+      for (int w = 0; w < W; ++w) {
+        w_have[w] = 0;
+        for (int64_t j = w; r + (int64_t)R * j < nchunks; j += W) {
+          att_part ch;
+          att_chunk8(qf, kc, vc, slot0, kvh, r + (int64_t)R * j, T, &ch);
+          if (!w_have[w])
+            wp[w] = ch;
+          else
+            att_merge(&wp[w], &ch);
+          w_have[w] = 1;
+        }
       }
+      att_fold_maxfirst(wp, w_have, W, &rk[r]);
+      rk_have[r] = r < nchunks;
     }
-    float M = -INFINITY, L = 0.0f, O[Q3O_HD];
-    for (int r = 0; r < Q3O_FUSED_CLUSTER; ++r) M = fmaxf(M, rk[r].m);
-    for (int d = 0; d < Q3O_HD; ++d) O[d] = 0.0f;
-    for (int r = 0; r < Q3O_FUSED_CLUSTER; ++r) {
-      const float E = q3o_expf(rk[r].m - M);
-      L = fmaf(rk[r].l, E, L);
-      for (int d = 0; d < Q3O_HD; ++d) O[d] = fmaf(rk[r].o[d], E, O[d]);
-    }
-    for (int d = 0; d < Q3O_HD; ++d) out[h * Q3O_HD + d] = q3o_f2h(O[d] / L);
+    att_part tot;
+    att_fold_maxfirst(rk, rk_have, R, &tot);
+    for (int d = 0; d < Q3O_HD; ++d) out[h * Q3O_HD + d] = q3o_f2h(tot.o[d] / tot.l);
   }
-  free(ch);
+}
+
+/* The fused engine's RMSNorm of the residual stream: the 16 ranks of a
+ * cluster each rebuild 64 elements (rank r: 64r .. 64r+63, lane t of 16:
+ * 4t .. 4t+3); a lane's sum of squares is an fma chain over its 4 elements,
+ * the rank's is the butterfly over its 16 lanes (offsets 8, 4, 2, 1), and
+ * ss = ((ss_0 + ss_1) + ...) + ss_15.  Then r = sqrt(ss/1024 + eps) and
+ * y = f16((x / r) * g) as in q3o_rmsnorm. */
+static void rmsnorm_fused(const uint16_t* x, const uint16_t* g, uint16_t* y) {
+  float xf[Q3O_DIM];
+  x_to_f32(x, xf, Q3O_DIM);
+  float ss = 0.0f;
+  for (int r = 0; r < 16; ++r) {
+    float a[16];
+    for (int t = 0; t < 16; ++t) {
+      float acc = 0.0f;
+      for (int i = 0; i < 4; ++i) {
+        const float v = xf[64 * r + 4 * t + i];
+        acc = fmaf(v, v, acc);
+      }
+      a[t] = acc;
+    }
+    for (int off = 8; off > 0; off >>= 1) {
+      float b[16];
+      for (int t = 0; t < 16; ++t) b[t] = a[t] + a[t ^ off];
+      for (int t = 0; t < 16; ++t) a[t] = b[t];
+    }
+    ss = r == 0 ? a[0] : ss + a[0];
+  }
+  const float rn = sqrtf(ss / (float)Q3O_DIM + kEps);
+  for (int k = 0; k < Q3O_DIM; ++k) y[k] = q3o_f2h((xf[k] / rn) * q3o_h2f(g[k]));
 }
 
 /* The fused engine's split GEMV (k_fused_attn's W_o slice, k_fused_ffn's
@@ -684,7 +765,11 @@ void q3o_layer(const q3o_weights* w, int layer, uint16_t* x, int64_t pos, uint16
                uint16_t* vc, int64_t S) {
   uint16_t xn[Q3O_DIM], q[2048], k[1024], v[1024], qn[2048], kn[1024], att[2048], o[1024],
       h1[1024], hn[1024], gu[6144], act[3072], d[1024];
-  q3o_rmsnorm(x, w->attn_norm + layer * Q3O_DIM, xn, Q3O_DIM);
+  const int fused = w->order == Q3O_ORDER_FUSED;
+  if (fused)
+    rmsnorm_fused(x, w->attn_norm + layer * Q3O_DIM, xn);
+  else
+    q3o_rmsnorm(x, w->attn_norm + layer * Q3O_DIM, xn, Q3O_DIM);
   q3o_gemv_q8_mlir(w->q8_q + layer * kBplQ, xn, q, 2048, 1024);
   q3o_gemv_q8_mlir(w->q8_k + layer * kBplKV, xn, k, 1024, 1024);
   q3o_gemv_q8_mlir(w->q8_v + layer * kBplKV, xn, v, 1024, 1024);
@@ -693,7 +778,6 @@ void q3o_layer(const q3o_weights* w, int layer, uint16_t* x, int64_t pos, uint16
   const int64_t slot = (int64_t)layer * S + pos;
   memcpy(kc + slot * 1024, kn, sizeof(kn));
   memcpy(vc + slot * 1024, v, sizeof(v));
-  const int fused = w->order == Q3O_ORDER_FUSED;
   if (fused)
     q3o_attention_fused(qn, kc, vc, (int64_t)layer * S, pos + 1, att);
   else
@@ -703,7 +787,10 @@ void q3o_layer(const q3o_weights* w, int layer, uint16_t* x, int64_t pos, uint16
   else
     q3o_gemv_q8_mlir(w->q8_o + layer * kBplO, att, o, 1024, 2048);
   q3o_add_f16(x, o, h1, Q3O_DIM);
-  q3o_rmsnorm(h1, w->ffn_norm + layer * Q3O_DIM, hn, Q3O_DIM);
+  if (fused)
+    rmsnorm_fused(h1, w->ffn_norm + layer * Q3O_DIM, hn);
+  else
+    q3o_rmsnorm(h1, w->ffn_norm + layer * Q3O_DIM, hn, Q3O_DIM);
   q3o_gemv_q8_mlir(w->q8_gate_up + layer * kBplGU, hn, gu, 6144, 1024);
   q3o_swiglu(gu, act, Q3O_FFN);
   if (fused)

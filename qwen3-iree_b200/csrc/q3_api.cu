@@ -370,6 +370,48 @@ static cudaError_t launch_cluster_x(void (*k)(KArgs...), dim3 grid, dim3 block, 
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+// Tensor maps are encoded through the driver entry point
+// cuTensorMapEncodeTiled (no link-time libcuda dependency).
+typedef CUresult (*PfnEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PfnEncodeTiled encode_fn() {
+  static PfnEncodeTiled fn = nullptr;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PfnEncodeTiled)p;
+  }
+  return fn;
+}
+
+// 2-D map over a row-major matrix: `inner` elements per row, `outer` rows,
+// rows `row_bytes` apart; box {box_inner, box_outer}.
+static int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                       uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                       CUtensorMapSwizzle sw) {
+  PfnEncodeTiled fn = encode_fn();
+  if (!fn) return set_err(Q3_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+  Q3_REQUIRE(((uintptr_t)base & 15u) == 0 && row_bytes % 16 == 0,
+             "tensor map base / row stride must be 16-byte aligned");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_err(Q3_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return Q3_OK;
+}
+
 struct LaunchShape {
   int grid, nstages;
   size_t smem;
@@ -755,6 +797,34 @@ extern "C" int q3_decode_attention_noalloc(const void* qkv, const void* q_norm, 
 }
 
 // One layer of the fused engine on caller buffers ------------------------------
+// Tensor maps of the fused kernels: W_o and W_down of all layers as u32
+// matrices (boxes: a head pair's 272-byte slice of 64 rows; a slice's
+// 416-byte window of 64 rows), the K cache (64-dim half boxes, 128-byte
+// swizzle) and the V cache of `slots` positions.
+struct FusedMaps {
+  CUtensorMap wo, k, v, wd;
+};
+
+static int make_fused_maps(FusedMaps* f, const q3_weights* w, const void* kc, const void* vc,
+                           int64_t slots) {
+  int rc = make_map_2d(&f->wo, CU_TENSOR_MAP_DATA_TYPE_UINT32, w->q8_attn_output, kORowBytes / 4,
+                       (uint64_t)kLayers * kDim, kORowBytes, kFaOBytes / 4, kFaORows,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc == Q3_OK)
+    rc = make_map_2d(&f->k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kc, (uint64_t)kNKV * kHD,
+                     (uint64_t)slots, (uint64_t)kNKV * kHD * 2, 64, kFaChunk,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc == Q3_OK)
+    rc = make_map_2d(&f->v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, vc, (uint64_t)kNKV * kHD,
+                     (uint64_t)slots, (uint64_t)kNKV * kHD * 2, kHD, kFaChunk,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc == Q3_OK)
+    rc = make_map_2d(&f->wd, CU_TENSOR_MAP_DATA_TYPE_UINT32, w->q8_ffn_down, kDRowBytes / 4,
+                     (uint64_t)kLayers * kDim, kDRowBytes, kFbDWin / 4, kFbDRows,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+  return rc;
+}
+
 // The fused kernels' attributes (dynamic shared memory above 48 KB, 16-CTA
 // clusters), set once per device.
 static int fused_attrs() {
@@ -801,6 +871,9 @@ extern "C" int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, 
   int rc_ = Q3_OK;
   cudaStream_t st = (cudaStream_t)stream;
   FusedLayerWs* f = (FusedLayerWs*)ws;
+  FusedMaps maps;
+  rc_ = make_fused_maps(&maps, w, kc, vc, (int64_t)(layer + 1) * S);
+  if (rc_) return rc_;
   Q3_CUDA(cudaMemsetAsync(&f->seq, 0, sizeof(SeqState), st));
   Q3_CUDA(cudaMemcpyAsync(&f->seq.pos, pos, sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
   rc_ = fused_attrs();
@@ -810,7 +883,10 @@ extern "C" int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, 
   fa.wq = (const uint8_t*)w->q8_attn_q + layer * kBplQ;
   fa.wk = (const uint8_t*)w->q8_attn_k + layer * kBplKV;
   fa.wv = (const uint8_t*)w->q8_attn_v + layer * kBplKV;
-  fa.wo = (const uint8_t*)w->q8_attn_output + layer * kBplO;
+  fa.wo_map = maps.wo;
+  fa.k_map = maps.k;
+  fa.v_map = maps.v;
+  fa.layer = layer;
   fa.attn_norm = (const uint16_t*)w->attn_norm + layer * kDim;
   fa.q_norm = (const uint16_t*)w->attn_q_norm + layer * kHD;
   fa.k_norm = (const uint16_t*)w->attn_k_norm + layer * kHD;
@@ -829,7 +905,8 @@ extern "C" int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, 
   FbArgs fb;
   memset(&fb, 0, sizeof(fb));
   fb.wgu = (const uint8_t*)w->q8_ffn_gate_up + layer * kBplGU;
-  fb.wd = (const uint8_t*)w->q8_ffn_down + layer * kBplD;
+  fb.wd_map = maps.wd;
+  fb.layer = layer;
   fb.ffn_norm = (const uint16_t*)w->ffn_norm + layer * kDim;
   fb.x = f->x;
   fb.opart = f->opart;
@@ -934,6 +1011,7 @@ struct q3_model {
   // cluster kernels per layer), or one persistent kernel
   int engine = Q3_ENGINE_GRAPH;
   float *opart = nullptr, *dpart = nullptr;  // fused engine: split O / down partials [8][1024]
+  struct FusedMaps* fmaps = nullptr;         // fused engine: tensor maps (weights, caches)
   cudaGraphExec_t g_ingest_f = nullptr, g_gen_f = nullptr;
   int launches_gen_f = 0, launches_ingest_f = 0;
   int fused_clusters = 0;        // co-resident 16-CTA clusters of the fused kernels (0: unavailable)
@@ -1115,7 +1193,10 @@ static int enqueue_layers_fused(q3_model* m, bool ingest, int* launches, const S
     fa.wq = (const uint8_t*)m->w.q8_attn_q + l * kBplQ;
     fa.wk = (const uint8_t*)m->w.q8_attn_k + l * kBplKV;
     fa.wv = (const uint8_t*)m->w.q8_attn_v + l * kBplKV;
-    fa.wo = (const uint8_t*)m->w.q8_attn_output + l * kBplO;
+    fa.wo_map = m->fmaps->wo;
+    fa.k_map = m->fmaps->k;
+    fa.v_map = m->fmaps->v;
+    fa.layer = l;
     fa.attn_norm = (const uint16_t*)m->w.attn_norm + l * kDim;
     fa.q_norm = (const uint16_t*)m->w.attn_q_norm + l * kHD;
     fa.k_norm = (const uint16_t*)m->w.attn_k_norm + l * kHD;
@@ -1145,7 +1226,8 @@ static int enqueue_layers_fused(q3_model* m, bool ingest, int* launches, const S
     FbArgs fb;
     memset(&fb, 0, sizeof(fb));
     fb.wgu = (const uint8_t*)m->w.q8_ffn_gate_up + l * kBplGU;
-    fb.wd = (const uint8_t*)m->w.q8_ffn_down + l * kBplD;
+    fb.wd_map = m->fmaps->wd;
+    fb.layer = l;
     fb.ffn_norm = (const uint16_t*)m->w.ffn_norm + l * kDim;
     fb.x = m->x;
     fb.opart = m->opart;
@@ -1228,6 +1310,7 @@ static void model_free(q3_model* m) {
                  m->trace_dev, m->opart, m->dpart};
   for (void* p : dev)
     if (p) cudaFree(p);
+  delete m->fmaps;
   if (m->h_st) cudaFreeHost(m->h_st);
   if (m->h_tokens) cudaFreeHost(m->h_tokens);
   if (m->own_stream && m->stream) cudaStreamDestroy(m->stream);
@@ -1292,6 +1375,12 @@ static int fused_setup(q3_model* m) {
   }
   m->fused_clusters = na < nb ? na : nb;
   if (m->fused_clusters < 1) return Q3_OK;
+  m->fmaps = new FusedMaps();
+  rc = make_fused_maps(m->fmaps, &m->w, m->kc, m->vc, (int64_t)kLayers * m->S);
+  if (rc) {
+    m->fused_clusters = 0;
+    return rc;
+  }
   Q3_CUDA(cudaMalloc((void**)&m->opart, kFParts * kDim * sizeof(float)));
   Q3_CUDA(cudaMalloc((void**)&m->dpart, kFParts * kDim * sizeof(float)));
   Q3_CUDA(cudaMemset(m->opart, 0, kFParts * kDim * sizeof(float)));
@@ -1759,6 +1848,7 @@ extern "C" int q3_model_trace_phases(q3_model* m, int64_t steps, long long* out,
   Q3_REQUIRE(cap >= nl * per, "cap %lld below %lld", (long long)cap, (long long)(nl * per));
   long long* dev = nullptr;
   Q3_CUDA(cudaMalloc((void**)&dev, (size_t)(nl * per) * sizeof(long long)));
+  Q3_CUDA(cudaMemset(dev, 0, (size_t)(nl * per) * sizeof(long long)));
   cudaGraphExec_t g = nullptr;
   int n = 0, ps = 0;
   StepProbe pr;

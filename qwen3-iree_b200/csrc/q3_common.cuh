@@ -387,6 +387,25 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(dsmem_map(local_addr, rank)) : "memory");
   return v;
 }
+// 16-byte store into CTA `rank`'s shared memory at the address `local_addr`
+// has in this CTA (16-byte aligned).  Remote stores are posted: a cluster
+// barrier (arrive.release / wait.acquire) makes them visible to the target.
+__device__ __forceinline__ void st_dsmem_v4(uint32_t local_addr, uint32_t rank, uint4 v) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dsmem_map(local_addr, rank)),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+// 16-byte asynchronous store into CTA `rank`'s shared memory whose arrival
+// completes `bytes` on that CTA's mbarrier (the address `local_bar` has in
+// this CTA): the receiver waits on its own barrier, no cluster barrier needed.
+__device__ __forceinline__ void st_async_v4(uint32_t local_addr, uint32_t rank, uint4 v,
+                                            uint32_t local_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          dsmem_map(local_addr, rank)),
+      "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(dsmem_map(local_bar, rank))
+      : "memory");
+}
 __device__ __forceinline__ uint16_t ld_dsmem_u16(uint32_t local_addr, uint32_t rank) {
   uint16_t v;
   asm volatile("ld.shared::cluster.u16 %0, [%1];" : "=h"(v) : "r"(dsmem_map(local_addr, rank)) : "memory");

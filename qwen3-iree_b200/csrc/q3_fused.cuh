@@ -38,6 +38,7 @@
 #include "q3_attn.cuh"
 #include "q3_common.cuh"
 #include "q3_gemv.cuh"
+#include "q3_tc.cuh"
 
 namespace q3 {
 
@@ -52,16 +53,21 @@ constexpr uint32_t kRow1K = (kDim / kQBlk) * kQBytes;  // 1088: a K = 1024 Q8_0 
 constexpr int kFaORows = kDim / kFC;                 // 64 rows of W_o per CTA
 constexpr uint32_t kORowBytes = (2 * kDim / kQBlk) * kQBytes;  // 2176: a W_o row
 constexpr uint32_t kFaOBytes = 8 * kQBytes;          // 272: a W_o row's 8 blocks of one head pair
-constexpr int kFaAttWarps = 2;                       // warps that own a K/V chunk slot
-constexpr uint32_t kFaKStride = 272;                 // padded K row: lane-per-key reads conflict-free
-constexpr uint32_t kFaKTile = kAttChunk * kFaKStride;  // 8704
-constexpr uint32_t kFaVTile = kAttChunk * kHD * 2;     // 8192
-constexpr uint32_t kFaSlot = kFaKTile + kFaVTile;
+constexpr int kFaAttWarps = 8;                       // every warp owns a K/V chunk slot
+constexpr int kFaChunk = 8;                          // keys per attention chunk
+// A chunk's K tile: two SWIZZLE_128B boxes of 8 keys x 64 dims (one 1024-byte
+// swizzle atom each; the 16-byte reads of 8 keys are bank-conflict free); its
+// V tile: one plain box of 8 keys x 128 dims.  Slots are 1024-byte aligned.
+constexpr uint32_t kFaKHalf = kFaChunk * 64 * 2;       // 1024
+constexpr uint32_t kFaKTile = 2 * kFaKHalf;            // 2048
+constexpr uint32_t kFaVTile = kFaChunk * kHD * 2;      // 2048
+constexpr uint32_t kFaSlot = kFaKTile + kFaVTile;      // 4096
 constexpr uint32_t kFaWqkvBytes = kFaRows * kRow1K;          // 34816
 constexpr uint32_t kFaWoBytes = kFaORows * kFaOBytes;        // 17408
-constexpr uint32_t kFaSmem = kFaWqkvBytes + kFaWoBytes + kFaAttWarps * kFaSlot;  // 86016
-constexpr int kFaMaxLocal = 8;  // chunks per CTA: caches up to 8 * 16 * 32 = 4096 positions
-constexpr int64_t kFusedMaxPositions = (int64_t)kFaMaxLocal * kFC * kAttChunk;
+// dynamic shared memory: K/V slots first (aligned), then the weights
+constexpr uint32_t kFaSmem = 1024 + kFaAttWarps * kFaSlot + kFaWqkvBytes + kFaWoBytes;  // 85248
+constexpr int kFaMaxPasses = 4;  // chunks per warp: caches up to 4 * 8 * 16 * 8 = 4096 positions
+constexpr int64_t kFusedMaxPositions = (int64_t)kFaMaxPasses * kFaAttWarps * kFC * kFaChunk;
 
 // ---- k_fused_ffn
 constexpr int kFbThreads = 384;                      // 12 warps
@@ -80,10 +86,16 @@ static_assert(kFbAct * kFC * kFParts == kFFN, "FFN slices");
 static_assert(kFbThreads / 32 * 2 == kFbAct, "two act values per warp");
 
 struct FaArgs {
+  // W_o of all layers as u32 [28*1024 rows, 544] (box {68, 64}: a head
+  // pair's 272-byte slice of 64 rows); the K cache as f16 [slots, 1024] (box
+  // {64, 32}, SWIZZLE_128B) and the V cache (box {128, 32})
+  CUtensorMap wo_map;
+  CUtensorMap k_map;
+  CUtensorMap v_map;
+  int layer;
   const uint8_t* wq;          // this layer's W_q [2048, 1024] Q8_0 (reference layout)
   const uint8_t* wk;          // W_k [1024, 1024]
   const uint8_t* wv;          // W_v [1024, 1024]
-  const uint8_t* wo;          // W_o [1024, 2048]
   const uint16_t* attn_norm;  // [1024]
   const uint16_t* q_norm;     // [128]
   const uint16_t* k_norm;     // [128]
@@ -108,8 +120,9 @@ struct FaArgs {
 };
 
 struct FbArgs {
+  CUtensorMap wd_map;         // W_down of all layers as u32 [28*1024 rows, 816], box {104, 64}
+  int layer;
   const uint8_t* wgu;         // this layer's W_gate|up [6144, 1024] (gate rows, then up rows)
-  const uint8_t* wd;          // W_down [1024, 3072]
   const uint16_t* ffn_norm;   // [1024]
   const uint16_t* x;          // residual (the attention kernel's x_out)
   const float* opart;         // [8][1024]
@@ -124,7 +137,7 @@ struct FbArgs {
 
 // Phase stamps (latency analysis): thread 0 of each CTA records %globaltimer
 // at the end of each numbered step of the kernels below.
-constexpr int kFPhases = 12;
+constexpr int kFPhases = 16;
 __device__ __forceinline__ void fphase(long long* p, int k) {
   if (p != nullptr && threadIdx.x == 0) {
     long long t;
@@ -149,35 +162,6 @@ __device__ __forceinline__ void load_xblock(const uint16_t* xs, int b, uint32_t 
   }
 }
 
-// x (f16 [1024], xr) -> xs = f16((x / r) * g) in the block layout, r =
-// sqrt(ss/1024 + eps) with ss in warp 0's lane-strided fma order + butterfly
-// (the exact engine's RMSNorm).  gr[i] = g[threadIdx.x + 256 i] for the first
-// 256 threads.  Called by every thread; begins and ends with __syncthreads.
-__device__ __forceinline__ void fused_rmsnorm(const uint16_t* xr, const uint16_t (&gr)[4],
-                                              uint16_t* xs, float* rs) {
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float ss = 0.0f;
-#pragma unroll 8
-    for (int k = threadIdx.x; k < kDim; k += 32) {
-      const float v = h2f(xr[k]);
-      ss = __fmaf_rn(v, v, ss);
-    }
-    ss = warp_sum(ss);
-    if (threadIdx.x == 0) *rs = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kDim), kEps));
-  }
-  __syncthreads();
-  if (threadIdx.x < 256) {
-    const float r = *rs;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = threadIdx.x + 256 * i;
-      xs[xh_index(k)] = rms_apply(xr[k], gr[i], r);
-    }
-  }
-  __syncthreads();
-}
-
 // Per-head RMSNorm + NeoX RoPE (head_norm_rope's operations) of a head held in
 // shared memory.
 __device__ __forceinline__ void head_norm_rope_smem(const uint16_t* x, const uint16_t (&gv)[4],
@@ -200,6 +184,59 @@ __device__ __forceinline__ void head_norm_rope_smem(const uint16_t* x, const uin
   dst[lane + 96] = f2h(__fadd_rn(__fmul_rn(n[1], s1), __fmul_rn(n[3], c1)));
 }
 
+// ---------------------------------------------------------------------------
+// Cluster exchanges.  Every exchange is a push: the producer stores 16-byte
+// pieces into the consumers' shared memory with st.async, whose arrival
+// counts bytes on the consumer's own mbarrier; a consumer waits for its
+// expected byte count and nothing else (no cluster barrier after the release).
+// ---------------------------------------------------------------------------
+constexpr int kFSlice = kDim / kFC;  // 64 residual-stream elements rebuilt per rank
+constexpr uint32_t kFSliceBytes = kFC * (kFSlice * 2 + 16);  // 64 values + (ss, 0, 0, 0) from each rank
+
+// Rank r's slice of the residual stream and its sum of squares, by warp 0
+// (lanes 0-15 hold 4 elements each, v): stored into yloc, pushed with the
+// slice's sum of squares to every rank (xr[64 r ..], xss[r]).  The slice's
+// sum of squares: each lane's fma chain over its 4 elements, then
+// v += shfl_xor(v, 8), (4), (2), (1) over the 16 lanes.  Warp 0 only.
+__device__ __forceinline__ void push_slice(uint2 v, int r, int lane, uint16_t* yloc, uint16_t* xr,
+                                           float4* xss, uint4* ssl, uint64_t* bar) {
+  float acc = 0.0f;
+  const float e[4] = {h2f((uint16_t)(v.x & 0xffffu)), h2f((uint16_t)(v.x >> 16)),
+                      h2f((uint16_t)(v.y & 0xffffu)), h2f((uint16_t)(v.y >> 16))};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc = __fmaf_rn(e[i], e[i], acc);
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+  if (lane < 16) *reinterpret_cast<uint2*>(yloc + 4 * lane) = v;
+  if (lane == 0) *ssl = make_uint4(__float_as_uint(acc), 0u, 0u, 0u);
+  __syncwarp();
+  for (int i = lane; i < 9 * kFC; i += 32) {
+    const int dst = i / 9, piece = i % 9;
+    const uint4 val = piece < 8 ? reinterpret_cast<const uint4*>(yloc)[piece] : *ssl;
+    const uint32_t at = piece < 8 ? smem_u32(xr + kFSlice * r + 8 * piece) : smem_u32(&xss[r]);
+    st_async_v4(at, (uint32_t)dst, val, smem_u32(bar));
+  }
+}
+
+// RMSNorm of the gathered x (xr) with gamma gam (shared memory) into xs
+// (block layout): ss = ((ss_0 + ss_1) + ...) + ss_15 over the ranks' slice
+// sums, r = sqrt(ss/1024 + eps), y = f16((x / r) * g).  Threads 0-255.
+__device__ __forceinline__ void slice_rmsnorm(const uint16_t* xr, const float4* xss,
+                                              const uint16_t* gam, uint16_t* xs) {
+  if (threadIdx.x < 256) {
+    float ss = xss[0].x;
+#pragma unroll
+    for (int q = 1; q < kFC; ++q) ss = __fadd_rn(ss, xss[q].x);
+    const float rn = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kDim), kEps));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = threadIdx.x + 256 * i;
+      xs[xh_index(k)] = rms_apply(xr[k], gam[k], rn);
+    }
+  }
+  __syncthreads();
+}
+
 // ===========================================================================
 // k_fused_attn: grid 8 clusters x 16 CTAs, 256 threads.
 // ===========================================================================
@@ -211,24 +248,33 @@ __device__ __forceinline__ void head_norm_rope_smem(const uint16_t* x, const uin
 // chunks: M_r = max_j m_j, e_j = exp(m_j - M_r), l_r = fma chain of l_j * e_j
 // over j, o_r = fma chain of o_j * e_j.  The cluster folds the ranks the same
 // way (M = max M_r, E_r = exp(M_r - M), chains over r = 0..15) and
-// out_d = f16(O_d / L).  A rank without chunks contributes M_r = -inf.
+// out_d = f16(O_d / L); rank q folds output dims 16q .. 16q+15.  A rank
+// without chunks contributes M_r = -inf.
 __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_constant__ FaArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* wqkv = smem;
-  uint8_t* wo = smem + kFaWqkvBytes;
-  uint8_t* kvs = wo + kFaWoBytes;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* kvs = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
+  uint8_t* wqkv = kvs + kFaAttWarps * kFaSlot;
+  uint8_t* wo = wqkv + kFaWqkvBytes;
   __shared__ __align__(16) uint16_t xr[kDim];
+  __shared__ __align__(16) float4 xss[kFC];
+  __shared__ __align__(16) uint16_t yloc[kFSlice];
+  __shared__ __align__(16) uint4 ssl;
   __shared__ __align__(16) uint16_t xs[kDim / kQBlk * kXhStride];
   __shared__ __align__(16) uint16_t loc[kFaRows];
   __shared__ __align__(16) uint16_t qkv_h[4 * kHD];  // q head 2h | q head 2h+1 | k | v (raw)
   __shared__ __align__(16) uint16_t qs[2][kHD];
   __shared__ __align__(16) uint16_t ks[kHD];
-  __shared__ __align__(16) AttnPartial part[kFaMaxLocal][2];
+  __shared__ __align__(16) AttnPartial part[kFaAttWarps][2];  // each warp's running fold
   __shared__ __align__(16) AttnPartial cpart[2];
-  __shared__ __align__(16) float2 pw[kFaAttWarps][kAttChunk];
+  // this rank's share of the cluster fold: from every rank q, (M, l, -, -,
+  // o[16 dims]) of the output dims 16r .. 16r+15 of the head pair
+  __shared__ __align__(16) float fin[kFC][20];
+  __shared__ __align__(16) uint16_t fout[16];
   __shared__ __align__(16) uint16_t att[2 * kHD / kQBlk * kXhStride];
-  __shared__ __align__(8) uint64_t wbar, kvbar[kFaAttWarps];
-  __shared__ float rs;
+  __shared__ __align__(8) uint64_t wbar, kvbar[kFaAttWarps], xbar, qbar, fbar, abar;
+  __shared__ __align__(16) float rope_c[64], rope_s[64];      // RoPE angles at pos
+  __shared__ __align__(16) uint16_t qkn[2][kHD];              // q_norm, k_norm gammas
+  __shared__ __align__(16) uint16_t gam[kDim];                // attn_norm gamma
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x / kFC;
@@ -238,7 +284,16 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   if (tid == 0) {
     mbar_init(&wbar, 1);
     for (int i = 0; i < kFaAttWarps; ++i) mbar_init(&kvbar[i], 1);
+    mbar_init(&xbar, 1);
+    mbar_init(&qbar, 1);
+    mbar_init(&fbar, 1);
+    mbar_init(&abar, 1);
     fence_mbar_init();
+    // the bytes each exchange brings in from the 16 ranks
+    mbar_expect_tx(&xbar, kFSliceBytes);
+    mbar_expect_tx(&qbar, kFC * 4 * 16);
+    mbar_expect_tx(&fbar, kFC * 5 * 16);
+    mbar_expect_tx(&abar, kFC * 2 * 16);
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -247,86 +302,88 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   // CTA, so a CTA that returns here takes its whole cluster with it.
   if (a.seq->stop != 0) return;
   const int64_t pos = a.seq->pos;
-  if (pos < 0 || pos >= a.S || attn_nchunks(pos) > kFC * kFaMaxLocal) {
+  if (pos < 0 || pos >= a.S || pos >= kFusedMaxPositions) {
     if (tid == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
     return;
   }
   const int64_t T = pos + 1;
-  const int nch = attn_nchunks(pos);
+  const int nch = (int)((T + kFaChunk - 1) / kFaChunk);
   const int nloc = r < nch ? (nch - 1 - r) / kFC + 1 : 0;  // local chunks j: ci = r + 16 j
+  cluster_sync_all();  // every rank's exchange barriers are initialised
 
-  // ---- bulk copies that do not depend on the previous kernel
+  // ---- copies that do not depend on the previous kernel
   const uint64_t pol_w = l2_policy_evict_first();
-  const uint64_t pol_kv = l2_policy_evict_normal();
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_expect_tx(&wbar, kFaWqkvBytes + kFaWoBytes);
-      bulk_g2s(wqkv, a.wq + (int64_t)(2 * kHD * h + kFaQRows * r) * kRow1K, kFaQRows * kRow1K,
-               &wbar, pol_w);
-      bulk_g2s(wqkv + kFaQRows * kRow1K, a.wk + (int64_t)(kHD * h + kFaKRows * r) * kRow1K,
-               kFaKRows * kRow1K, &wbar, pol_w);
-      bulk_g2s(wqkv + (kFaQRows + kFaKRows) * kRow1K,
-               a.wv + (int64_t)(kHD * h + kFaKRows * r) * kRow1K, kFaKRows * kRow1K, &wbar, pol_w);
-    }
-    __syncwarp();
-    for (int i = lane; i < kFaORows; i += 32)
-      bulk_g2s(wo + i * kFaOBytes, a.wo + (int64_t)(kFaORows * r + i) * kORowBytes + kFaOBytes * h,
-               kFaOBytes, &wbar, pol_w);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&a.wo_map);
+    prefetch_tmap(&a.k_map);
+    prefetch_tmap(&a.v_map);
+    mbar_expect_tx(&wbar, kFaWqkvBytes + kFaWoBytes);
+    bulk_g2s(wqkv, a.wq + (int64_t)(2 * kHD * h + kFaQRows * r) * kRow1K, kFaQRows * kRow1K,
+             &wbar, pol_w);
+    bulk_g2s(wqkv + kFaQRows * kRow1K, a.wk + (int64_t)(kHD * h + kFaKRows * r) * kRow1K,
+             kFaKRows * kRow1K, &wbar, pol_w);
+    bulk_g2s(wqkv + (kFaQRows + kFaKRows) * kRow1K,
+             a.wv + (int64_t)(kHD * h + kFaKRows * r) * kRow1K, kFaKRows * kRow1K, &wbar, pol_w);
+    tma_load_2d(wo, &a.wo_map, (int)(kFaOBytes / 4) * h, a.layer * kDim + kFaORows * r, &wbar);
   }
-  // cached keys (< pos) of local chunk j into warp w's slot; the whole warp calls
+  // local chunk j (keys 8 (r + 16 j) ..) into warp w's slot: whole boxes;
+  // rows past pos are never used, rows past the cache read as zeros
   auto issue_chunk = [&](int w, int j) {
-    const int64_t t0 = (int64_t)(r + kFC * j) * kAttChunk;
-    int64_t nk = pos - t0;
-    nk = nk < 0 ? 0 : (nk > kAttChunk ? kAttChunk : nk);
-    uint8_t* slot = kvs + w * kFaSlot;
-    if (lane == 0) mbar_expect_tx(&kvbar[w], (uint32_t)nk * 2u * kHD * 2u);
-    __syncwarp();
-    if (lane < nk) {
-      const int64_t off = (a.slot0 + t0 + lane) * (kNKV * kHD) + h * kHD;
-      bulk_g2s(slot + lane * kFaKStride, a.kc + off, kHD * 2, &kvbar[w], pol_kv);
-      bulk_g2s(slot + kFaKTile + lane * kHD * 2, a.vc + off, kHD * 2, &kvbar[w], pol_kv);
+    if (lane == 0) {
+      const int y = (int)(a.slot0 + (int64_t)(r + kFC * j) * kFaChunk);
+      uint8_t* slot = kvs + w * kFaSlot;
+      mbar_expect_tx(&kvbar[w], kFaSlot);
+      tma_load_2d(slot, &a.k_map, kHD * h, y, &kvbar[w]);
+      tma_load_2d(slot + kFaKHalf, &a.k_map, kHD * h + 64, y, &kvbar[w]);
+      tma_load_2d(slot + kFaKTile, &a.v_map, kHD * h, y, &kvbar[w]);
     }
+    __syncwarp();
   };
   if (warp < kFaAttWarps && warp < nloc) issue_chunk(warp, warp);
 
-  // constants: gammas, RoPE angles at pos, the layer-0 embedding row
-  uint16_t gr[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) gr[i] = a.attn_norm[tid + 256 * i];
-  float rc0 = 0.f, rs0 = 0.f, rc1 = 0.f, rs1 = 0.f;
-  uint16_t gv[4] = {0, 0, 0, 0};
-  if (warp < 3) {
-    const float* ct = a.rope_cos + pos * 64;
-    const float* sn = a.rope_sin + pos * 64;
-    rc0 = ct[lane], rs0 = sn[lane], rc1 = ct[lane + 32], rs1 = sn[lane + 32];
-    const uint16_t* g = warp < 2 ? a.q_norm : a.k_norm;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) gv[i] = g[lane + 32 * i];
+  // constants: gammas, RoPE angles at pos, the layer-0 embedding slice
+  // Constants go through shared memory: values loaded into registers before
+  // the dependency wait were measured to arrive only after it.
+  reinterpret_cast<uint2*>(gam)[tid] = reinterpret_cast<const uint2*>(a.attn_norm)[tid];
+  // RoPE angles and the QK-norm gammas staged in shared memory (read after the wait)
+  if (tid < 64) {
+    rope_c[tid] = a.rope_cos[pos * 64 + tid];
+    rope_s[tid] = a.rope_sin[pos * 64 + tid];
+  } else if (tid < 64 + kHD) {
+    qkn[0][tid - 64] = a.q_norm[tid - 64];
+    qkn[1][tid - 64] = a.k_norm[tid - 64];
   }
-  uint2 xemb = make_uint2(0u, 0u);
-  if (a.tokens != nullptr) {
+  const int k0 = kFSlice * r + 4 * (lane & 15);  // warp 0: this lane's 4 slice elements
+  if (a.tokens != nullptr && warp == 0) {
     int64_t tok = a.tokens[pos];
     if (tok < 0 || tok >= kVocab) {
       if (tid == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
       tok = 0;
     }
-    xemb = *reinterpret_cast<const uint2*>(a.embd + tok * (int64_t)kDim + 4 * tid);
+    if (lane < 16)
+      *reinterpret_cast<uint2*>(yloc + 4 * lane) =
+          *reinterpret_cast<const uint2*>(a.embd + tok * (int64_t)kDim + k0);
   }
 
+  fphase(a.phase, 11);
   pdl_wait();  // the previous kernel's outputs (h1, dpart) are visible
   ktrace_release(a.trace);
   fphase(a.phase, 1);
 
-  // 1) the residual stream x (4 values per thread); CTA 0 publishes it
-  {
-    const uint2 xv = a.tokens != nullptr ? xemb
-                     : a.dpart == nullptr ? __ldcg(reinterpret_cast<const uint2*>(a.h1 + 4 * tid))
-                                          : resid_plus_parts(a.h1, a.dpart, 4 * tid);
-    *reinterpret_cast<uint2*>(xr + 4 * tid) = xv;
-    if (blockIdx.x == 0) *reinterpret_cast<uint2*>(a.x_out + 4 * tid) = xv;
+  // 1) this rank's slice of x (cluster 0 publishes it), pushed with its sum of squares
+  if (warp == 0) {
+    uint2 xv = make_uint2(0u, 0u);
+    if (lane < 16)
+      xv = a.tokens != nullptr ? *reinterpret_cast<const uint2*>(yloc + 4 * lane)
+           : a.dpart == nullptr ? __ldcg(reinterpret_cast<const uint2*>(a.h1 + k0))
+                                : resid_plus_parts(a.h1, a.dpart, k0);
+    __syncwarp();
+    if (h == 0 && lane < 16) *reinterpret_cast<uint2*>(a.x_out + k0) = xv;
+    push_slice(xv, r, lane, yloc, xr, xss, &ssl, &xbar);
   }
+  bool ok = mbar_wait_own(&xbar, 0u, a.err, kErrTimeoutFull);
   // 2) RMSNorm with attn_norm
-  fused_rmsnorm(xr, gr, xs, &rs);
+  slice_rmsnorm(xr, xss, gam, xs);
   fphase(a.phase, 2);
 
   // 3) Q|K|V rows: warp w takes rows w, w+8 (q), w+16 (k), w+24 (v); lane = block
@@ -343,25 +400,29 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
       if (lane == 0) loc[row] = f2h(d);
     }
   }
-  cluster_sync_all();  // every rank's Q|K|V rows are visible to the cluster
+  __syncthreads();
   fphase(a.phase, 4);
-
-  // 4) the head pair's raw q (2 x 128), k and v from the 16 ranks
-  {
-    qkv_h[tid] = ld_dsmem_u16(smem_u32(&loc[tid % kFaQRows]), (uint32_t)(tid / kFaQRows));
-    if (tid < kHD) {
-      const uint32_t src = (uint32_t)(tid / kFaKRows);
-      qkv_h[2 * kHD + tid] = ld_dsmem_u16(smem_u32(&loc[kFaQRows + tid % kFaKRows]), src);
-      qkv_h[3 * kHD + tid] = ld_dsmem_u16(smem_u32(&loc[kFaQRows + kFaKRows + tid % kFaKRows]), src);
-    }
+  // 4) every rank pushes its rows into every rank's copy of the head pair's
+  //    raw q (2 x 128) | k | v: q rows 16r.., k rows 8r.., v rows 8r..
+  if (tid < 4 * kFC) {
+    const int dst = tid >> 2, piece = tid & 3;
+    const uint4 v = reinterpret_cast<const uint4*>(loc)[piece];
+    const int at = piece < 2 ? kFaQRows * r + 8 * piece
+                             : (piece == 2 ? 2 * kHD : 3 * kHD) + kFaKRows * r;
+    st_async_v4(smem_u32(qkv_h + at), (uint32_t)dst, v, smem_u32(&qbar));
+  }
+  ok = mbar_wait_own(&qbar, 0u, a.err, kErrTimeoutFull) && ok;
+  fphase(a.phase, 5);
+  // 5) QK-norm + RoPE: q heads by warps 0, 1; the k head by warp 2
+  if (warp < 3) {
+    uint16_t gv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) gv[i] = qkn[warp < 2 ? 0 : 1][lane + 32 * i];
+    head_norm_rope_smem(qkv_h + (warp < 2 ? warp : 2) * kHD, gv, rope_c[lane], rope_s[lane],
+                        rope_c[lane + 32], rope_s[lane + 32], lane, warp < 2 ? qs[warp] : ks);
   }
   __syncthreads();
-  // 5) QK-norm + RoPE: q heads by warps 0, 1; the k head by warp 2
-  if (warp < 3)
-    head_norm_rope_smem(qkv_h + (warp < 2 ? warp : 2) * kHD, gv, rc0, rs0, rc1, rs1, lane,
-                        warp < 2 ? qs[warp] : ks);
-  __syncthreads();
-  fphase(a.phase, 5);
+  fphase(a.phase, 6);
   // the new K (normed, roped) and V (raw) rows at slot layer*S + pos
   if (r == 0 && tid < kHD) {
     const int64_t off = (a.slot0 + pos) * (kNKV * kHD) + h * kHD + tid;
@@ -369,26 +430,41 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
     a.vc[off] = qkv_h[3 * kHD + tid];
   }
 
-  // 6) this rank's chunks: warp w < 2 takes local chunks w, w+2, ... through its slot
+  // 6) this rank's chunks: warp w takes local chunks w, w+8, ... through its
+  //    slot and folds them as it goes (att_merge order); lane = 8 q + key
+  //    for the scores (dims 32q .. 32q+31 of the key), lane = 4 head dims for p.v
   bool kvok = true;
-  if (warp < kFaAttWarps) {
-    const uint8_t* slot = kvs + warp * kFaSlot;
+  {
+    const uint32_t slot = smem_u32(kvs + warp * kFaSlot);
+    const int key = lane & 7, qd = lane >> 3;
+    float m0 = -__int_as_float(0x7f800000), m1 = m0, l0 = 0.0f, l1 = 0.0f;
+    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
     int pass = 0;
     for (int j = warp; j < nloc; j += kFaAttWarps, ++pass) {
       kvok = mbar_wait_own(&kvbar[warp], (uint32_t)(pass & 1), a.err, kErrTimeoutFull) && kvok;
-      const int64_t t0 = (int64_t)(r + kFC * j) * kAttChunk;
-      const int64_t t = t0 + lane;
+      if (j == 0) fphase(a.phase, 7);
+      const int64_t t0 = (int64_t)(r + kFC * j) * kFaChunk;
+      const int64_t t = t0 + key;
       const bool valid = t < T;
       float s0 = -__int_as_float(0x7f800000), s1 = s0;
-      if (valid) {
-        const uint4* kr = t == pos ? reinterpret_cast<const uint4*>(ks)
-                                   : reinterpret_cast<const uint4*>(slot + lane * kFaKStride);
+      {
+        // dims 32 qd .. 32 qd + 31 = 16-byte chunks 4 qd .. 4 qd + 3 of the key:
+        // the new key from ks, cached keys from the swizzled tile
         const uint4* q0 = reinterpret_cast<const uint4*>(qs[0]);
         const uint4* q1 = reinterpret_cast<const uint4*>(qs[1]);
         float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-        for (int v = 0; v < kHD / 8; ++v) {
-          const uint4 kv = kr[v], x0 = q0[v], x1 = q1[v];
+        for (int i = 0; i < 4; ++i) {
+          const int v = 4 * qd + i;
+          uint4 kv;
+          if (t == pos) {
+            kv = reinterpret_cast<const uint4*>(ks)[v];
+          } else {
+            const uint32_t ad = slot + (v >> 3) * kFaKHalf + sw128_chunk_offset((uint32_t)key, (uint32_t)(v & 7));
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(kv.x), "=r"(kv.y), "=r"(kv.z), "=r"(kv.w) : "r"(ad));
+          }
+          const uint4 x0 = q0[v], x1 = q1[v];
           a0 = fma_h2(x0.x, kv.x, a0);
           a0 = fma_h2(x0.y, kv.y, a0);
           a0 = fma_h2(x0.z, kv.z, a0);
@@ -398,91 +474,126 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
           a1 = fma_h2(x1.z, kv.z, a1);
           a1 = fma_h2(x1.w, kv.w, a1);
         }
-        s0 = __fmul_rn(a0, kAttnScale);
-        s1 = __fmul_rn(a1, kAttnScale);
+        // the key's dot: (a_q0 + a_q1) + (a_q2 + a_q3)
+        a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 8));
+        a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 8));
+        a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 16));
+        a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 16));
+        if (valid) {
+          s0 = __fmul_rn(a0, kAttnScale);
+          s1 = __fmul_rn(a1, kAttnScale);
+        }
       }
-      const float m0 = warp_max_redux(s0), m1 = warp_max_redux(s1);
-      const float p0 = valid ? q3_expf(__fsub_rn(s0, m0)) : 0.0f;
-      const float p1 = valid ? q3_expf(__fsub_rn(s1, m1)) : 0.0f;
-      const float l0 = warp_sum(p0), l1 = warp_sum(p1);
-      pw[warp][lane] = make_float2(p0, p1);
-      __syncwarp();
-      // p.v: lane = head dims 4 lane .. 4 lane + 3, keys in order; keys past
-      // the end have p = 0 and V = 0 and add an exact +0
-      float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-      for (int tt = 0; tt < kAttChunk; ++tt) {
-        const float2 pp = pw[warp][tt];
+      const float cm0 = warp_max_redux(s0), cm1 = warp_max_redux(s1);
+      float p0 = valid ? q3_expf(__fsub_rn(s0, cm0)) : 0.0f;
+      float p1 = valid ? q3_expf(__fsub_rn(s1, cm1)) : 0.0f;
+      // chunk sums over the 8 keys: ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7))
+      float cl0 = p0, cl1 = p1;
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) {
+        cl0 = __fadd_rn(cl0, __shfl_xor_sync(0xffffffffu, cl0, off));
+        cl1 = __fadd_rn(cl1, __shfl_xor_sync(0xffffffffu, cl1, off));
+      }
+      if (j == 0) fphase(a.phase, 8);
+      // p.v: lane = dims 4 lane .. 4 lane + 3, keys in order (p of key tt from lane tt);
+      // keys past the end have p = 0 and V = 0 and add an exact +0
+      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int tt = 0; tt < kFaChunk; ++tt) {
+        const float pa = __shfl_sync(0xffffffffu, p0, tt), pb = __shfl_sync(0xffffffffu, p1, tt);
         const int64_t tk = t0 + tt;
         uint2 vt = make_uint2(0u, 0u);
         if (tk < pos)
-          vt = *reinterpret_cast<const uint2*>(slot + kFaKTile + tt * kHD * 2 + 8 * lane);
+          asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];"
+                       : "=r"(vt.x), "=r"(vt.y) : "r"(slot + kFaKTile + tt * kHD * 2 + 8 * lane));
         else if (tk == pos)
           vt = *reinterpret_cast<const uint2*>(qkv_h + 3 * kHD + 4 * lane);
         const float v0 = h2f((uint16_t)(vt.x & 0xffffu)), v1 = h2f((uint16_t)(vt.x >> 16));
         const float v2 = h2f((uint16_t)(vt.y & 0xffffu)), v3 = h2f((uint16_t)(vt.y >> 16));
-        o0[0] = __fmaf_rn(pp.x, v0, o0[0]);
-        o0[1] = __fmaf_rn(pp.x, v1, o0[1]);
-        o0[2] = __fmaf_rn(pp.x, v2, o0[2]);
-        o0[3] = __fmaf_rn(pp.x, v3, o0[3]);
-        o1[0] = __fmaf_rn(pp.y, v0, o1[0]);
-        o1[1] = __fmaf_rn(pp.y, v1, o1[1]);
-        o1[2] = __fmaf_rn(pp.y, v2, o1[2]);
-        o1[3] = __fmaf_rn(pp.y, v3, o1[3]);
+        c0[0] = __fmaf_rn(pa, v0, c0[0]);
+        c0[1] = __fmaf_rn(pa, v1, c0[1]);
+        c0[2] = __fmaf_rn(pa, v2, c0[2]);
+        c0[3] = __fmaf_rn(pa, v3, c0[3]);
+        c1[0] = __fmaf_rn(pb, v0, c1[0]);
+        c1[1] = __fmaf_rn(pb, v1, c1[1]);
+        c1[2] = __fmaf_rn(pb, v2, c1[2]);
+        c1[3] = __fmaf_rn(pb, v3, c1[3]);
       }
-      if (lane == 0) {
-        part[j][0].m = m0, part[j][0].l = l0;
-        part[j][1].m = m1, part[j][1].l = l1;
-      }
-      *reinterpret_cast<float4*>(&part[j][0].o[4 * lane]) = make_float4(o0[0], o0[1], o0[2], o0[3]);
-      *reinterpret_cast<float4*>(&part[j][1].o[4 * lane]) = make_float4(o1[0], o1[1], o1[2], o1[3]);
-      __syncwarp();  // every lane is done with the slot and with pw
+      __syncwarp();  // every lane is done with the slot
       if (j + kFaAttWarps < nloc) issue_chunk(warp, j + kFaAttWarps);
+      if (pass == 0) {
+        m0 = cm0, l0 = cl0, m1 = cm1, l1 = cl1;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o0[e] = c0[e], o1[e] = c1[e];
+      } else {
+        att_merge(m0, l0, o0, cm0, cl0, c0);
+        att_merge(m1, l1, o1, cm1, cl1, c1);
+      }
     }
+    if (lane == 0) {
+      part[warp][0].m = m0, part[warp][0].l = l0;
+      part[warp][1].m = m1, part[warp][1].l = l1;
+    }
+    *reinterpret_cast<float4*>(&part[warp][0].o[4 * lane]) = make_float4(o0[0], o0[1], o0[2], o0[3]);
+    *reinterpret_cast<float4*>(&part[warp][1].o[4 * lane]) = make_float4(o1[0], o1[1], o1[2], o1[3]);
   }
   __syncthreads();
-  fphase(a.phase, 6);
-  // 7) this rank's fold: thread (head hh, dim d)
+  fphase(a.phase, 9);
+  // 7) this rank's fold over its 8 warps: thread (head hh, dim d); a warp
+  //    without chunks holds m = -inf, l = 0, o = 0
   {
     const int hh = tid >> 7, d = tid & (kHD - 1);
     float M = -__int_as_float(0x7f800000);
-    for (int j = 0; j < nloc; ++j) M = fmaxf(M, part[j][hh].m);
+#pragma unroll
+    for (int w = 0; w < kFaAttWarps; ++w) M = fmaxf(M, part[w][hh].m);
     float l = 0.0f, o = 0.0f;
-    for (int j = 0; j < nloc; ++j) {
-      const float e = q3_expf(__fsub_rn(part[j][hh].m, M));
-      l = __fmaf_rn(part[j][hh].l, e, l);
-      o = __fmaf_rn(part[j][hh].o[d], e, o);
+#pragma unroll
+    for (int w = 0; w < kFaAttWarps; ++w) {
+      // exp(-inf - M) = 0 leaves l and o unchanged; a rank without chunks
+      // (M = -inf) keeps l = o = 0
+      const float e = M == -__int_as_float(0x7f800000) ? 0.0f : q3_expf(__fsub_rn(part[w][hh].m, M));
+      l = __fmaf_rn(part[w][hh].l, e, l);
+      o = __fmaf_rn(part[w][hh].o[d], e, o);
     }
     cpart[hh].o[d] = o;
     if (d == 0) cpart[hh].m = M, cpart[hh].l = l;
   }
-  cluster_sync_all();  // every rank's fold is visible to the cluster
-  fphase(a.phase, 7);
-  // 8) the cluster's fold; warps 0-3 head 2h, warps 4-7 head 2h+1
-  {
-    const int hh = warp >> 2, d = tid & (kHD - 1);
-    float Mr = -__int_as_float(0x7f800000), lr = 0.0f;
-    if (lane < kFC) {
-      Mr = ld_dsmem_f32(smem_u32(&cpart[hh].m), (uint32_t)lane);
-      lr = ld_dsmem_f32(smem_u32(&cpart[hh].l), (uint32_t)lane);
-    }
-    float orr[kFC];
-#pragma unroll
-    for (int q = 0; q < kFC; ++q) orr[q] = ld_dsmem_f32(smem_u32(&cpart[hh].o[d]), (uint32_t)q);
-    const float M = warp_max(Mr);
-    const float E = lane < kFC ? q3_expf(__fsub_rn(Mr, M)) : 0.0f;
+  __syncthreads();
+  // push (M, l) and 16 dims of o to the rank that folds those dims: rank q
+  // owns dims 16q .. 16q+15 of the pair (head q / 8)
+  if (tid < 5 * kFC) {
+    const int dst = tid / 5, piece = tid % 5, hh = dst >> 3, d0 = 16 * (dst & 7);
+    uint4 v;
+    if (piece == 0)
+      v = make_uint4(__float_as_uint(cpart[hh].m), __float_as_uint(cpart[hh].l), 0u, 0u);
+    else
+      v = *reinterpret_cast<const uint4*>(&cpart[hh].o[d0 + 4 * (piece - 1)]);
+    st_async_v4(smem_u32(&fin[r][4 * piece]), (uint32_t)dst, v, smem_u32(&fbar));
+  }
+  // 8) fold dims 16r .. 16r+15 over the ranks (lane q < 16 holds rank q's
+  //    weight) and push them into every rank's attention output
+  if (warp == 0) {
+    ok = mbar_wait_own(&fbar, 0u, a.err, kErrTimeoutFull) && ok;
+    fphase(a.phase, 10);
+    const int q = lane & (kFC - 1);
+    const float Mq = fin[q][0];
+    const float M = warp_max(lane < kFC ? Mq : -__int_as_float(0x7f800000));
+    const float E = q3_expf(__fsub_rn(Mq, M));
     float L = 0.0f, O = 0.0f;
 #pragma unroll
-    for (int q = 0; q < kFC; ++q) {
-      const float Eq = __shfl_sync(0xffffffffu, E, q);
-      L = __fmaf_rn(__shfl_sync(0xffffffffu, lr, q), Eq, L);
-      O = __fmaf_rn(orr[q], Eq, O);
+    for (int k = 0; k < kFC; ++k) {
+      const float Ek = __shfl_sync(0xffffffffu, E, k);
+      L = __fmaf_rn(fin[k][1], Ek, L);
+      O = __fmaf_rn(fin[k][4 + q], Ek, O);
     }
-    att[xh_index(hh * kHD + d)] = f2h(__fdiv_rn(O, L));
+    if (lane < kFC) fout[lane] = f2h(__fdiv_rn(O, L));
+    __syncwarp();
+    const int dst = lane >> 1, piece = lane & 1;
+    const uint4 v = reinterpret_cast<const uint4*>(fout)[piece];
+    st_async_v4(smem_u32(att + xh_index(kFC * r + 8 * piece)), (uint32_t)dst, v, smem_u32(&abar));
   }
-  cluster_arrive();  // done reading the cluster's shared memory (waited on before exit)
-  __syncthreads();
-  fphase(a.phase, 8);
+  ok = mbar_wait_own(&abar, 0u, a.err, kErrTimeoutFull) && ok;
+  fphase(a.phase, 12);
   // 9) the head pair's slice of W_o: rows 64r + 8w + i, lane = 4 i + sub takes
   //    blocks 2 sub, 2 sub + 1 (acc = fma(scale, inner, acc) per block), then
   //    v += shfl_xor(v, 1); v += shfl_xor(v, 2)
@@ -502,15 +613,20 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
     acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
     if (sub == 0) a.opart[h * kDim + kFaORows * r + row] = acc;
   }
-  // a CTA leaves only with its copies landed and after every rank's DSMEM reads
+  // a CTA leaves only with its copies and every rank's pushes into it landed
+  // (waited again, bounded, after a wait that gave up)
+  if (!ok) {
+    mbar_wait_own(&xbar, 0u, nullptr, 0);
+    mbar_wait_own(&qbar, 0u, nullptr, 0);
+    mbar_wait_own(&fbar, 0u, nullptr, 0);
+    mbar_wait_own(&abar, 0u, nullptr, 0);
+  }
   if (!wok) mbar_wait_own(&wbar, 0u, nullptr, 0);
   if (!kvok && warp < kFaAttWarps && nloc > warp) {
     const int passes = (nloc - 1 - warp) / kFaAttWarps + 1;
     mbar_wait_own(&kvbar[warp], (uint32_t)((passes - 1) & 1), nullptr, 0);
   }
-  fphase(a.phase, 9);
-  cluster_wait();
-  fphase(a.phase, 10);
+  fphase(a.phase, 13);
   ktrace_end(a.trace);
 }
 
@@ -525,13 +641,16 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* wg = smem;
   uint8_t* wu = smem + kFbGUBytes;
-  uint8_t* wd = smem + 2 * kFbGUBytes;
+  uint8_t* wd = smem + 2 * kFbGUBytes;  // 128-byte aligned (the box destination)
   __shared__ __align__(16) uint16_t hr[kDim];
+  __shared__ __align__(16) float4 xss[kFC];
+  __shared__ __align__(16) uint16_t yloc[kFSlice];
+  __shared__ __align__(16) uint4 ssl;
   __shared__ __align__(16) uint16_t xs[kDim / kQBlk * kXhStride];
-  __shared__ __align__(16) uint16_t act_loc[kFbAct];
+  __shared__ __align__(16) uint16_t act_loc[kFbAct];  // 48 bytes: 3 pushes of 8
   __shared__ __align__(16) uint16_t act_all[kFbDBlocks * kXhStride];
-  __shared__ __align__(8) uint64_t wbar;
-  __shared__ float rs;
+  __shared__ __align__(8) uint64_t wbar, hbar, actbar;
+  __shared__ __align__(16) uint16_t gam[kDim];  // ffn_norm gamma
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x / kFC;
@@ -540,47 +659,51 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   fphase(a.phase, 0);
   if (tid == 0) {
     mbar_init(&wbar, 1);
+    mbar_init(&hbar, 1);
+    mbar_init(&actbar, 1);
     fence_mbar_init();
+    mbar_expect_tx(&hbar, kFSliceBytes);
+    mbar_expect_tx(&actbar, kFC * 3 * 16);
   }
   __syncthreads();
   pdl_launch_dependents();
   if (a.seq->stop != 0) return;  // uniform over the grid (see k_fused_attn)
+  cluster_sync_all();  // every rank's exchange barriers are initialised
 
   const uint64_t pol_w = l2_policy_evict_first();
   // W_down row window: the slice's 12 blocks start at byte 408c of a row,
   // which is 16-byte aligned for even c and 8 bytes past a boundary for odd c
   const uint32_t dwin0 = (uint32_t)(kFbDBlocks * kQBytes * c) & ~15u;
   const uint32_t dboff = (uint32_t)(kFbDBlocks * kQBytes * c) - dwin0;
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_expect_tx(&wbar, kFbSmem);
-      const int g0 = kFbSlice * c + kFbAct * r;  // first gate row (= act index)
-      bulk_g2s(wg, a.wgu + (int64_t)g0 * kRow1K, kFbGUBytes, &wbar, pol_w);
-      bulk_g2s(wu, a.wgu + (int64_t)(kFFN + g0) * kRow1K, kFbGUBytes, &wbar, pol_w);
-    }
-    __syncwarp();
-    for (int i = lane; i < kFbDRows; i += 32)
-      bulk_g2s(wd + i * kFbDWin, a.wd + (int64_t)(kFbDRows * r + i) * kDRowBytes + dwin0, kFbDWin,
-               &wbar, pol_w);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&a.wd_map);
+    mbar_expect_tx(&wbar, kFbSmem);
+    const int g0 = kFbSlice * c + kFbAct * r;  // first gate row (= act index)
+    bulk_g2s(wg, a.wgu + (int64_t)g0 * kRow1K, kFbGUBytes, &wbar, pol_w);
+    bulk_g2s(wu, a.wgu + (int64_t)(kFFN + g0) * kRow1K, kFbGUBytes, &wbar, pol_w);
+    tma_load_2d(wd, &a.wd_map, (int)(dwin0 / 4), a.layer * kDim + kFbDRows * r, &wbar);
   }
-  uint16_t gr[4] = {0, 0, 0, 0};
-  if (tid < 256) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) gr[i] = a.ffn_norm[tid + 256 * i];
-  }
+  if (tid < 256) reinterpret_cast<uint2*>(gam)[tid] = reinterpret_cast<const uint2*>(a.ffn_norm)[tid];
 
+  fphase(a.phase, 7);
   pdl_wait();  // x and the O partials are visible
   ktrace_release(a.trace);
   fphase(a.phase, 1);
 
-  // 1) h1 = f16(x + f16(sum_h opart[h])); CTA 0 publishes it
-  if (tid < 256) {
-    const uint2 hv = resid_plus_parts(a.x, a.opart, 4 * tid);
-    *reinterpret_cast<uint2*>(hr + 4 * tid) = hv;
-    if (blockIdx.x == 0) *reinterpret_cast<uint2*>(a.h1_out + 4 * tid) = hv;
+  // 1) this rank's slice of h1 = f16(x + f16(sum_h opart[h])) (cluster 0
+  //    publishes it), pushed with its sum of squares
+  if (warp == 0) {
+    const int k0 = kFSlice * r + 4 * (lane & 15);
+    uint2 hv = make_uint2(0u, 0u);
+    if (lane < 16) {
+      hv = resid_plus_parts(a.x, a.opart, k0);
+      if (c == 0) *reinterpret_cast<uint2*>(a.h1_out + k0) = hv;
+    }
+    push_slice(hv, r, lane, yloc, hr, xss, &ssl, &hbar);
   }
+  bool ok = mbar_wait_own(&hbar, 0u, a.err, kErrTimeoutFull);
   // 2) RMSNorm with ffn_norm
-  fused_rmsnorm(hr, gr, xs, &rs);
+  slice_rmsnorm(hr, xss, gam, xs);
   fphase(a.phase, 2);
 
   // 3) gate|up rows: warp w -> act values 2w, 2w+1 of this CTA; lane = block
@@ -599,12 +722,17 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
       if (lane == 0) act_loc[row] = swiglu_h(f2h(g), f2h(u));
     }
   }
-  cluster_sync_all();  // every rank's act values are visible to the cluster
-  fphase(a.phase, 4);
-  // 4) the slice's 384 act values from the 16 ranks
-  act_all[xh_index(tid)] = ld_dsmem_u16(smem_u32(&act_loc[tid % kFbAct]), (uint32_t)(tid / kFbAct));
-  cluster_arrive();  // done reading the cluster's shared memory (waited on before exit)
   __syncthreads();
+  fphase(a.phase, 4);
+  // 4) every rank pushes its 24 act values (3 x 8) into every rank's copy of
+  //    the slice's 384 (block layout; a group of 8 never crosses a block)
+  if (tid < 3 * kFC) {
+    const int dst = tid / 3, piece = tid % 3;
+    const uint4 v = reinterpret_cast<const uint4*>(act_loc)[piece];
+    st_async_v4(smem_u32(act_all + xh_index(kFbAct * r + 8 * piece)), (uint32_t)dst, v,
+                smem_u32(&actbar));
+  }
+  ok = mbar_wait_own(&actbar, 0u, a.err, kErrTimeoutFull) && ok;
   fphase(a.phase, 5);
   // 5) the slice's columns of W_down
   if (warp < kFbDRows / 8) {
@@ -624,10 +752,12 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
     if (sub == 0) a.dpart[c * kDim + kFbDRows * r + row] = acc;
   }
   if (a.advance != nullptr && blockIdx.x == 0 && tid == 0) a.advance->pos += 1;
+  if (!ok) {
+    mbar_wait_own(&hbar, 0u, nullptr, 0);
+    mbar_wait_own(&actbar, 0u, nullptr, 0);
+  }
   if (!wok) mbar_wait_own(&wbar, 0u, nullptr, 0);
   fphase(a.phase, 6);
-  cluster_wait();
-  fphase(a.phase, 7);
   ktrace_end(a.trace);
 }
 
