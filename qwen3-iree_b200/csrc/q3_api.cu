@@ -838,6 +838,14 @@ static int fused_attrs() {
   Q3_CUDA(cudaFuncSetAttribute(k_fused_attn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   Q3_CUDA(cudaFuncSetAttribute(k_fused_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFbSmem));
   Q3_CUDA(cudaFuncSetAttribute(k_fused_ffn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  // One carve-out for every kernel of the step: an SM configured for one of
+  // them can then take a CTA of the next one beside it.
+  Q3_CUDA(cudaFuncSetAttribute(k_fused_attn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared));
+  Q3_CUDA(cudaFuncSetAttribute(k_fused_ffn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared));
+  Q3_CUDA(cudaFuncSetAttribute(k_vocab_argmax, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared));
   done.insert(dev);
   return Q3_OK;
 }

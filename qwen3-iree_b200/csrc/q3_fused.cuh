@@ -250,7 +250,7 @@ __device__ __forceinline__ void slice_rmsnorm(const uint16_t* xr, const float4* 
 // way (M = max M_r, E_r = exp(M_r - M), chains over r = 0..15) and
 // out_d = f16(O_d / L); rank q folds output dims 16q .. 16q+15.  A rank
 // without chunks contributes M_r = -inf.
-__global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_constant__ FaArgs a) {
+__global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* kvs = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
   uint8_t* wqkv = kvs + kFaAttWarps * kFaSlot;

@@ -304,7 +304,8 @@ def main(argv=None) -> int:
     ap.add_argument("--text", action="append", default=None, help="text prompt (with --tokenizer)")
     ap.add_argument("--seed", type=int, default=0, help="weights and synthetic prompts")
     ap.add_argument("--gguf", default=None, help="Qwen3-0.6B Q8_0 GGUF checkpoint (else random init)")
-    ap.add_argument("--engine", default="graph", choices=["graph", "persistent"])
+    ap.add_argument("--engine", default=None, choices=["fused", "graph", "persistent"],
+                    help="decode engine (default: the library's, fused where available)")
     ap.add_argument("--max-seq-len", type=int, default=1024)
     ap.add_argument("--json", default=None, help="write results here")
     ap.add_argument("--batch", type=int, default=0, help="batched mode: B sequences")
