@@ -250,7 +250,7 @@ __device__ __forceinline__ void slice_rmsnorm(const uint16_t* xr, const float4* 
 // way (M = max M_r, E_r = exp(M_r - M), chains over r = 0..15) and
 // out_d = f16(O_d / L); rank q folds output dims 16q .. 16q+15.  A rank
 // without chunks contributes M_r = -inf.
-__global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
+__global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_constant__ FaArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* kvs = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
   uint8_t* wqkv = kvs + kFaAttWarps * kFaSlot;
@@ -271,7 +271,7 @@ __global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
   __shared__ __align__(16) float fin[kFC][20];
   __shared__ __align__(16) uint16_t fout[16];
   __shared__ __align__(16) uint16_t att[2 * kHD / kQBlk * kXhStride];
-  __shared__ __align__(8) uint64_t wbar, kvbar[kFaAttWarps], xbar, qbar, fbar, abar;
+  __shared__ __align__(8) uint64_t wbar, obar, cbar, kvbar[kFaAttWarps], xbar, qbar, fbar, abar;
   __shared__ __align__(16) float rope_c[64], rope_s[64];      // RoPE angles at pos
   __shared__ __align__(16) uint16_t qkn[2][kHD];              // q_norm, k_norm gammas
   __shared__ __align__(16) uint16_t gam[kDim];                // attn_norm gamma
@@ -283,6 +283,8 @@ __global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
   fphase(a.phase, 0);
   if (tid == 0) {
     mbar_init(&wbar, 1);
+    mbar_init(&obar, 1);
+    mbar_init(&cbar, 1);
     for (int i = 0; i < kFaAttWarps; ++i) mbar_init(&kvbar[i], 1);
     mbar_init(&xbar, 1);
     mbar_init(&qbar, 1);
@@ -300,8 +302,9 @@ __global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
   // The decode state changes only in a step's last kernel, and every step is
   // its own graph launch: read it before the wait.  It is the same for every
   // CTA, so a CTA that returns here takes its whole cluster with it.
-  if (a.seq->stop != 0) return;
+  const int stop = a.seq->stop;
   const int64_t pos = a.seq->pos;
+  if (stop != 0) return;
   if (pos < 0 || pos >= a.S || pos >= kFusedMaxPositions) {
     if (tid == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
     return;
@@ -317,14 +320,13 @@ __global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
     prefetch_tmap(&a.wo_map);
     prefetch_tmap(&a.k_map);
     prefetch_tmap(&a.v_map);
-    mbar_expect_tx(&wbar, kFaWqkvBytes + kFaWoBytes);
+    mbar_expect_tx(&wbar, kFaWqkvBytes);
     bulk_g2s(wqkv, a.wq + (int64_t)(2 * kHD * h + kFaQRows * r) * kRow1K, kFaQRows * kRow1K,
              &wbar, pol_w);
     bulk_g2s(wqkv + kFaQRows * kRow1K, a.wk + (int64_t)(kHD * h + kFaKRows * r) * kRow1K,
              kFaKRows * kRow1K, &wbar, pol_w);
     bulk_g2s(wqkv + (kFaQRows + kFaKRows) * kRow1K,
              a.wv + (int64_t)(kHD * h + kFaKRows * r) * kRow1K, kFaKRows * kRow1K, &wbar, pol_w);
-    tma_load_2d(wo, &a.wo_map, (int)(kFaOBytes / 4) * h, a.layer * kDim + kFaORows * r, &wbar);
   }
   // local chunk j (keys 8 (r + 16 j) ..) into warp w's slot: whole boxes;
   // rows past pos are never used, rows past the cache read as zeros
@@ -342,34 +344,43 @@ __global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
   if (warp < kFaAttWarps && warp < nloc) issue_chunk(warp, warp);
 
   // constants: gammas, RoPE angles at pos, the layer-0 embedding slice
-  // Constants go through shared memory: values loaded into registers before
-  // the dependency wait were measured to arrive only after it.
-  reinterpret_cast<uint2*>(gam)[tid] = reinterpret_cast<const uint2*>(a.attn_norm)[tid];
-  // RoPE angles and the QK-norm gammas staged in shared memory (read after the wait)
-  if (tid < 64) {
-    rope_c[tid] = a.rope_cos[pos * 64 + tid];
-    rope_s[tid] = a.rope_sin[pos * 64 + tid];
-  } else if (tid < 64 + kHD) {
-    qkn[0][tid - 64] = a.q_norm[tid - 64];
-    qkn[1][tid - 64] = a.k_norm[tid - 64];
+  // Constants (gammas, RoPE angles at pos, the layer-0 embedding slice) come
+  // by bulk copy into shared memory: no register waits on them before the
+  // release (values loaded into registers there were measured to arrive only
+  // after it).
+  if (warp == 2 && lane == 0) {
+    const uint64_t pol_c = l2_policy_evict_normal();
+    int64_t tok = 0;
+    if (a.tokens != nullptr) {
+      tok = a.tokens[pos];
+      if (tok < 0 || tok >= kVocab) {
+        if (a.err) atomicCAS(a.err, 0, kErrBadToken);
+        tok = 0;
+      }
+    }
+    mbar_expect_tx(&cbar, kDim * 2 + 2 * kHD * 2 + 2 * 64 * 4 + (a.tokens != nullptr ? kFSlice * 2 : 0));
+    bulk_g2s(gam, a.attn_norm, kDim * 2, &cbar, pol_c);
+    bulk_g2s(qkn[0], a.q_norm, kHD * 2, &cbar, pol_c);
+    bulk_g2s(qkn[1], a.k_norm, kHD * 2, &cbar, pol_c);
+    bulk_g2s(rope_c, a.rope_cos + pos * 64, 64 * 4, &cbar, pol_c);
+    bulk_g2s(rope_s, a.rope_sin + pos * 64, 64 * 4, &cbar, pol_c);
+    if (a.tokens != nullptr)
+      bulk_g2s(yloc, a.embd + tok * (int64_t)kDim + kFSlice * r, kFSlice * 2, &cbar, pol_c);
   }
   const int k0 = kFSlice * r + 4 * (lane & 15);  // warp 0: this lane's 4 slice elements
-  if (a.tokens != nullptr && warp == 0) {
-    int64_t tok = a.tokens[pos];
-    if (tok < 0 || tok >= kVocab) {
-      if (tid == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
-      tok = 0;
-    }
-    if (lane < 16)
-      *reinterpret_cast<uint2*>(yloc + 4 * lane) =
-          *reinterpret_cast<const uint2*>(a.embd + tok * (int64_t)kDim + k0);
-  }
 
   fphase(a.phase, 11);
   pdl_wait();  // the previous kernel's outputs (h1, dpart) are visible
   ktrace_release(a.trace);
   fphase(a.phase, 1);
 
+  // the W_o slice is needed last: its copy goes out after the release, so that
+  // fewer bytes are in flight while the slices below are read from L2
+  if (warp == 1 && lane == 0) {
+    mbar_expect_tx(&obar, kFaWoBytes);
+    tma_load_2d(wo, &a.wo_map, (int)(kFaOBytes / 4) * h, a.layer * kDim + kFaORows * r, &obar);
+  }
+  bool ok = mbar_wait_own(&cbar, 0u, a.err, kErrTimeoutFull);  // constants (long landed)
   // 1) this rank's slice of x (cluster 0 publishes it), pushed with its sum of squares
   if (warp == 0) {
     uint2 xv = make_uint2(0u, 0u);
@@ -381,24 +392,24 @@ __global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
     if (h == 0 && lane < 16) *reinterpret_cast<uint2*>(a.x_out + k0) = xv;
     push_slice(xv, r, lane, yloc, xr, xss, &ssl, &xbar);
   }
-  bool ok = mbar_wait_own(&xbar, 0u, a.err, kErrTimeoutFull);
-  // 2) RMSNorm with attn_norm
+  // 2) while the slices travel: this warp's rows w, w+8 (q), w+16 (k), w+24
+  //    (v) at block `lane` converted to exact half2 registers
+  const bool wok = mbar_wait_own(&wbar, 0u, a.err, kErrTimeoutFull);
+  uint32_t hq[4][1][16];
+  float sq[4][1];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    q8_row_to_h2regs<1>(smem_u32(wqkv) + (warp + 8 * i) * kRow1K, kDim / kQBlk, lane, hq[i], sq[i]);
+  fphase(a.phase, 3);
+  ok = mbar_wait_own(&xbar, 0u, a.err, kErrTimeoutFull) && ok;
+  // 3) RMSNorm with attn_norm
   slice_rmsnorm(xr, xss, gam, xs);
   fphase(a.phase, 2);
-
-  // 3) Q|K|V rows: warp w takes rows w, w+8 (q), w+16 (k), w+24 (v); lane = block
-  const bool wok = mbar_wait_own(&wbar, 0u, a.err, kErrTimeoutFull);
-  fphase(a.phase, 3);
-  {
-    uint32_t xb[16];
-    load_xblock(xs, lane, xb);
+  // 4) Q|K|V dots (the block order of q8_block_dot_mlir)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int row = warp + 8 * i;
-      const Q8BlockWords bw = q8_load_block(smem_u32(wqkv) + row * kRow1K + kQBytes * lane);
-      const float d = warp_sum(q8_block_dot_mlir(bw, xb, 0.0f));
-      if (lane == 0) loc[row] = f2h(d);
-    }
+  for (int i = 0; i < 4; ++i) {
+    const float d = q8_h2regs_dot_xh<1>(hq[i], sq[i], kDim / kQBlk, lane, xs);
+    if (lane == 0) loc[warp + 8 * i] = f2h(d);
   }
   __syncthreads();
   fphase(a.phase, 4);
@@ -594,6 +605,7 @@ __global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
   }
   ok = mbar_wait_own(&abar, 0u, a.err, kErrTimeoutFull) && ok;
   fphase(a.phase, 12);
+  const bool ook = mbar_wait_own(&obar, 0u, a.err, kErrTimeoutFull);
   // 9) the head pair's slice of W_o: rows 64r + 8w + i, lane = 4 i + sub takes
   //    blocks 2 sub, 2 sub + 1 (acc = fma(scale, inner, acc) per block), then
   //    v += shfl_xor(v, 1); v += shfl_xor(v, 2)
@@ -616,12 +628,14 @@ __global__ void __maxnreg__(72) k_fused_attn(const __grid_constant__ FaArgs a) {
   // a CTA leaves only with its copies and every rank's pushes into it landed
   // (waited again, bounded, after a wait that gave up)
   if (!ok) {
+    mbar_wait_own(&cbar, 0u, nullptr, 0);
     mbar_wait_own(&xbar, 0u, nullptr, 0);
     mbar_wait_own(&qbar, 0u, nullptr, 0);
     mbar_wait_own(&fbar, 0u, nullptr, 0);
     mbar_wait_own(&abar, 0u, nullptr, 0);
   }
   if (!wok) mbar_wait_own(&wbar, 0u, nullptr, 0);
+  if (!ook) mbar_wait_own(&obar, 0u, nullptr, 0);
   if (!kvok && warp < kFaAttWarps && nloc > warp) {
     const int passes = (nloc - 1 - warp) / kFaAttWarps + 1;
     mbar_wait_own(&kvbar[warp], (uint32_t)((passes - 1) & 1), nullptr, 0);
@@ -649,7 +663,7 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   __shared__ __align__(16) uint16_t xs[kDim / kQBlk * kXhStride];
   __shared__ __align__(16) uint16_t act_loc[kFbAct];  // 48 bytes: 3 pushes of 8
   __shared__ __align__(16) uint16_t act_all[kFbDBlocks * kXhStride];
-  __shared__ __align__(8) uint64_t wbar, hbar, actbar;
+  __shared__ __align__(8) uint64_t wbar, dbar, cbar, hbar, actbar;
   __shared__ __align__(16) uint16_t gam[kDim];  // ffn_norm gamma
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -659,6 +673,8 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   fphase(a.phase, 0);
   if (tid == 0) {
     mbar_init(&wbar, 1);
+    mbar_init(&dbar, 1);
+    mbar_init(&cbar, 1);
     mbar_init(&hbar, 1);
     mbar_init(&actbar, 1);
     fence_mbar_init();
@@ -677,19 +693,26 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   const uint32_t dboff = (uint32_t)(kFbDBlocks * kQBytes * c) - dwin0;
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&a.wd_map);
-    mbar_expect_tx(&wbar, kFbSmem);
+    mbar_expect_tx(&wbar, 2 * kFbGUBytes);
     const int g0 = kFbSlice * c + kFbAct * r;  // first gate row (= act index)
     bulk_g2s(wg, a.wgu + (int64_t)g0 * kRow1K, kFbGUBytes, &wbar, pol_w);
     bulk_g2s(wu, a.wgu + (int64_t)(kFFN + g0) * kRow1K, kFbGUBytes, &wbar, pol_w);
-    tma_load_2d(wd, &a.wd_map, (int)(dwin0 / 4), a.layer * kDim + kFbDRows * r, &wbar);
   }
-  if (tid < 256) reinterpret_cast<uint2*>(gam)[tid] = reinterpret_cast<const uint2*>(a.ffn_norm)[tid];
+  if (warp == 2 && lane == 0) {  // the gamma by bulk copy (see k_fused_attn)
+    mbar_expect_tx(&cbar, kDim * 2);
+    bulk_g2s(gam, a.ffn_norm, kDim * 2, &cbar, l2_policy_evict_normal());
+  }
 
   fphase(a.phase, 7);
   pdl_wait();  // x and the O partials are visible
   ktrace_release(a.trace);
   fphase(a.phase, 1);
 
+  // the W_down window is needed last: its copy goes out after the release
+  if (warp == 1 && lane == 0) {
+    mbar_expect_tx(&dbar, kFbDBytes);
+    tma_load_2d(wd, &a.wd_map, (int)(dwin0 / 4), a.layer * kDim + kFbDRows * r, &dbar);
+  }
   // 1) this rank's slice of h1 = f16(x + f16(sum_h opart[h])) (cluster 0
   //    publishes it), pushed with its sum of squares
   if (warp == 0) {
@@ -702,6 +725,7 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
     push_slice(hv, r, lane, yloc, hr, xss, &ssl, &hbar);
   }
   bool ok = mbar_wait_own(&hbar, 0u, a.err, kErrTimeoutFull);
+  ok = mbar_wait_own(&cbar, 0u, a.err, kErrTimeoutFull) && ok;
   // 2) RMSNorm with ffn_norm
   slice_rmsnorm(hr, xss, gam, xs);
   fphase(a.phase, 2);
@@ -734,6 +758,7 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   }
   ok = mbar_wait_own(&actbar, 0u, a.err, kErrTimeoutFull) && ok;
   fphase(a.phase, 5);
+  const bool dok = mbar_wait_own(&dbar, 0u, a.err, kErrTimeoutFull);
   // 5) the slice's columns of W_down
   if (warp < kFbDRows / 8) {
     const int i = lane >> 2, sub = lane & 3;
@@ -753,10 +778,12 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   }
   if (a.advance != nullptr && blockIdx.x == 0 && tid == 0) a.advance->pos += 1;
   if (!ok) {
+    mbar_wait_own(&cbar, 0u, nullptr, 0);
     mbar_wait_own(&hbar, 0u, nullptr, 0);
     mbar_wait_own(&actbar, 0u, nullptr, 0);
   }
   if (!wok) mbar_wait_own(&wbar, 0u, nullptr, 0);
+  if (!dok) mbar_wait_own(&dbar, 0u, nullptr, 0);
   fphase(a.phase, 6);
   ktrace_end(a.trace);
 }
