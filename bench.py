@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Qwen3-0.6B Q8_0 batch-1 greedy decode on B200 -- the BASELINE metric.
+"""Qwen3-0.6B Q8_0 greedy decode on B200 -- the BASELINE metric.
 
 Workload: 28 layers of Q8_0 projections + GQA
 attention over the flat KV cache + tied f16 vocab GEMV + argmax, seeded
@@ -13,12 +13,21 @@ generated tokens; every sequence restarts from the same prompt.
   python bench.py --impl reference [...]               the CPU oracle (reference arm)
 
 value: tokens/s over all ranks, device time (CUDA events on the decoder's
-stream) of the K timed steps, max over ranks.  e2e: q3_run (the public call
+stream) of the K timed steps, max over ranks, on the library's default
+engine (fused: two cluster kernels per layer).  e2e: q3_run (the public call
 mirroring the reference's @run) with host prompt in / host tokens out, wall
 clock, as scripts/benchmark.py measures it.  N>1 (torchrun): independent
-replicas, one per GPU, no collective on the data path (replicas only).
-"batched": BASELINE configs[3] (B=32) and configs[4] (B=64 per replica) on the
-tensor-core batched path, device time of 128 steps.
+replicas, one per GPU, no collective on the data path (replicas only); the
+ranks meet only for the start barrier and the max / sum of their timings,
+over gloo (host memory), not NCCL.
+roofline: the per-step fraction -- algorithmic bytes of a step (weights + the
+KV rows read and written) over the measured step time, against the measured
+copy bandwidth -- with each kernel kind's share and bandwidth from the live
+kernel trace (global-timer stamps inside the kernels; nothing serialised).
+Extra legs: "configs0" (the attn_q GEMV over a rotating
+pool larger than L2), "configs1" (configs[1]: one layer at position 511),
+"batched" (configs[3] B=32 and configs[4] B=64 per replica, tensor-core
+path, device time of 128 steps).
 """
 from __future__ import annotations
 
@@ -70,27 +79,6 @@ def load_peaks() -> tuple[float, str]:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
-
-
-def graph_roofline(kern: dict, peak: float, peak_src: str, traffic: dict) -> dict:
-    """Roofline object of the graph engine's dominant kernel kind.  Each Q8_0
-    launch also prefetches the next launch's weights into L2, so its ncu DRAM
-    bytes with L2 flushed per kernel ("traffic") are its own weights plus the
-    next launch's; the pipelined capture (no flush) gives per-launch and
-    per-step figures comparable with the algorithmic bytes."""
-    dom = max(kern, key=lambda k: kern[k]["total_us_per_step"])
-    roof = {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["achieved_gbs"],
-            "peak": peak, "unit": "GB/s", "frac": kern[dom]["achieved_gbs"] / peak,
-            "traffic": traffic.get(dom), "peak_source": peak_src}
-    if all(f"{k}_pipelined" in traffic for k in kern):
-        roof["traffic_pipelined"] = traffic[f"{dom}_pipelined"]
-        roof["traffic_pipelined_per_step"] = sum(
-            traffic[f"{k}_pipelined"] * kern[k]["launches_per_step"] for k in kern)
-        roof["alg_bytes_per_step"] = sum(
-            kern[k]["alg_bytes_per_launch"] * kern[k]["launches_per_step"] for k in kern)
-        roof["traffic_note"] = ("traffic: ncu with L2 flushed per kernel = own weights + the next "
-                                "launch's (prefetched into L2); traffic_pipelined: no flush")
-    return roof
 
 
 def load_traffic() -> dict:
@@ -163,10 +151,10 @@ class ClockSampler:
 # ---------------------------------------------------------------- distributed plumbing
 class Dist:
     """torch.distributed for the barrier and the max/sum over ranks of the
-    timings only; the decode itself has no collective (replicas).  NCCL on the
-    GPU box; "gloo" (CPU tensors) for the multi-rank tests of this logic."""
+    timings only; the decode itself has no collective (replicas).  gloo over
+    host tensors: no NCCL is involved, on the GPU box or in the tests."""
 
-    def __init__(self, backend: str = "nccl"):
+    def __init__(self, backend: str = "gloo"):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -314,6 +302,74 @@ def config_dict(args) -> dict:
 
 
 # ---------------------------------------------------------------- our path
+# kernel kinds of the live trace (include/q3b200.h Q3_KIND_*)
+TRACE_KINDS = {0: "qkv", 1: "attn", 2: "o", 3: "gate_up", 4: "down", 5: "vocab",
+               7: "fused_attn", 8: "fused_ffn"}
+KV_BYTES_W = 2 * KV_ROW  # K and V rows of one position, one layer
+
+
+def kernel_alg_bytes(name: str, pos: float) -> float:
+    """Algorithmic HBM bytes of one launch of a decode-step kernel at position
+    pos: its weights (+ gammas) and the K/V rows it reads and writes."""
+    gam = 2 * 1024 * 2
+    kv = KV_BYTES_W * pos + KV_BYTES_W  # cached rows read, the new row written
+    if name == "fused_attn":
+        return Q8_BYTES["qkv"] + Q8_BYTES["o"] + gam / 2 + 2 * 128 * 2 + kv
+    if name == "fused_ffn":
+        return Q8_BYTES["gate_up"] + Q8_BYTES["down"] + gam / 2
+    if name == "attn":
+        return attn_bytes(int(pos))
+    if name == "vocab":
+        return VOCAB_BYTES
+    return Q8_BYTES[name] + ACT_BYTES[name]
+
+
+def live_kernels(dec, steps: int, pos: float) -> dict:
+    """Per kernel kind of one decode step, from the live kernel trace (each
+    kernel stamps the global timer; the step runs as in the timed loop):
+    the time it adds to the step (its last CTA's end minus the previous
+    kernel's), its share, and algorithmic bytes / that time."""
+    t, kinds = dec.trace_kernels(steps)
+    ends = t[:, 3].astype(np.float64)
+    add = np.diff(np.concatenate([[0.0], ends]))
+    step_ns = float(ends[-1])
+    out = {}
+    for k in sorted(set(kinds.tolist())):
+        name = TRACE_KINDS.get(int(k), str(k))
+        sel = add[kinds == k]
+        b = kernel_alg_bytes(name, pos)
+        avg_us = float(sel.mean()) / 1e3
+        out[name] = {"launches_per_step": int(sel.size), "avg_us": avg_us,
+                     "total_us_per_step": float(sel.sum()) / 1e3,
+                     "share": float(sel.sum()) / step_ns, "alg_bytes_per_launch": b,
+                     "achieved_gbs": b / (avg_us * 1e-6) / 1e9}
+    return out
+
+
+def step_roofline(bytes_per_step: float, ms_per_step: float, kern: dict, peak: float,
+                  peak_src: str, engine: str, launches: int, traffic: dict) -> dict:
+    """The headline roofline object: the whole decode step against the HBM
+    roofline (the north star's per-token fraction), with the dominant kernel
+    kind's own figures; traffic = ncu DRAM bytes per step from one-launch
+    captures of each kernel kind (profiles/), or null."""
+    ach = bytes_per_step / (ms_per_step * 1e-3) / 1e9
+    dom = max(kern, key=lambda k: kern[k]["total_us_per_step"])
+    tr = None
+    if kern and all(k in traffic for k in kern):
+        tr = sum(traffic[k] * kern[k]["launches_per_step"] for k in kern)
+    d = dict(kern[dom])
+    d["name"] = dom
+    d["frac"] = d["achieved_gbs"] / peak
+    d["traffic"] = traffic.get(dom)
+    return {"bound": "hbm", "kernel": f"decode step ({engine} engine, {launches} launches)",
+            "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+            "traffic": tr, "alg_bytes": bytes_per_step, "per": "step",
+            "frac_of_8tbs": ach / NOMINAL_HBM_GBS, "peak_source": peak_src,
+            "dominant_kernel": d,
+            "timing": "achieved = algorithmic bytes of a step / measured step time (CUDA "
+                      "events over the timed steps); kernel figures from the live trace"}
+
+
 def run_ours(args, d: Dist) -> None:
     import q3b200
     from q3b200.weights import synthetic_weights
@@ -355,49 +411,42 @@ def run_ours(args, d: Dist) -> None:
     d.barrier()
     t_max = d.max(total_ms)
     value = d.sum(done) / (t_max / 1e3)
+    ms = t_max / (done if done else 1)
 
-    # per-kernel device times from an event-instrumented step graph
-    prof_steps = 8
-    prof = q3b200.Qwen3Decoder(dw, max_seq_len=CACHE, engine="graph")
-    prof.generate_begin(prompt, prof_steps + 64, -1)
-    prof.generate_steps(64)
-    times_us, kinds = prof.profile_steps(prof_steps)
-    prof.generate_end(prof_steps + 64)
-    prof.close()
-    ppos = PROMPT_LEN + 64 + prof_steps // 2
-    kern = {}
-    for name_i, name in enumerate(KIND_NAMES):
-        sel = times_us[kinds == name_i]
-        if sel.size == 0:
-            continue
-        if name in Q8_BYTES:
-            b = Q8_BYTES[name] + ACT_BYTES[name]
-        elif name == "vocab":
-            b = VOCAB_BYTES
-        else:
-            b = attn_bytes(ppos)
-        avg = float(sel.mean())
-        kern[name] = {"launches_per_step": int(sel.size), "avg_us": avg,
-                      "total_us_per_step": float(sel.sum()), "alg_bytes_per_launch": b,
-                      "achieved_gbs": b / (avg * 1e-6) / 1e9}
-    step_us = float(times_us.sum())
-    for k in kern.values():
-        k["share"] = k["total_us_per_step"] / step_us
+    # per-kernel figures from the live trace, at the middle of the timed positions
+    tr_steps = 8
+    mid = GEN_PER_SEQ // 2
+    dec.generate_begin(prompt, mid + tr_steps + 1, -1)
+    dec.generate_steps(mid)
+    kern = live_kernels(dec, tr_steps, PROMPT_LEN + mid + tr_steps / 2)
+    dec.generate_end(mid + tr_steps + 1)
     peak, peak_kind = load_peaks()
     peak_src = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6.65 TB/s")
-    if dec.engine == "persistent":
-        # one kernel runs every timed step: its launch covers a whole chunk of steps
-        per_step = bytes_total / done
-        ach = per_step / (t_max / done * 1e-3) / 1e9
-        tr = load_traffic().get("persistent_per_step")
-        roof = {"bound": "hbm", "kernel": "k_decode_persistent", "achieved": ach, "peak": peak,
-                "unit": "GB/s", "frac": ach / peak, "traffic": tr,
-                "alg_bytes_per_launch": bytes_total / len(chunks), "traffic_unit": "bytes per step",
-                "peak_source": peak_src}
-    else:
-        roof = graph_roofline(kern, peak, peak_src, load_traffic())
+    roof = step_roofline(bytes_total / done, ms, kern, peak, peak_src, dec.engine,
+                         dec.launches_per_step(), load_traffic())
 
+    from q3b200.benchmark import gemv_pool, layer_bench
+
+    configs0 = gemv_pool(seed=args.seed)
+    for k in ("q3_gemv_q8_overlapped", "q3_gemv_q8"):
+        configs0[k]["frac_of_measured"] = configs0[k]["gbs"] / peak
+        configs0[k]["frac_of_8tbs"] = configs0[k]["gbs"] / NOMINAL_HBM_GBS
+    configs1 = layer_bench(dw, seed=args.seed)
+    configs1["frac_of_measured"] = configs1["gbs"] / peak
+    # the same layer inside the decode step: the engine's kernels of one layer
+    # at position 511 (512 keys attended), from the live trace
+    pos1 = 511
+    dec.generate_begin(prompt, pos1 - PROMPT_LEN + 8, -1)
+    dec.generate_steps(pos1 - PROMPT_LEN - 2)
+    k1 = live_kernels(dec, 4, pos1)
+    dec.generate_end(pos1 - PROMPT_LEN + 8)
+    per_layer = sum(v["total_us_per_step"] for k, v in k1.items() if k != "vocab") / 28
+    b1 = 18825728
+    configs1["in_engine"] = {"us_per_layer": per_layer, "gbs": b1 / (per_layer * 1e-6) / 1e9,
+                             "frac_of_measured": b1 / (per_layer * 1e-6) / 1e9 / peak,
+                             "how": "live trace of the decode step at position 511: the time the "
+                                    "layer's kernels add to the step, averaged over the 28 layers"}
     # streaming GEMV bandwidth: 28 layers of one projection in one launch
     gemv_stream = measure_gemv_stream(q3b200, dw, peak) if not args.quick else {}
     batched = {} if args.no_batched else {
@@ -427,7 +476,6 @@ def run_ours(args, d: Dist) -> None:
                          f"on {cpu_model()}"}
 
     if d.rank == 0:
-        ms = t_max / (done if done else 1)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": d.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -443,11 +491,9 @@ def run_ours(args, d: Dist) -> None:
                             "tokens out per call, wall clock incl. prompt ingestion"},
             "gpu_launches": launches,
             "engine": dec.engine,
-            "step_roofline": {"alg_bytes_per_step": bytes_total / done,
-                              "achieved_gbs": bytes_total / done / (ms * 1e-3) / 1e9,
-                              "frac_of_8tbs": bytes_total / done / (ms * 1e-3) / 1e9 / NOMINAL_HBM_GBS,
-                              "frac_of_measured": bytes_total / done / (ms * 1e-3) / 1e9 / peak},
-            "graph_engine_kernels": kern,
+            "kernels": kern,
+            "configs0": configs0,
+            "configs1": configs1,
             "gemv_stream": gemv_stream,
             "batched": batched,
             "device_error": err,
@@ -564,7 +610,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU decode time")
     ap.add_argument("--ref-budget", type=float, default=60.0, help="seconds, reference arm")
     ap.add_argument("--quick", action="store_true", help="skip the GEMV streaming sweep")
-    ap.add_argument("--engine", default="graph", choices=["persistent", "graph"])
+    ap.add_argument("--engine", default=None, choices=["fused", "graph", "persistent"],
+                    help="decode engine (default: the library's, fused where available)")
     ap.add_argument("--no-batched", action="store_true", help="skip the B=32 / B=64 legs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

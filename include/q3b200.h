@@ -218,11 +218,15 @@ typedef struct q3_weights {
  * runs over slots layer*S + 0..pos.  w: the stacked weights (layer selects
  * the slice); pos: DEVICE int64 (pos < S <= 4096); rope tables f32 [S, 64];
  * workspace: q3_fused_layer_workspace_bytes() bytes.  Three kernels: the
- * attention block, the feed-forward block and the residual rebuild. */
+ * attention block, the feed-forward block and the residual rebuild.
+ * flags: 0, or Q3_LAYER_OVERLAP -- the first kernel may begin (its weight and
+ * K/V copies, its read of pos) while the previous kernel in the stream still
+ * runs; then that kernel must not write w, pos or the cached K/V rows. */
+#define Q3_LAYER_OVERLAP 1
 size_t q3_fused_layer_workspace_bytes(void);
 int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, void* x_out, void* k_cache,
                    void* v_cache, int64_t S, const int64_t* pos, const float* rope_cos,
-                   const float* rope_sin, void* workspace, void* stream);
+                   const float* rope_sin, void* workspace, int flags, void* stream);
 
 typedef struct q3_model q3_model;
 

@@ -850,21 +850,19 @@ static int fused_attrs() {
   return Q3_OK;
 }
 
-// Workspace: the O and down partials, h1, the intermediate x and a sequence
-// state holding pos (copied from the caller's device pos).
+// Workspace: the O and down partials, h1 and the intermediate x.
 struct FusedLayerWs {
   float opart[kFParts * kDim];
   float dpart[kFParts * kDim];
   uint16_t x[kDim];
   uint16_t h1[kDim];
-  SeqState seq;
 };
 
 extern "C" size_t q3_fused_layer_workspace_bytes(void) { return sizeof(FusedLayerWs) + 256; }
 
 extern "C" int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, void* x_out,
                               void* kc, void* vc, int64_t S, const int64_t* pos,
-                              const float* rope_cos, const float* rope_sin, void* ws,
+                              const float* rope_cos, const float* rope_sin, void* ws, int flags,
                               void* stream) {
   Q3_REQUIRE(w && x_in && x_out && kc && vc && pos && rope_cos && rope_sin && ws, "null pointer");
   Q3_REQUIRE(layer >= 0 && layer < kLayers, "layer %d out of range", layer);
@@ -880,10 +878,9 @@ extern "C" int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, 
   cudaStream_t st = (cudaStream_t)stream;
   FusedLayerWs* f = (FusedLayerWs*)ws;
   FusedMaps maps;
+  Q3_REQUIRE((flags & ~Q3_LAYER_OVERLAP) == 0, "unknown flags 0x%x", flags);
   rc_ = make_fused_maps(&maps, w, kc, vc, (int64_t)(layer + 1) * S);
   if (rc_) return rc_;
-  Q3_CUDA(cudaMemsetAsync(&f->seq, 0, sizeof(SeqState), st));
-  Q3_CUDA(cudaMemcpyAsync(&f->seq.pos, pos, sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
   rc_ = fused_attrs();
   if (rc_) return rc_;
   FaArgs fa;
@@ -907,9 +904,9 @@ extern "C" int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, 
   fa.rope_sin = rope_sin;
   fa.slot0 = (int64_t)layer * S;
   fa.S = S;
-  fa.seq = &f->seq;
-  Q3_CUDA(launch_cluster_x(k_fused_attn, dim3(kFParts * kFC), dim3(kFaThreads), kFaSmem, st, false,
-                           kFC, fa));
+  fa.pos = pos;
+  Q3_CUDA(launch_cluster_x(k_fused_attn, dim3(kFParts * kFC), dim3(kFaThreads), kFaSmem, st,
+                           (flags & Q3_LAYER_OVERLAP) != 0, kFC, fa));
   FbArgs fb;
   memset(&fb, 0, sizeof(fb));
   fb.wgu = (const uint8_t*)w->q8_ffn_gate_up + layer * kBplGU;
@@ -920,7 +917,6 @@ extern "C" int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, 
   fb.opart = f->opart;
   fb.h1_out = f->h1;
   fb.dpart = f->dpart;
-  fb.seq = &f->seq;
   Q3_CUDA(launch_cluster_x(k_fused_ffn, dim3(kFParts * kFC), dim3(kFbThreads), kFbSmem, st, true,
                            kFC, fb));
   Q3_CUDA(launch_ex(k_resid_parts, dim3(1), dim3(256), 0, st, true, (const uint16_t*)f->h1,
@@ -1223,7 +1219,8 @@ static int enqueue_layers_fused(q3_model* m, bool ingest, int* launches, const S
     fa.rope_sin = m->rope_sin;
     fa.slot0 = (int64_t)l * m->S;
     fa.S = m->S;
-    fa.seq = m->st;
+    fa.pos = &m->st->pos;
+    fa.stop = &m->st->stop;
     fa.err = m->err;
     fa.trace = probe_trace(probe, Q3_KIND_FUSED_ATTN);
     fa.phase = probe_phase(probe);
@@ -1241,7 +1238,7 @@ static int enqueue_layers_fused(q3_model* m, bool ingest, int* launches, const S
     fb.opart = m->opart;
     fb.h1_out = m->h1;
     fb.dpart = m->dpart;
-    fb.seq = m->st;
+    fb.stop = &m->st->stop;
     if (ingest && l == kLayers - 1) fb.advance = m->st;
     fb.err = m->err;
     fb.trace = probe_trace(probe, Q3_KIND_FUSED_FFN);

@@ -113,7 +113,8 @@ struct FaArgs {
   const float* rope_sin;
   int64_t slot0;              // layer * S
   int64_t S;
-  const SeqState* seq;
+  const int64_t* pos;         // device position (read before the dependency wait)
+  const int32_t* stop;        // optional: the step is skipped when *stop != 0
   int* err;
   unsigned long long* trace;  // optional launch timing record
   long long* phase;           // optional per-CTA phase stamps [grid][kFPhases] (ns)
@@ -128,7 +129,7 @@ struct FbArgs {
   const float* opart;         // [8][1024]
   uint16_t* h1_out;           // h1, written by CTA 0 (the next layer's residual)
   float* dpart;               // out: [8][1024] down partials (one per FFN slice)
-  const SeqState* seq;
+  const int32_t* stop;        // optional: the step is skipped when *stop != 0
   SeqState* advance;          // if set, pos += 1 (the last kernel of a prompt-ingestion step)
   int* err;
   unsigned long long* trace;
@@ -302,8 +303,8 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   // The decode state changes only in a step's last kernel, and every step is
   // its own graph launch: read it before the wait.  It is the same for every
   // CTA, so a CTA that returns here takes its whole cluster with it.
-  const int stop = a.seq->stop;
-  const int64_t pos = a.seq->pos;
+  const int stop = a.stop != nullptr ? *a.stop : 0;
+  const int64_t pos = *a.pos;
   if (stop != 0) return;
   if (pos < 0 || pos >= a.S || pos >= kFusedMaxPositions) {
     if (tid == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
@@ -683,7 +684,7 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   }
   __syncthreads();
   pdl_launch_dependents();
-  if (a.seq->stop != 0) return;  // uniform over the grid (see k_fused_attn)
+  if (a.stop != nullptr && *a.stop != 0) return;  // uniform over the grid (see k_fused_attn)
   cluster_sync_all();  // every rank's exchange barriers are initialised
 
   const uint64_t pol_w = l2_policy_evict_first();

@@ -82,7 +82,7 @@ SIGNATURES = {
     "q3_iree_dispatch_20": [P, P, P, U32, U32, P],
     "q3_iree_dispatch_24": [P, P, P, U32, P],
     "q3_fused_layer_workspace_bytes": [],
-    "q3_fused_layer": [ctypes.POINTER(Weights), I, P, P, P, P, I64, P, P, P, P, P],
+    "q3_fused_layer": [ctypes.POINTER(Weights), I, P, P, P, P, I64, P, P, P, P, I, P],
     "q3_model_create": [ctypes.POINTER(Weights), I64, P, PP],
     "q3_model_destroy": [P],
     "q3_model_stream": [P],

@@ -278,7 +278,7 @@ def layer_bench(dw, seed: int = 0, reps: int = 10, warmup: int = 3) -> dict:
     with g:
         for l in range(28):
             call("q3_fused_layer", ctypes.byref(dw.struct), l, xs[l % 2].ptr, xs[(l + 1) % 2].ptr,
-                 kc.ptr, vc.ptr, S, dpos.ptr, dc.ptr, ds.ptr, ws.ptr, st)
+                 kc.ptr, vc.ptr, S, dpos.ptr, dc.ptr, ds.ptr, ws.ptr, 1, st)
     ev = Events()
     for _ in range(warmup):
         g.launch()

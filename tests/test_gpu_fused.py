@@ -62,7 +62,7 @@ def _fused_layer(q3, dw, x, kc, vc, S, pos):
     c, s = _rope(q3, S)
     ws = q3.DeviceArray((L.q3_fused_layer_workspace_bytes(),), np.uint8, zero=True)
     rc = L.q3_fused_layer(ctypes.byref(dw.struct), LAYER, dx.ptr, dy.ptr, dkc.ptr, dvc.ptr, S,
-                          dpos.ptr, c.ptr, s.ptr, ws.ptr, None)
+                          dpos.ptr, c.ptr, s.ptr, ws.ptr, 0, None)
     assert rc == 0, L.q3_last_error()
     assert L.q3_stream_synchronize(None) == 0
     return dy.download(), dkc.download(), dvc.download()
@@ -152,5 +152,5 @@ def test_fused_layer_rejects_long_caches(gpu, layer_models):
     L = gpu.lib()
     buf = gpu.DeviceArray((64,), np.uint8, zero=True)
     p = buf.ptr
-    rc = L.q3_fused_layer(ctypes.byref(dw.struct), 0, p, p, p, p, 8192, p, p, p, p, None)
+    rc = L.q3_fused_layer(ctypes.byref(dw.struct), 0, p, p, p, p, 8192, p, p, p, p, 0, None)
     assert rc == 1 and b"4096" in L.q3_last_error()

@@ -71,19 +71,30 @@ def test_single_process_dist_is_a_no_op():
     d.close()
 
 
-def test_graph_roofline_reports_flushed_and_pipelined_traffic():
+def test_step_roofline_is_the_per_step_fraction():
+    """The headline roofline: algorithmic bytes of a step over the measured
+    step time against the peak; the dominant kind from the live trace keeps
+    its own figures; traffic per step only when every kind was captured."""
     import bench
 
-    kern = {"qkv": {"total_us_per_step": 80.0, "achieved_gbs": 500.0, "launches_per_step": 28,
-                    "alg_bytes_per_launch": 4.5e6},
+    kern = {"fused_attn": {"total_us_per_step": 200.0, "achieved_gbs": 1000.0,
+                           "launches_per_step": 28, "alg_bytes_per_launch": 7e6},
             "vocab": {"total_us_per_step": 50.0, "achieved_gbs": 6000.0, "launches_per_step": 1,
                       "alg_bytes_per_launch": 311e6}}
-    tr = bench.load_traffic()
-    r = bench.graph_roofline(kern, 6500.0, "measured", tr)
-    assert r["kernel"] == "qkv" and abs(r["frac"] - 500.0 / 6500.0) < 1e-12
-    assert r["traffic"] == tr["qkv"]
-    assert r["traffic_pipelined"] == tr["qkv_pipelined"]
-    assert r["traffic_pipelined_per_step"] == 28 * tr["qkv_pipelined"] + tr["vocab_pipelined"]
-    # without pipelined figures only the flushed capture is reported
-    r2 = bench.graph_roofline(kern, 6500.0, "measured", {"qkv": 1.0})
-    assert "traffic_pipelined" not in r2 and r2["traffic"] == 1.0
+    r = bench.step_roofline(8e8, 0.4, kern, 6400.0, "measured", "fused", 57,
+                            {"fused_attn": 7.1e6, "vocab": 3.12e8})
+    assert r["achieved"] == pytest.approx(8e8 / 0.4e-3 / 1e9)
+    assert r["frac"] == pytest.approx(r["achieved"] / 6400.0)
+    assert r["dominant_kernel"]["name"] == "fused_attn"
+    assert r["traffic"] == pytest.approx(28 * 7.1e6 + 3.12e8)
+    r2 = bench.step_roofline(8e8, 0.4, kern, 6400.0, "measured", "fused", 57, {"vocab": 1.0})
+    assert r2["traffic"] is None and r2["dominant_kernel"]["traffic"] is None
+
+
+def test_kernel_bytes_count_weights_and_kv():
+    import bench
+
+    a0 = bench.kernel_alg_bytes("fused_attn", 0)
+    a9 = bench.kernel_alg_bytes("fused_attn", 9)
+    assert a9 - a0 == 9 * bench.KV_BYTES_W
+    assert bench.kernel_alg_bytes("fused_ffn", 100) == bench.kernel_alg_bytes("fused_ffn", 0)
