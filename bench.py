@@ -166,7 +166,9 @@ class Dist:
             import torch
             import torch.distributed as dist
 
-            timeout = datetime.timedelta(seconds=300)
+            # a replica that fails ends the others' next collective with an
+            # error after this long, instead of holding them
+            timeout = datetime.timedelta(seconds=float(os.environ.get("Q3_DIST_TIMEOUT_S", "300")))
             if backend == "nccl":
                 torch.cuda.set_device(self.local)
                 dist.init_process_group("nccl", timeout=timeout,

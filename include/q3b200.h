@@ -168,6 +168,16 @@ int q3_decode_attention_noalloc(const void* qkv, const void* q_norm, const void*
                                 void* k_cache, void* v_cache, int64_t slot0, int64_t S,
                                 const int64_t* pos, void* out, void* stream);
 
+/* Bounded device waits.  Every wait in these kernels gives up after a spin
+ * budget (about 1 s of SM clock), records a code in a device error word and
+ * returns.  q3_selftest_bounded_wait launches one such wait on a device flag:
+ * it ends when *flag == expect or after limit_cycles (<= 2e9) and then writes
+ * 3 (wait expired) into *err if *err was 0.  q3_check_error_word synchronizes
+ * `stream` and returns Q3_ERR_DEVICE if the word at err is non-zero. */
+int q3_selftest_bounded_wait(const int* flag, int expect, int64_t limit_cycles, int* err,
+                             void* stream);
+int q3_check_error_word(const int* err, void* stream);
+
 /* ------------------------------------------------- IREE-ABI kernels
  * The six substituted executables of compile.sh:36-42 / :58-65, compiled for
  * sm_100a with the same export names and parameter lists
@@ -334,6 +344,15 @@ int q3_model_trace_kernels(q3_model* m, int64_t steps, long long* out, int32_t* 
 
 /* Kernel launches of one generation step of the GRAPH engine. */
 int q3_model_launches_per_step(q3_model* m, int64_t* n);
+/* Test hook for the device-side checks: writes the decode state on purpose --
+ * Q3_POKE_TOKEN: the token table entry at position index; Q3_POKE_POS: the
+ * current position -- so that a following step meets an out-of-range token
+ * or position.  The kernels then record kErrBadToken / kErrBadPos (4 / 5) in
+ * the error word, touch nothing outside their buffers, and the next call
+ * returns Q3_ERR_DEVICE; the model stays usable for a new generation. */
+#define Q3_POKE_TOKEN 0
+#define Q3_POKE_POS 1
+int q3_model_poke(q3_model* m, int what, int64_t index, int64_t value);
 /* Device error word of the last run (0: none; see q3_strerror(Q3_ERR_DEVICE)). */
 int q3_model_device_error(q3_model* m, int* code);
 

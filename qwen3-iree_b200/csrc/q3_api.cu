@@ -924,6 +924,40 @@ extern "C" int q3_fused_layer(const q3_weights* w, int layer, const void* x_in, 
   return Q3_OK;
 }
 
+// Error-path plumbing ---------------------------------------------------------
+// One thread waits, bounded by limit_cycles of SM clock, for *flag == expect;
+// on expiry it records kErrTimeoutGrid in *err (the same bounded-wait pattern
+// as every wait of the decode kernels) and returns, leaving the context usable.
+__global__ void k_bounded_wait(const int* flag, int expect, long long limit, int* err) {
+  if (threadIdx.x != 0) return;
+  const long long t0 = clock64();
+  while (*(volatile const int*)flag != expect) {
+    if (clock64() - t0 > limit) {
+      atomicCAS(err, 0, kErrTimeoutGrid);
+      return;
+    }
+  }
+}
+
+extern "C" int q3_selftest_bounded_wait(const int* flag, int expect, int64_t limit_cycles,
+                                        int* err, void* stream) {
+  Q3_REQUIRE(flag && err, "null pointer");
+  Q3_REQUIRE(limit_cycles >= 1 && limit_cycles <= kSpinCycles,
+             "limit_cycles must be in [1, %lld]", (long long)kSpinCycles);
+  k_bounded_wait<<<1, 32, 0, (cudaStream_t)stream>>>(flag, expect, (long long)limit_cycles, err);
+  Q3_CUDA(cudaGetLastError());
+  return Q3_OK;
+}
+
+extern "C" int q3_check_error_word(const int* err, void* stream) {
+  Q3_REQUIRE(err, "null pointer");
+  int code = 0;
+  Q3_CUDA(cudaMemcpyAsync(&code, err, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  Q3_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  if (code != 0) return set_err(Q3_ERR_DEVICE, "kernel error word %d", code);
+  return Q3_OK;
+}
+
 // IREE-ABI dispatch launchers --------------------------------------------------
 #define Q3_IREE_CHECK(w, b1, b2)                                                  \
   Q3_REQUIRE((w) && (b1) && (b2), "null binding");                                \
@@ -1113,6 +1147,7 @@ static int enqueue_layers(q3_model* m, bool ingest, int* launches, const StepPro
     a.err = m->err;
     if (l == 0) {
       a.tokens = m->tokens;
+      a.S = m->S;
       a.embd = (const uint16_t*)m->w.token_embd;
       a.embed_out = m->x;
     }
@@ -1269,6 +1304,7 @@ static int enqueue_vocab(q3_model* m, int* launches, const StepProbe* probe, int
   v.counter = m->am_counter;
   v.seq = m->st;
   v.tokens = m->tokens;
+  v.S = m->S;
   v.err = m->err;
   v.trace = probe_trace(probe, Q3_KIND_VOCAB);
   int rc = launch_vocab(v, st, launches, true);
@@ -1525,6 +1561,23 @@ extern "C" int q3_model_launches_per_step(q3_model* m, int64_t* n) {
   Q3_REQUIRE(m && n, "null pointer");
   *n = m->engine == Q3_ENGINE_FUSED ? m->launches_gen_f : m->engine == Q3_ENGINE_PERSISTENT ? 1
                                                                                           : m->launches_gen;
+  return Q3_OK;
+}
+
+extern "C" int q3_model_poke(q3_model* m, int what, int64_t index, int64_t value) {
+  Q3_REQUIRE(m, "null model");
+  if (what == Q3_POKE_TOKEN) {
+    Q3_REQUIRE(index >= 0 && index <= m->S, "token index %lld outside [0, %lld]",
+               (long long)index, (long long)m->S);
+    Q3_CUDA(cudaMemcpyAsync(m->tokens + index, &value, sizeof(int64_t), cudaMemcpyHostToDevice,
+                            m->stream));
+  } else if (what == Q3_POKE_POS) {
+    Q3_CUDA(cudaMemcpyAsync(&m->st->pos, &value, sizeof(int64_t), cudaMemcpyHostToDevice,
+                            m->stream));
+  } else {
+    return set_err(Q3_ERR_INVALID, "unknown poke %d", what);
+  }
+  Q3_CUDA(cudaStreamSynchronize(m->stream));
   return Q3_OK;
 }
 

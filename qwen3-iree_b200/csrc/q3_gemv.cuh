@@ -59,6 +59,7 @@ struct Q8GemvArgs {
   // input is row tokens[seq->pos] of embd, and CTA 0 also stores it to embed_out.
   const int64_t* tokens;
   const SeqState* seq;
+  int64_t S;             // positions the token table covers (tokens has S + 1 entries)
   const uint16_t* embd;
   uint16_t* embed_out;
   SeqState* advance;     // if set, pos += 1 (the step's last kernel, prompt ingestion)
@@ -499,10 +500,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv_q8(const __grid_consta
   if (kNorm && !stopped) {
     load_gamma_regs<G * 1024>(a.norm_g, a.K, gr);
     if (a.tokens != nullptr) {
-      int64_t tok = a.tokens[a.seq->pos];
-      if (tok < 0 || tok >= kVocab) {
-        if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
-        tok = 0;
+      const int64_t pos = a.seq->pos;
+      int64_t tok = 0;
+      if (pos < 0 || pos >= a.S) {  // a corrupted state: report it, touch nothing outside
+        if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
+      } else {
+        tok = a.tokens[pos];
+        if (tok < 0 || tok >= kVocab) {
+          if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
+          tok = 0;
+        }
       }
       xin = a.embd + tok * (int64_t)kDim;
     }
@@ -729,10 +736,16 @@ __global__ void __launch_bounds__(kGemv1tThreads, gemv1t_min_blocks<G, MODE>())
   if (kNorm && !stopped) {
     load_gamma_regs<G * 1024>(a.norm_g, a.K, gr);
     if (a.tokens != nullptr) {
-      int64_t tok = a.tokens[a.seq->pos];
-      if (tok < 0 || tok >= kVocab) {
-        if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
-        tok = 0;
+      const int64_t pos = a.seq->pos;
+      int64_t tok = 0;
+      if (pos < 0 || pos >= a.S) {  // a corrupted state: report it, touch nothing outside
+        if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
+      } else {
+        tok = a.tokens[pos];
+        if (tok < 0 || tok >= kVocab) {
+          if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadToken);
+          tok = 0;
+        }
       }
       xin = a.embd + tok * (int64_t)kDim;
     }
@@ -844,6 +857,7 @@ struct VocabArgs {
   // Decode-state update done by the last CTA (optional):
   SeqState* seq;           // pos += 1; tokens[pos] = argmax; n_gen / stop bookkeeping
   int64_t* tokens;
+  int64_t S;               // positions the token table covers (tokens has S + 1 entries)
   int* err;
   int nstages;
   unsigned long long* trace;  // optional launch timing record (4 values)
@@ -990,6 +1004,12 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
     if (a.seq != nullptr) {
       SeqState* st = a.seq;
       const int64_t pos = st->pos;
+      if (pos < 0 || pos >= a.S) {  // a corrupted state: report it, write nothing
+        if (a.err) atomicCAS(a.err, 0, kErrBadPos);
+        st->stop = 1;
+        *a.counter = 0u;
+        return;
+      }
       a.tokens[pos + 1] = bi;
       if (pos >= st->n_prompt) {
         st->n_gen += 1;

@@ -95,6 +95,9 @@ SIGNATURES = {
     "q3_generate_end": [P, P, PI64],
     "q3_model_launches_per_step": [P, PI64],
     "q3_model_device_error": [P, ctypes.POINTER(ctypes.c_int)],
+    "q3_model_poke": [P, I, I64, I64],
+    "q3_selftest_bounded_wait": [P, I, I64, P, P],
+    "q3_check_error_word": [P, P],
     "q3_model_profile_steps": [P, I64, P, P, I64],
     "q3_model_set_engine": [P, I],
     "q3_model_engine": [P, ctypes.POINTER(ctypes.c_int)],

@@ -2,7 +2,10 @@
 
 Run in the build container, where the reference checkout exists:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <reference checkout>]
+
+(default: $Q3_REFERENCE, else a checkout named `reference` beside this
+repository).
 
 It imports quantize_q8_0 / dequant_q8_0 from the reference's
 tools/create_q8_irpa.py (lines 103-129; the module imports only numpy and
@@ -47,7 +50,9 @@ def edge_blocks():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("Q3_REFERENCE", "/root/reference"))
+    here = os.path.dirname(os.path.abspath(__file__))
+    sibling = os.path.normpath(os.path.join(here, "..", "..", "..", "reference"))
+    ap.add_argument("--ref", default=os.environ.get("Q3_REFERENCE", sibling))
     args = ap.parse_args()
     ref = load_reference(args.ref)
 

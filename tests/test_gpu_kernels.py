@@ -263,3 +263,29 @@ def test_reference_vocab_kernel_pins_the_oracle(gpu, O, ref):
         assert getattr(lib_, fn)(dw.ptr, db1.ptr, db2.ptr, 256, None) == 0
         _sync(gpu)
         assert np.array_equal(bits(db2.download()[256:].view(np.float16)), want), fn
+
+
+@pytest.mark.parametrize("d,N,K,in_off,out_off,bpl", IREE)
+def test_product_gemvs_match_the_reference_kernels(gpu, O, ref, d, N, K, in_off, out_off, bpl):
+    """The product's GEMV orders against the reference's own dispatch_N.cu run
+    on this GPU, same data, within the north star's rel-L2 <= 1e-3: the
+    GPU-dialect order of q3_gemv_q8 (and its overlapped launch) and, for the
+    O and down shapes, the fused engine's K-split order (8 slices summed in
+    f32).  The data of dispatch 3 is BASELINE configs[0]: W N(0,0.02)
+    quantised Q8_0, x N(0,1)."""
+    w, x, dw, db1, db2, oo, _ = _iree_setup(gpu, O, N, K, in_off, out_off, 300 + d)
+    assert _launch(ref, "ref", d, dw, db1, db2, oo, 1) == 0
+    _sync(gpu)
+    want = db2.download()[oo:oo + 2 * N].view(np.float16)
+    L = gpu.lib()
+    wl = gpu.DeviceArray.from_host(np.ascontiguousarray(w[1]))
+    dx = _up(gpu, x)
+    for fn in ("q3_gemv_q8", "q3_gemv_q8_overlapped"):
+        dy = gpu.DeviceArray((N,), np.float16)
+        assert getattr(L, fn)(wl.ptr, dx.ptr, dy.ptr, N, K, None) == 0
+        _sync(gpu)
+        got = dy.download()
+        assert rel_l2(got, want) <= 1e-3, (fn, rel_l2(got, want))
+    if K in (2048, 3072):  # the fused engine's split O / down projections
+        split = O.gemv_q8_split(w[1], x, N, K, 8)
+        assert rel_l2(split, want) <= 1e-3

@@ -53,6 +53,42 @@ def test_two_gloo_ranks_aggregate_like_the_gpu_run():
         assert value == pytest.approx(3000.0 / 0.2)
 
 
+def _failing_rank_main(rank: int, world: int, port: int, q) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank), Q3_DIST_TIMEOUT_S="10")
+    sys.path.insert(0, ROOT)
+    import bench
+
+    d = bench.Dist(backend="gloo")
+    if rank == 1:  # this replica fails before the barrier and leaves
+        os._exit(3)
+    try:
+        d.barrier()
+        d.max(1.0)
+        q.put((rank, "no error"))
+    except Exception as e:  # the failure reaches rank 0 as an error, not a hang
+        q.put((rank, type(e).__name__))
+
+
+def test_a_failed_replica_is_reported_not_hung_on():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_failing_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+    alive = [p.is_alive() for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert not any(alive), "a rank still waits on the failed replica"
+    assert procs[1].exitcode == 3
+    rank, what = q.get(timeout=10)
+    assert rank == 0 and what != "no error"
+
+
 def test_aggregate_is_units_over_slowest_rank():
     sys.path.insert(0, ROOT)
     import bench
