@@ -10,7 +10,8 @@ no PyTorch.
 
 Differences forced by this environment: there is no checkpoint or
 tokenizer.json here, so weights are the seeded random-init model of the
-benchmark configs unless --gguf names a Q8_0 checkpoint, and prompts are
+benchmark configs unless --irpa (the reference's archives) or --gguf names a
+Q8_0 checkpoint, and prompts are
 token-id lists -- seeded ones by default, one line of ids per prompt with
 --prompts-file, or text with --tokenizer.
 
@@ -69,7 +70,12 @@ def load_tokenizer(path: str | None):
 
 
 def load_weights(args):
-    """The checkpoint given with --gguf, else the seeded random-init model."""
+    """The checkpoint given with --irpa (the reference's archives) or --gguf,
+    else the seeded random-init model."""
+    if getattr(args, "irpa", None):
+        from .irpa import load_qwen3_q8_irpa
+
+        return load_qwen3_q8_irpa(*args.irpa)
     if getattr(args, "gguf", None):
         from .gguf import load_qwen3_q8
 
@@ -304,6 +310,8 @@ def main(argv=None) -> int:
     ap.add_argument("--text", action="append", default=None, help="text prompt (with --tokenizer)")
     ap.add_argument("--seed", type=int, default=0, help="weights and synthetic prompts")
     ap.add_argument("--gguf", default=None, help="Qwen3-0.6B Q8_0 GGUF checkpoint (else random init)")
+    ap.add_argument("--irpa", nargs="+", default=None,
+                    help="the reference's .irpa archive(s) (tools/create_q8_irpa.py output)")
     ap.add_argument("--engine", default=None, choices=["fused", "graph", "persistent"],
                     help="decode engine (default: the library's, fused where available)")
     ap.add_argument("--max-seq-len", type=int, default=1024)

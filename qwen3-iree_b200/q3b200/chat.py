@@ -8,7 +8,8 @@ does the same through libq3b200.so (q3_run).
 
 With --tokenizer PATH (a tokenizer.json; the `tokenizers` package) lines are
 text; without one (none ships here) a line is a list of token ids and the
-reply is printed as ids.  Weights: a Q8_0 GGUF checkpoint with --gguf, else
+reply is printed as ids.  Weights: the reference's .irpa archives with --irpa,
+a Q8_0 GGUF checkpoint with --gguf, else
 the seeded random-init model.
 
   python -m q3b200.chat [--max-tokens 256] [--tokenizer tokenizer.json]
@@ -52,6 +53,8 @@ def main(argv=None) -> int:
     ap.add_argument("--max-seq-len", type=int, default=1024)
     ap.add_argument("--seed", type=int, default=0, help="random-init weights")
     ap.add_argument("--gguf", default=None, help="Qwen3-0.6B Q8_0 GGUF checkpoint (else random init)")
+    ap.add_argument("--irpa", nargs="+", default=None,
+                    help="the reference's .irpa archive(s) (tools/create_q8_irpa.py output)")
     ap.add_argument("--device", type=int, default=0)
     args = ap.parse_args(argv)
 
