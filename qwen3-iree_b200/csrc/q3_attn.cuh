@@ -131,6 +131,24 @@ __device__ __forceinline__ void head_norm_rope_g(const uint16_t* x, const uint16
   dst[lane + 96] = f2h(__fadd_rn(__fmul_rn(n[1], s1), __fmul_rn(n[3], c1)));
 }
 
+// The same with the head's values v[i] = x[lane + 32 i] already loaded.
+__device__ __forceinline__ void norm_rope_vals(const float (&v)[4], const uint16_t (&gv)[4], float c0,
+                                               float s0, float c1, float s1, int lane,
+                                               uint16_t* dst) {
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = __fmaf_rn(v[i], v[i], ss);
+  ss = warp_sum(ss);
+  const float r = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, 128.0f), kEps));
+  float n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = h2f(f2h(__fmul_rn(__fdiv_rn(v[i], r), h2f(gv[i]))));
+  dst[lane] = f2h(__fsub_rn(__fmul_rn(n[0], c0), __fmul_rn(n[2], s0)));
+  dst[lane + 64] = f2h(__fadd_rn(__fmul_rn(n[0], s0), __fmul_rn(n[2], c0)));
+  dst[lane + 32] = f2h(__fsub_rn(__fmul_rn(n[1], c1), __fmul_rn(n[3], s1)));
+  dst[lane + 96] = f2h(__fadd_rn(__fmul_rn(n[1], s1), __fmul_rn(n[3], c1)));
+}
+
 __device__ __forceinline__ void att_merge(float& m, float& l, float (&o)[4], float mb, float lb,
                                           const float (&ob)[4]) {
   const float mm = fmaxf(m, mb);

@@ -86,6 +86,12 @@ __host__ __device__ constexpr int bgemm_substages(int naccum) { return naccum ==
 constexpr int kBgMaxKc = 2;       // chunks per CTA: all of its activations stay resident
 constexpr int kBgMaxSplits = 8;   // CTAs per tile = one portable cluster
 
+// Items of the split reduction per CTA: ceil(total / splits), rounded up to a
+// multiple of 4 so that every share starts on a 16-byte boundary.
+__host__ __device__ constexpr int bgemm_red_per(int total, int splits) {
+  return ((total + splits - 1) / splits + 3) / 4 * 4;
+}
+
 // Dynamic shared memory: weight stages (reused for the f32 partials), every
 // activation slice of the CTA's K range, and one raw stage per chunk.
 __host__ __device__ constexpr size_t bgemm_smem_bytes(int npad, int naccum, int kc) {
@@ -164,7 +170,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
   constexpr int SUB = bgemm_substages(NACC);
   constexpr uint32_t TCOLS = NPAD * NACC <= 32 ? 32 : NPAD * NACC <= 64 ? 64 : 128;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t raw_full[kBgMaxKc], x_full, acc_full;
+  __shared__ __align__(8) uint64_t raw_full[kBgMaxKc], x_full, acc_full, red_bar;
   __shared__ __align__(8) uint64_t a_full[kBgSubStages], a_empty[kBgSubStages];
   __shared__ uint32_t tmem_base;
 
@@ -189,7 +195,14 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
     }
     mbar_init(&x_full, 1);
     mbar_init(&acc_full, 1);
+    mbar_init(&red_bar, 1);
     fence_mbar_init();
+    if (gridDim.y > 1) {  // the bytes of this CTA's share of the split reduction
+      const int total = 128 * NPAD, per = bgemm_red_per(total, (int)gridDim.y);
+      const int i0 = (int)cluster_rank() * per;
+      const int len = i0 >= total ? 0 : (total - i0 < per ? total - i0 : per);
+      mbar_expect_tx(&red_bar, (uint32_t)((int)gridDim.y * NACC * len * 4));
+    }
   }
   if (warp == 1) {
     tmem_alloc(&tmem_base, TCOLS);
@@ -312,8 +325,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
           }
         }
       } else if (splits > 1) {
-        // partial [acc][b][row] f32 over the (now idle) weight stages; rows
-        // contiguous so the remote reads of consecutive rows hit distinct banks
+        // partial [acc][b][row] f32 over the (now idle) raw weight stages
 #pragma unroll
         for (int acc = 0; acc < NACC; ++acc) {
 #pragma unroll
@@ -329,7 +341,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
 #pragma unroll
             for (int j = 0; j < 16; ++j)
               asm volatile("st.shared.b32 [%0], %1;" ::"r"(
-                               sA + (uint32_t)(((acc * NPAD + col0 + j) * 128 + (int)r) * 4)),
+                               sR + (uint32_t)(((acc * NPAD + col0 + j) * 128 + (int)r) * 4)),
                            "r"(v[j])
                            : "memory");
           }
@@ -339,30 +351,48 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
   }
   if (splits > 1) {
     // ------------------------------------------------ cluster reduction
+    // CTA d reduces items [d*per, (d+1)*per) of the tile's 128 x NPAD outputs
+    // (item = b*128 + row).  After one cluster barrier (every CTA's MMAs are
+    // done, so every weight-stage region is free), each CTA pushes its
+    // partial of those items into CTA d's stage region as R[s][acc][j] with
+    // 16-byte st.async whose bytes count on d's red_bar; d waits for its
+    // bytes and sums R[0..S-1] in split order (the same bits whatever the
+    // timing).  No CTA touches another's shared memory after its own wait.
     __syncwarp();
-    cluster_sync_all();  // every CTA's partial is in its shared memory
+    cluster_sync_all();
+    const int total = 128 * NPAD, per = bgemm_red_per(total, splits);
+    const int me = (int)cluster_rank();
     if (warp >= 2) {
+      const int t = threadIdx.x - 64;  // 0 .. 255
+      for (int dst = 0; dst < splits; ++dst) {
+        const int i0 = dst * per;
+        const int len = i0 >= total ? 0 : (total - i0 < per ? total - i0 : per);
+        for (int acc = 0; acc < NACC; ++acc)
+          for (int j4 = t; j4 < len / 4; j4 += 32 * kBgDqWarps) {
+            uint4 v;
+            lds128(sR + (uint32_t)(((acc * total) + i0 + 4 * j4) * 4), v.x, v.y, v.z, v.w);
+            st_async_v4(sA + (uint32_t)(((me * NACC + acc) * per + 4 * j4) * 4), (uint32_t)dst, v,
+                        smem_u32(&red_bar));
+          }
+      }
+      const bool got = Q3_BWAIT(&red_bar, 0, kErrTimeoutFull, 11);
       pdl_wait();  // reads the residual stream / writes buffers of earlier kernels
-      const int t = threadIdx.x - 64;                      // 0 .. 255
-      const int total = 128 * NPAD;
-      const int per = (total + splits - 1) / splits;
-      const int i0 = (int)cluster_rank() * per;
+      const int i0 = me * per;
       const int i1 = i0 + per < total ? i0 + per : total;
-      for (int i = i0 + t; i < i1; i += 32 * kBgDqWarps) {
+      for (int i = i0 + t; got && i < i1; i += 32 * kBgDqWarps) {
         const int b = i >> 7, row = i & 127;
         if (b >= a.B) continue;
         float sum[NACC];
 #pragma unroll
         for (int acc = 0; acc < NACC; ++acc) {
-          float v[kBgMaxSplits];
-          const uint32_t off = sA + (uint32_t)(((acc * NPAD + b) * 128 + row) * 4);
-#pragma unroll
-          for (int sp = 0; sp < kBgMaxSplits; ++sp)
-            v[sp] = sp < splits ? ld_dsmem_f32(off, (uint32_t)sp) : 0.0f;
-          float s0 = v[0];
-#pragma unroll
-          for (int sp = 1; sp < kBgMaxSplits; ++sp)
-            if (sp < splits) s0 = __fadd_rn(s0, v[sp]);
+          float s0 = 0.0f;
+          for (int sp = 0; sp < splits; ++sp) {
+            float v;
+            asm volatile("ld.shared.f32 %0, [%1];"
+                         : "=f"(v)
+                         : "r"(sA + (uint32_t)(((sp * NACC + acc) * per + (i - i0)) * 4)));
+            s0 = sp == 0 ? v : __fadd_rn(s0, v);
+          }
           sum[acc] = s0;
         }
         const int n = n0 + row;
@@ -375,9 +405,8 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
           out = f2h(sum[0]);
         a.y[(int64_t)b * a.ldy + n] = out;
       }
+      if (!got) Q3_BWAIT(&red_bar, 0, kErrTimeoutFull, 12);  // pushes into this CTA landed
     }
-    __syncwarp();
-    cluster_sync_all();  // no CTA leaves while another still reads its shared memory
   }
   tc_fence_before();
   __syncthreads();

@@ -5,18 +5,30 @@
 // attention over keys 0..pos (:456-530) -- for B sequences with their own
 // positions, built for HBM throughput instead of batch-1 latency:
 //
-//   * CTA = (kv head h, segment of 512 keys, sequence b); a producer thread
-//     streams 32-key K and V tiles (one 8 KB tensor-TMA box each, the cache
-//     seen as [B*28*S rows, 1024] f16) through a ring of stages.  Cache rows
-//     below pos were written by earlier launches, so the stream starts before
-//     the wait on the previous kernel; only q and the new row need it.
+//   * the work is the list of 32-key chunks of every (sequence b, kv head h),
+//     flattened in (b, h, chunk) order; CTA g of a persistent grid (two per
+//     SM) takes the equal share [g T / G, (g+1) T / G) of the T chunks, so
+//     every CTA streams the same number of bytes whatever the mix of
+//     positions (no tail wave).  A share cuts the list into pieces, one per
+//     (b, h) it touches.
+//   * a producer thread streams the share's 32-key K and V tiles (one 8 KB
+//     tensor-TMA box each, the cache seen as [B*28*S rows, 1024] f16)
+//     through a ring of stages.  Cache rows below pos were written by
+//     earlier launches, so the stream starts before the wait on the previous
+//     kernel; only q and the new row need it.
+//   * a q warp stages, per piece, the normed and roped q of both q heads of h
+//     and the new K/V row (written to the cache once, by the piece that holds
+//     the last chunk) in a ring of piece slots; its loads of one piece are
+//     issued together, and the gammas and RoPE rows (which do not depend on
+//     the previous kernel) before the wait.
 //   * 4 consumer warps take chunks round robin and keep an online softmax
-//     (m, l, o) for both q heads of the kv head: lane = key for q.k (each lane
-//     reads its K row in a lane-rotated 16-byte order, so a quarter warp hits
-//     8 distinct bank groups), lane = 4 head dims for p.v.
-//   * the warps' states merge in warp order; a sequence whose keys span
-//     several segments publishes one partial per segment and the CTA that
-//     finishes last for (b, h) merges them in segment order.
+//     (m, l, o) for both q heads: lane = key for q.k (each lane reads its K
+//     row in a lane-rotated 16-byte order, so a quarter warp hits 8 distinct
+//     bank groups), lane = 4 head dims for p.v.  At the end of a piece the
+//     warp that finishes it last merges the 4 states in warp order; a (b, h)
+//     that spans CTAs publishes one partial per CTA and the CTA that
+//     finishes it last merges them in CTA order (the same bits whatever the
+//     timing).
 //
 // The accumulation order differs from the batch-1 kernel's, so this path is
 // held to a tolerance (rel-L2 <= 1e-3), like the rest of the batched decoder.
@@ -31,7 +43,8 @@
 namespace q3 {
 
 constexpr int kBaWarps = 4;                       // consumer warps
-constexpr int kBaThreads = 32 * (kBaWarps + 1);   // + the producer warp
+constexpr int kBaThreads = 32 * (kBaWarps + 2);   // + the producer and the q warp
+constexpr int kBaProducer = kBaWarps;             // warp index of the producer
 #ifndef Q3_BA_STAGES
 #define Q3_BA_STAGES 6
 #endif
@@ -46,8 +59,10 @@ constexpr int kBaStages = Q3_BA_STAGES;           // K+V tiles in flight per CTA
 // producer arms chunk i.
 constexpr int kBaFullBars = ((kBaStages + kBaWarps - 1) / kBaWarps) * kBaWarps;
 static_assert(kBaFullBars % kBaWarps == 0 && kBaFullBars >= kBaStages, "full barrier count");
-constexpr int kBaSegChunks = 16;                  // default 32-key chunks per CTA (512 keys)
 constexpr uint32_t kBaTileBytes = 32u * kHD * 2u; // one 32-key K (or V) tile
+constexpr int kBaCtasPerSm = 2;                   // persistent grid: CTAs per SM
+constexpr int kBaQSlots = 4;                      // pieces whose q is staged ahead
+constexpr int kBaMaxBatch = 64;
 
 struct BAttnArgs {
   CUtensorMap kmap;        // K cache f16 [B*28*S rows, 1024], box {128, 32}
@@ -62,79 +77,174 @@ struct BAttnArgs {
   uint16_t* vc;
   int64_t S;               // slots per layer
   int layer;
+  int B;                   // sequences, <= 64
   const int64_t* pos;      // pos[b * pos_stride]
   int pos_stride;
   uint16_t* out;           // [npad][2048]
-  AttnPartial* part;       // [B][8][max_segs][2]
-  unsigned int* counters;  // [B][8]
-  int max_segs;
-  int seg_chunks;          // 32-key chunks per CTA
+  AttnPartial* part;       // [gridDim.x][2 slots][2 q heads]
+  unsigned int* counters;  // [B][8], zero between launches
   int* err;
   int tag;
   unsigned long long* trace;  // optional launch timing record
 };
 
+// One (b, h) piece of a CTA's share: chunks [u0, u1) of the flattened list,
+// of which (b, h) owns [s0, s1).
+struct BaPiece {
+  int b, h;
+  int u0, u1, s0, s1;
+};
+
 struct BAttnSmem {
   uint64_t full[kBaFullBars], empty[kBaStages];
-  float wm[kBaWarps][2], wl[kBaWarps][2];
-  float wo[kBaWarps][2][kHD];
-  uint16_t qs[2][kHD];
-  uint16_t ks[kHD];
-  int last;
+  uint64_t qready[kBaQSlots], qfree[kBaQSlots], wfree[2];
+  int nch[kBaMaxBatch];        // chunks of sequence b (per kv head)
+  int pre[kBaMaxBatch + 1];    // pre[b] = 8 * sum of nch below b
+  long long pos[kBaMaxBatch];
+  int b0, bad;
+  unsigned int pcnt[2];        // warps done with the piece in state slot p % 2
+  __align__(16) uint16_t q[kBaQSlots][2][kHD];
+  __align__(16) uint16_t kn[kBaQSlots][kHD];
+  __align__(16) uint16_t vn[kBaQSlots][kHD];
+  float wm[2][kBaWarps][2], wl[2][kBaWarps][2];
+  __align__(16) float wo[2][kBaWarps][2][kHD];
 };
 
 __host__ __device__ constexpr size_t battn_smem_bytes() {
   return 1024 + (size_t)kBaStages * 2 * kBaTileBytes;
 }
 
-__device__ __forceinline__ int battn_nsegs(int64_t pos, int seg_chunks) {
-  const int nch = (int)((pos + kAttChunk) / kAttChunk);
-  return (nch + seg_chunks - 1) / seg_chunks;
+// Partials a grid of `grid` CTAs may publish, and the workspace they and the
+// per-(b, h) counters take.
+__host__ __device__ constexpr size_t battn_workspace_bytes(int grid, int B) {
+  return sizeof(AttnPartial) * (size_t)grid * 4 + (size_t)B * kNKV * 4;
 }
 
-__device__ __forceinline__ void battn_named_sync() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 consumer warps
+// The CTA whose share holds flattened chunk u (shares [g T / G, (g+1) T / G)).
+__device__ __forceinline__ int battn_cta_of(long long u, long long T, long long G) {
+  return (int)(((u + 1) * G + T - 1) / T - 1);
 }
 
-__global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BAttnArgs a) {
+// Walks the pieces of share [lo, hi): start with (b0, the h holding lo).
+struct BaWalker {
+  int b, h, lo, hi;
+  __device__ void start(const BAttnSmem& sm, int b_first, int lo_, int hi_) {
+    b = b_first;
+    lo = lo_;
+    hi = hi_;
+    h = (lo - sm.pre[b]) / sm.nch[b];
+  }
+  __device__ bool done(const BAttnSmem& sm) const {
+    return b >= kBaMaxBatch || sm.pre[b] + h * sm.nch[b] >= hi;
+  }
+  __device__ BaPiece get(const BAttnSmem& sm) const {
+    BaPiece p;
+    p.b = b;
+    p.h = h;
+    p.s0 = sm.pre[b] + h * sm.nch[b];
+    p.s1 = p.s0 + sm.nch[b];
+    p.u0 = p.s0 > lo ? p.s0 : lo;
+    p.u1 = p.s1 < hi ? p.s1 : hi;
+    return p;
+  }
+  __device__ void next() {
+    if (++h == kNKV) {
+      h = 0;
+      ++b;
+    }
+  }
+};
+
+__device__ __forceinline__ void battn_merge_state(float& m, float& l, float (&o)[4], float mb,
+                                                  float lb, const float (&ob)[4]) {
+  if (lb == 0.0f) return;  // nothing on that side
+  if (l == 0.0f) {
+    m = mb;
+    l = lb;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = ob[j];
+    return;
+  }
+  att_merge(m, l, o, mb, lb, ob);
+}
+
+__global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid_constant__ BAttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(16) BAttnSmem sm;
-  const int h = blockIdx.x, seg = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - smem_u32(smem_raw));
-
-  // positions were set by an earlier graph launch: readable before the wait
-  const int64_t pos = a.pos[(int64_t)b * a.pos_stride];
-  const bool bad = pos < 0 || pos >= a.S || pos >= a.rope_rows ||
-                   battn_nsegs(pos, a.seg_chunks) > a.max_segs;
-  if (bad || seg >= battn_nsegs(pos, a.seg_chunks)) {
-    pdl_launch_dependents();
-    if (bad && seg == 0 && h == 0 && threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
-    return;
-  }
-  const int nch_all = (int)((pos + kAttChunk) / kAttChunk);
-  const int c0 = seg * a.seg_chunks;
-  const int nch = nch_all - c0 < a.seg_chunks ? nch_all - c0 : a.seg_chunks;
-  const int nsegs = battn_nsegs(pos, a.seg_chunks);
-  const int64_t row0 = ((int64_t)b * kLayers + a.layer) * a.S;  // cache row of slot 0
-
+  const int B = a.B;
   ktrace_start(a.trace);
+
+  // ------------------------------------------------ the work list
+  // positions were set by an earlier graph launch: readable before the wait
   if (threadIdx.x == 0) {
+    sm.bad = 0;
+    sm.pcnt[0] = sm.pcnt[1] = 0u;
+  }
+  __syncthreads();
+  if (threadIdx.x < B) {
+    const int64_t pos = a.pos[(int64_t)threadIdx.x * a.pos_stride];
+    const bool bad = pos < 0 || pos >= a.S || pos >= a.rope_rows;
+    sm.pos[threadIdx.x] = pos;
+    sm.nch[threadIdx.x] = bad ? 1 : (int)(pos / kAttChunk) + 1;
+    if (bad) sm.bad = 1;
+  }
+  if (threadIdx.x == 32 * kBaProducer) {
     for (int i = 0; i < kBaFullBars; ++i) mbar_init(&sm.full[i], 1);
     for (int i = 0; i < kBaStages; ++i) mbar_init(&sm.empty[i], 1);
+    for (int i = 0; i < kBaQSlots; ++i) {
+      mbar_init(&sm.qready[i], 32);
+      mbar_init(&sm.qfree[i], 32);
+    }
+    mbar_init(&sm.wfree[0], 32);
+    mbar_init(&sm.wfree[1], 32);
     fence_mbar_init();
   }
   __syncthreads();
+  if (warp == 0) {  // exclusive prefix of 8 * nch over b (B <= 64: two lanes' worth)
+    const int v0 = lane < B ? kNKV * sm.nch[lane] : 0;
+    const int v1 = lane + 32 < B ? kNKV * sm.nch[lane + 32] : 0;
+    int i0 = v0, i1 = v1;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int t0 = __shfl_up_sync(0xffffffffu, i0, d), t1 = __shfl_up_sync(0xffffffffu, i1, d);
+      if (lane >= d) i0 += t0, i1 += t1;
+    }
+    const int tot0 = __shfl_sync(0xffffffffu, i0, 31);
+    sm.pre[lane] = i0 - v0;
+    sm.pre[lane + 32] = tot0 + i1 - v1;
+    if (lane == 31) sm.pre[kBaMaxBatch] = tot0 + i1;
+  }
+  __syncthreads();
+  const long long T = sm.pre[kBaMaxBatch];
+  const long long G = (long long)gridDim.x < T ? (long long)gridDim.x : T;
+  const int g = blockIdx.x;
+  if (sm.bad || g >= G) {
+    pdl_launch_dependents();
+    if (sm.bad && g == 0 && threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
+    return;
+  }
+  const int lo = (int)(g * T / G), hi = (int)((g + 1) * T / G);
+  if (warp == 0) {  // the sequence holding chunk lo
+    for (int bb = lane; bb < B; bb += 32)
+      if (sm.pre[bb] <= lo && lo < sm.pre[bb + 1]) sm.b0 = bb;
+  }
+  __syncthreads();
   pdl_launch_dependents();
+  const int b_first = sm.b0;
 
-  if (warp == kBaWarps) {
+  if (warp == kBaProducer) {
     // ------------------------------------------------ producer: K/V tiles
     if (lane == 0) {
       prefetch_tmap(&a.kmap);
       prefetch_tmap(&a.vmap);
+      const int n = hi - lo;
+      int b = b_first, h = (lo - sm.pre[b]) / sm.nch[b];
+      int c = lo - sm.pre[b] - h * sm.nch[b];
       int issued = 0;
-      for (int i = 0; i < nch; ++i) {
+      for (int i = 0; i < n; ++i) {
         const int st = i % kBaStages;
         if (i >= kBaStages &&
             !mbar_wait_own(&sm.empty[st], ((i / kBaStages) - 1) & 1, a.err,
@@ -142,10 +252,17 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
           break;
         uint64_t* const fb = &sm.full[i % kBaFullBars];
         mbar_expect_tx(fb, 2 * kBaTileBytes);
-        const int y = (int)(row0 + (int64_t)(c0 + i) * kAttChunk);
+        const int y = (int)(((int64_t)b * kLayers + a.layer) * a.S + (int64_t)c * kAttChunk);
         tma_load_2d(gbase + st * 2 * kBaTileBytes, &a.kmap, h * kHD, y, fb);
         tma_load_2d(gbase + st * 2 * kBaTileBytes + kBaTileBytes, &a.vmap, h * kHD, y, fb);
         issued = i + 1;
+        if (++c == sm.nch[b]) {
+          c = 0;
+          if (++h == kNKV) {
+            h = 0;
+            ++b;
+          }
+        }
       }
       // no copy in flight at exit: every chunk before issued - kBaStages was
       // consumed, so only the last kBaStages can still be landing
@@ -153,197 +270,261 @@ __global__ void __launch_bounds__(kBaThreads) k_battn(const __grid_constant__ BA
         mbar_wait_own(&sm.full[i % kBaFullBars], (i / kBaFullBars) & 1, a.err,
                       kErrTimeoutFull | (2 << 4) | ((a.tag & 0xff) << 8), kSpinCycles);
     }
-    return;  // the producer warp takes no part in the consumers' barriers
+    return;  // the producer warp takes no part in the other warps' barriers
+  }
+
+  BaWalker wk;
+  wk.start(sm, b_first, lo, hi);
+
+  if (warp > kBaProducer) {
+    // ------------------------------------------------ q warp: per-piece q, new K/V row
+    uint16_t gq[4], gk[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      gq[i] = a.q_norm[lane + 32 * i];
+      gk[i] = a.k_norm[lane + 32 * i];
+    }
+    bool waited = false;
+    for (int p = 0; !wk.done(sm); ++p, wk.next()) {
+      const BaPiece pc = wk.get(sm);
+      const int sl = p % kBaQSlots;
+      if (p >= kBaQSlots &&
+          !mbar_wait_own(&sm.qfree[sl], ((p / kBaQSlots) - 1) & 1, a.err,
+                         kErrTimeoutEmpty | (3 << 4) | ((a.tag & 0xff) << 8), kSpinCycles))
+        break;
+      const bool holds_pos = pc.s1 <= hi;  // this piece holds the (b, h)'s last chunk
+      const int64_t pos = sm.pos[pc.b];
+      const float* ct = a.rope_cos + pos * 64;
+      const float* sn = a.rope_sin + pos * 64;
+      const float cc0 = ct[lane], s0 = sn[lane], cc1 = ct[lane + 32], s1 = sn[lane + 32];
+      if (!waited) {
+        pdl_wait();  // q, k, v come from the previous kernel
+        waited = true;
+      }
+      const unsigned short* qkv =
+          reinterpret_cast<const unsigned short*>(a.qkv) + (int64_t)pc.b * 4096;
+      float q0[4], q1[4], kn[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        q0[i] = h2f(__ldcg(qkv + 2 * pc.h * kHD + lane + 32 * i));
+        q1[i] = h2f(__ldcg(qkv + (2 * pc.h + 1) * kHD + lane + 32 * i));
+        kn[i] = holds_pos ? h2f(__ldcg(qkv + 2048 + pc.h * kHD + lane + 32 * i)) : 0.0f;
+      }
+      const uint2 v = holds_pos ? __ldcg(reinterpret_cast<const uint2*>(qkv + 3072 + pc.h * kHD) + lane)
+                                : make_uint2(0u, 0u);
+      norm_rope_vals(q0, gq, cc0, s0, cc1, s1, lane, sm.q[sl][0]);
+      norm_rope_vals(q1, gq, cc0, s0, cc1, s1, lane, sm.q[sl][1]);
+      if (holds_pos) {
+        norm_rope_vals(kn, gk, cc0, s0, cc1, s1, lane, sm.kn[sl]);
+        *reinterpret_cast<uint2*>(&sm.vn[sl][4 * lane]) = v;
+        __syncwarp();
+        const int64_t off =
+            (((int64_t)pc.b * kLayers + a.layer) * a.S + pos) * (kNKV * kHD) + pc.h * kHD;
+        *reinterpret_cast<uint2*>(a.kc + off + 4 * lane) =
+            *reinterpret_cast<const uint2*>(&sm.kn[sl][4 * lane]);
+        *reinterpret_cast<uint2*>(a.vc + off + 4 * lane) = v;
+      }
+      mbar_arrive(&sm.qready[sl]);
+    }
+    return;
   }
 
   // ------------------------------------------------ consumers (warps 0-3)
-  pdl_wait();  // q, k, v come from the previous kernel
-  ktrace_release(a.trace);
-  const uint16_t* qkv = a.qkv + (int64_t)b * 4096;
-  if (warp < 3) {
-    const float* ct = a.rope_cos + pos * 64;
-    const float* sn = a.rope_sin + pos * 64;
-    const float cc0 = ct[lane], s0 = sn[lane], cc1 = ct[lane + 32], s1 = sn[lane + 32];
-    if (warp < 2)
-      head_norm_rope(qkv + (2 * h + warp) * kHD, a.q_norm, cc0, s0, cc1, s1, lane, sm.qs[warp]);
-    else
-      head_norm_rope(qkv + 2048 + h * kHD, a.k_norm, cc0, s0, cc1, s1, lane, sm.ks);
-  }
-  battn_named_sync();
-  const bool holds_pos = seg == nsegs - 1;
-  if (holds_pos && threadIdx.x < kHD) {  // the new K (normed, roped) and V rows
-    const int64_t off = ((int64_t)b * kLayers * a.S + (int64_t)a.layer * a.S + pos) * (kNKV * kHD) +
-                        h * kHD + threadIdx.x;
-    a.kc[off] = sm.ks[threadIdx.x];
-    a.vc[off] = __ldcg(reinterpret_cast<const unsigned short*>(qkv) + 3072 + h * kHD + threadIdx.x);
-  }
-  // q in registers as f16 pairs: lane-rotated order matches the K reads below
-  const uint4* q0p = reinterpret_cast<const uint4*>(sm.qs[0]);
-  const uint4* q1p = reinterpret_cast<const uint4*>(sm.qs[1]);
-  const uint2 vnew = __ldcg(reinterpret_cast<const uint2*>(qkv + 3072 + h * kHD + 4 * lane));
-
-  float m[2] = {-__int_as_float(0x7f800000), -__int_as_float(0x7f800000)};
-  float l[2] = {0.0f, 0.0f};
-  float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  for (int i = warp; i < nch; i += kBaWarps) {
-    const int st = i % kBaStages;
-    if (!mbar_wait_own(&sm.full[i % kBaFullBars], (i / kBaFullBars) & 1, a.err,
-                       kErrTimeoutFull | (3 << 4) | ((a.tag & 0xff) << 8), kSpinCycles))
-      break;
-    const int64_t t0 = (int64_t)(c0 + i) * kAttChunk;
-    const int tp = pos < t0 + kAttChunk ? (int)(pos - t0) : -1;  // the new key in this chunk
-    const int nvalid = (pos + 1 - t0) < kAttChunk ? (int)(pos + 1 - t0) : kAttChunk;
-    const uint32_t kt = base + st * 2 * kBaTileBytes, vt = kt + kBaTileBytes;
-    // q.k, lane = key
-    float s[2] = {-__int_as_float(0x7f800000), -__int_as_float(0x7f800000)};
-    if (lane < nvalid) {
-      // four independent accumulation chains per head (16 FMAs deep, not 128)
-      float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int j = 0; j < kHD / 8; ++j) {
-        const int cidx = (j + lane) & 15;
-        uint4 kk;
-        if (lane == tp) {
-          kk = reinterpret_cast<const uint4*>(sm.ks)[cidx];
-        } else {
-          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(kk.x), "=r"(kk.y), "=r"(kk.z), "=r"(kk.w)
-                       : "r"(kt + (uint32_t)lane * 256u + (uint32_t)cidx * 16u));
-        }
-        const uint4 x0 = q0p[cidx], x1 = q1p[cidx];
-        a0[0] = fma_h2(x0.x, kk.x, a0[0]);
-        a0[1] = fma_h2(x0.y, kk.y, a0[1]);
-        a0[2] = fma_h2(x0.z, kk.z, a0[2]);
-        a0[3] = fma_h2(x0.w, kk.w, a0[3]);
-        a1[0] = fma_h2(x1.x, kk.x, a1[0]);
-        a1[1] = fma_h2(x1.y, kk.y, a1[1]);
-        a1[2] = fma_h2(x1.z, kk.z, a1[2]);
-        a1[3] = fma_h2(x1.w, kk.w, a1[3]);
+  for (int p = 0; !wk.done(sm); ++p, wk.next()) {
+    const BaPiece pc = wk.get(sm);
+    const int sl = p % kBaQSlots, ws = p & 1;
+    const bool qok = mbar_wait_own(&sm.qready[sl], (p / kBaQSlots) & 1, a.err,
+                                   kErrTimeoutFull | (4 << 4) | ((a.tag & 0xff) << 8), kSpinCycles);
+    if (p == 0) ktrace_release(a.trace);
+    if (!qok) break;
+    const int64_t pos = sm.pos[pc.b];
+    const uint4* q0p = reinterpret_cast<const uint4*>(sm.q[sl][0]);
+    const uint4* q1p = reinterpret_cast<const uint4*>(sm.q[sl][1]);
+    const uint4* knp = reinterpret_cast<const uint4*>(sm.kn[sl]);
+    const uint2 vnew = *reinterpret_cast<const uint2*>(&sm.vn[sl][4 * lane]);
+    float m[2] = {-__int_as_float(0x7f800000), -__int_as_float(0x7f800000)};
+    float l[2] = {0.0f, 0.0f};
+    float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    // chunks i of the share go to warp i % 4 (the full barriers' ownership)
+    const int ia = pc.u0 - lo, ib = pc.u1 - lo;
+    bool ok = true;
+    for (int i = ia + ((warp - ia) % kBaWarps + kBaWarps) % kBaWarps; i < ib; i += kBaWarps) {
+      const int st = i % kBaStages;
+      if (!mbar_wait_own(&sm.full[i % kBaFullBars], (i / kBaFullBars) & 1, a.err,
+                         kErrTimeoutFull | (5 << 4) | ((a.tag & 0xff) << 8), kSpinCycles)) {
+        ok = false;
+        break;
       }
-      s[0] = __fmul_rn(__fadd_rn(__fadd_rn(a0[0], a0[1]), __fadd_rn(a0[2], a0[3])), kAttnScale);
-      s[1] = __fmul_rn(__fadd_rn(__fadd_rn(a1[0], a1[1]), __fadd_rn(a1[2], a1[3])), kAttnScale);
+      const int64_t t0 = (int64_t)(lo + i - pc.s0) * kAttChunk;
+      const int tp = pos < t0 + kAttChunk ? (int)(pos - t0) : -1;  // the new key in this chunk
+      const int nvalid = (pos + 1 - t0) < kAttChunk ? (int)(pos + 1 - t0) : kAttChunk;
+      const uint32_t kt = base + st * 2 * kBaTileBytes, vt = kt + kBaTileBytes;
+      // q.k, lane = key
+      float s[2] = {-__int_as_float(0x7f800000), -__int_as_float(0x7f800000)};
+      if (lane < nvalid) {
+        // four independent accumulation chains per head (16 FMAs deep, not 128)
+        float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < kHD / 8; ++j) {
+          const int cidx = (j + lane) & 15;
+          uint4 kk;
+          if (lane == tp) {
+            kk = knp[cidx];
+          } else {
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(kk.x), "=r"(kk.y), "=r"(kk.z), "=r"(kk.w)
+                         : "r"(kt + (uint32_t)lane * 256u + (uint32_t)cidx * 16u));
+          }
+          const uint4 x0 = q0p[cidx], x1 = q1p[cidx];
+          a0[0] = fma_h2(x0.x, kk.x, a0[0]);
+          a0[1] = fma_h2(x0.y, kk.y, a0[1]);
+          a0[2] = fma_h2(x0.z, kk.z, a0[2]);
+          a0[3] = fma_h2(x0.w, kk.w, a0[3]);
+          a1[0] = fma_h2(x1.x, kk.x, a1[0]);
+          a1[1] = fma_h2(x1.y, kk.y, a1[1]);
+          a1[2] = fma_h2(x1.z, kk.z, a1[2]);
+          a1[3] = fma_h2(x1.w, kk.w, a1[3]);
+        }
+        s[0] = __fmul_rn(__fadd_rn(__fadd_rn(a0[0], a0[1]), __fadd_rn(a0[2], a0[3])), kAttnScale);
+        s[1] = __fmul_rn(__fadd_rn(__fadd_rn(a1[0], a1[1]), __fadd_rn(a1[2], a1[3])), kAttnScale);
+      }
+      float pr[2], scale[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const float cm = warp_max(s[hh]);
+        const float mn = fmaxf(m[hh], cm);
+        scale[hh] = q3_expf(__fsub_rn(m[hh], mn));
+        pr[hh] = lane < nvalid ? q3_expf(__fsub_rn(s[hh], mn)) : 0.0f;
+        l[hh] = __fmaf_rn(l[hh], scale[hh], warp_sum(pr[hh]));
+        m[hh] = mn;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) o[hh][d] = __fmul_rn(o[hh][d], scale[hh]);
+      }
+      // p.v, lane = head dims 4*lane .. 4*lane+3; a full chunk without the new
+      // key (the common case) runs fully unrolled so its shuffles and loads overlap
+      auto pv_step = [&](int tt, uint2 vv) {
+        const float p0 = __shfl_sync(0xffffffffu, pr[0], tt);
+        const float p1 = __shfl_sync(0xffffffffu, pr[1], tt);
+        const float v0 = h2f((uint16_t)(vv.x & 0xffffu)), v1 = h2f((uint16_t)(vv.x >> 16));
+        const float v2 = h2f((uint16_t)(vv.y & 0xffffu)), v3 = h2f((uint16_t)(vv.y >> 16));
+        o[0][0] = __fmaf_rn(p0, v0, o[0][0]);
+        o[0][1] = __fmaf_rn(p0, v1, o[0][1]);
+        o[0][2] = __fmaf_rn(p0, v2, o[0][2]);
+        o[0][3] = __fmaf_rn(p0, v3, o[0][3]);
+        o[1][0] = __fmaf_rn(p1, v0, o[1][0]);
+        o[1][1] = __fmaf_rn(p1, v1, o[1][1]);
+        o[1][2] = __fmaf_rn(p1, v2, o[1][2]);
+        o[1][3] = __fmaf_rn(p1, v3, o[1][3]);
+      };
+      auto ld_v = [&](int tt) {
+        uint2 vv;
+        asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];"
+                     : "=r"(vv.x), "=r"(vv.y)
+                     : "r"(vt + (uint32_t)tt * 256u + (uint32_t)lane * 8u));
+        return vv;
+      };
+      if (nvalid == kAttChunk && tp < 0) {
+#pragma unroll
+        for (int tt = 0; tt < kAttChunk; ++tt) pv_step(tt, ld_v(tt));
+      } else {
+        for (int tt = 0; tt < nvalid; ++tt) pv_step(tt, tt == tp ? vnew : ld_v(tt));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[st]);  // the stage may be refilled
     }
-    float p[2], scale[2];
+    if (!ok) break;
+    // ---- this warp's state of the piece, into state slot p % 2
+    if (p >= 2 && !mbar_wait_own(&sm.wfree[ws], ((p >> 1) - 1) & 1, a.err,
+                                 kErrTimeoutEmpty | (6 << 4) | ((a.tag & 0xff) << 8), kSpinCycles))
+      break;
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
-      const float cm = warp_max(s[hh]);
-      const float mn = fmaxf(m[hh], cm);
-      scale[hh] = q3_expf(__fsub_rn(m[hh], mn));
-      p[hh] = lane < nvalid ? q3_expf(__fsub_rn(s[hh], mn)) : 0.0f;
-      l[hh] = __fmaf_rn(l[hh], scale[hh], warp_sum(p[hh]));
-      m[hh] = mn;
-#pragma unroll
-      for (int d = 0; d < 4; ++d) o[hh][d] = __fmul_rn(o[hh][d], scale[hh]);
+      if (lane == 0) {
+        sm.wm[ws][warp][hh] = m[hh];
+        sm.wl[ws][warp][hh] = l[hh];
+      }
+      *reinterpret_cast<float4*>(&sm.wo[ws][warp][hh][4 * lane]) =
+          make_float4(o[hh][0], o[hh][1], o[hh][2], o[hh][3]);
     }
-    // p.v, lane = head dims 4*lane .. 4*lane+3; a full chunk without the new
-    // key (the common case) runs fully unrolled so its shuffles and loads overlap
-    auto pv_step = [&](int tt, uint2 vv) {
-      const float p0 = __shfl_sync(0xffffffffu, p[0], tt);
-      const float p1 = __shfl_sync(0xffffffffu, p[1], tt);
-      const float v0 = h2f((uint16_t)(vv.x & 0xffffu)), v1 = h2f((uint16_t)(vv.x >> 16));
-      const float v2 = h2f((uint16_t)(vv.y & 0xffffu)), v3 = h2f((uint16_t)(vv.y >> 16));
-      o[0][0] = __fmaf_rn(p0, v0, o[0][0]);
-      o[0][1] = __fmaf_rn(p0, v1, o[0][1]);
-      o[0][2] = __fmaf_rn(p0, v2, o[0][2]);
-      o[0][3] = __fmaf_rn(p0, v3, o[0][3]);
-      o[1][0] = __fmaf_rn(p1, v0, o[1][0]);
-      o[1][1] = __fmaf_rn(p1, v1, o[1][1]);
-      o[1][2] = __fmaf_rn(p1, v2, o[1][2]);
-      o[1][3] = __fmaf_rn(p1, v3, o[1][3]);
-    };
-    auto ld_v = [&](int tt) {
-      uint2 vv;
-      asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];"
-                   : "=r"(vv.x), "=r"(vv.y)
-                   : "r"(vt + (uint32_t)tt * 256u + (uint32_t)lane * 8u));
-      return vv;
-    };
-    if (nvalid == kAttChunk && tp < 0) {
-#pragma unroll
-      for (int tt = 0; tt < kAttChunk; ++tt) pv_step(tt, ld_v(tt));
-    } else {
-      for (int tt = 0; tt < nvalid; ++tt) pv_step(tt, tt == tp ? vnew : ld_v(tt));
-    }
+    __threadfence_block();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[st]);  // the stage may be refilled
-  }
-  // the warps' states, merged in warp order by warps 0 (q head 2h) and 1 (2h+1)
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(&sm.pcnt[ws], 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != kBaWarps - 1) continue;
+    // ---- the last warp of the piece merges the 4 states in warp order
+    __threadfence_block();
+    float mm[2], ll[2], oo[2][4];
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    if (lane == 0) {
-      sm.wm[warp][hh] = m[hh];
-      sm.wl[warp][hh] = l[hh];
-    }
-    *reinterpret_cast<float4*>(&sm.wo[warp][hh][4 * lane]) =
-        make_float4(o[hh][0], o[hh][1], o[hh][2], o[hh][3]);
-  }
-  battn_named_sync();
-  if (warp >= 2) return;
-  const int hh = warp;
-  float mm = sm.wm[0][hh], ll = sm.wl[0][hh], oo[4];
-  {
-    const float4 t4 = *reinterpret_cast<const float4*>(&sm.wo[0][hh][4 * lane]);
-    oo[0] = t4.x, oo[1] = t4.y, oo[2] = t4.z, oo[3] = t4.w;
-  }
-  for (int w = 1; w < kBaWarps; ++w) {
-    if (sm.wl[w][hh] == 0.0f) continue;  // a warp without chunks
-    const float4 t4 = *reinterpret_cast<const float4*>(&sm.wo[w][hh][4 * lane]);
-    const float ob[4] = {t4.x, t4.y, t4.z, t4.w};
-    att_merge(mm, ll, oo, sm.wm[w][hh], sm.wl[w][hh], ob);
-  }
-  if (nsegs > 1) {
-    AttnPartial* gp = a.part + (((int64_t)b * kNKV + h) * a.max_segs + seg) * 2 + hh;
-    if (lane == 0) {
-      gp->m = mm;
-      gp->l = ll;
-    }
-    *reinterpret_cast<float4*>(&gp->o[4 * lane]) = make_float4(oo[0], oo[1], oo[2], oo[3]);
-    asm volatile("bar.sync 2, 64;" ::: "memory");  // warps 0 and 1
-    if (threadIdx.x == 0) {
-      __threadfence();
-      const unsigned prev = atomicAdd(a.counters + b * kNKV + h, 1u);
-      sm.last = prev == (unsigned)(nsegs - 1);
-      if (sm.last) a.counters[b * kNKV + h] = 0u;
-      __threadfence();
-    }
-    asm volatile("bar.sync 2, 64;" ::: "memory");
-    if (!sm.last) {
-      ktrace_end(a.trace);
-      return;
-    }
-    const AttnPartial* pb = a.part + (((int64_t)b * kNKV + h) * a.max_segs) * 2 + hh;
-    mm = __ldcg(&pb->m);
-    ll = __ldcg(&pb->l);
-    {
-      const float4 t4 = __ldcg(reinterpret_cast<const float4*>(&pb->o[4 * lane]));
-      oo[0] = t4.x, oo[1] = t4.y, oo[2] = t4.z, oo[3] = t4.w;
-    }
-    for (int k0 = 1; k0 < nsegs; k0 += 8) {
-      float4 ob4[8];
-      float mb[8], lb[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (k0 + u < nsegs) {
-          const AttnPartial* q = pb + (int64_t)(k0 + u) * 2;
-          ob4[u] = __ldcg(reinterpret_cast<const float4*>(&q->o[4 * lane]));
-          mb[u] = __ldcg(&q->m);
-          lb[u] = __ldcg(&q->l);
-        }
+    for (int hh = 0; hh < 2; ++hh) {
+      mm[hh] = -__int_as_float(0x7f800000);
+      ll[hh] = 0.0f;
+      oo[hh][0] = oo[hh][1] = oo[hh][2] = oo[hh][3] = 0.0f;
+      for (int w = 0; w < kBaWarps; ++w) {
+        const float4 t4 = *reinterpret_cast<const float4*>(&sm.wo[ws][w][hh][4 * lane]);
+        const float ob[4] = {t4.x, t4.y, t4.z, t4.w};
+        battn_merge_state(mm[hh], ll[hh], oo[hh], sm.wm[ws][w][hh], sm.wl[ws][w][hh], ob);
       }
+    }
+    if (lane == 0) sm.pcnt[ws] = 0u;
+    __syncwarp();
+    mbar_arrive(&sm.wfree[ws]);   // the state slot may be rewritten
+    mbar_arrive(&sm.qfree[sl]);   // every warp is past this piece's q
+    const int bh = pc.b * kNKV + pc.h;
+    if (pc.s0 < lo || pc.s1 > hi) {
+      // (b, h) spans CTAs: publish this CTA's partial, the last one merges
+      const int slot = pc.s0 > lo ? 1 : 0;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (k0 + u < nsegs) {
-          const float ob[4] = {ob4[u].x, ob4[u].y, ob4[u].z, ob4[u].w};
-          att_merge(mm, ll, oo, mb[u], lb[u], ob);
+      for (int hh = 0; hh < 2; ++hh) {
+        AttnPartial* gp = a.part + ((int64_t)g * 2 + slot) * 2 + hh;
+        if (lane == 0) {
+          gp->m = mm[hh];
+          gp->l = ll[hh];
+        }
+        *reinterpret_cast<float4*>(&gp->o[4 * lane]) =
+            make_float4(oo[hh][0], oo[hh][1], oo[hh][2], oo[hh][3]);
+      }
+      __threadfence();
+      __syncwarp();
+      const int g1 = battn_cta_of(pc.s0, T, G), g2 = battn_cta_of(pc.s1 - 1, T, G);
+      unsigned last = 0;
+      if (lane == 0) {
+        const unsigned prevc = atomicAdd(a.counters + bh, 1u);
+        last = prevc == (unsigned)(g2 - g1);
+        if (last) a.counters[bh] = 0u;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      __threadfence();
+      const int lo1 = (int)(g1 * T / G);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        mm[hh] = -__int_as_float(0x7f800000);
+        ll[hh] = 0.0f;
+        oo[hh][0] = oo[hh][1] = oo[hh][2] = oo[hh][3] = 0.0f;
+      }
+      for (int gg = g1; gg <= g2; ++gg) {
+        const int sg = (gg == g1 && pc.s0 > lo1) ? 1 : 0;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const AttnPartial* q = a.part + ((int64_t)gg * 2 + sg) * 2 + hh;
+          const float4 t4 = __ldcg(reinterpret_cast<const float4*>(&q->o[4 * lane]));
+          const float ob[4] = {t4.x, t4.y, t4.z, t4.w};
+          battn_merge_state(mm[hh], ll[hh], oo[hh], __ldcg(&q->m), __ldcg(&q->l), ob);
         }
       }
     }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      uint16_t* outp = a.out + (int64_t)pc.b * 2048 + (2 * pc.h + hh) * kHD + 4 * lane;
+      uint2 pk;
+      pk.x = (uint32_t)f2h(__fdiv_rn(oo[hh][0], ll[hh])) |
+             ((uint32_t)f2h(__fdiv_rn(oo[hh][1], ll[hh])) << 16);
+      pk.y = (uint32_t)f2h(__fdiv_rn(oo[hh][2], ll[hh])) |
+             ((uint32_t)f2h(__fdiv_rn(oo[hh][3], ll[hh])) << 16);
+      *reinterpret_cast<uint2*>(outp) = pk;
+    }
   }
-  uint16_t* outp = a.out + (int64_t)b * 2048 + (2 * h + hh) * kHD + 4 * lane;
-  uint2 pk;
-  pk.x = (uint32_t)f2h(__fdiv_rn(oo[0], ll)) | ((uint32_t)f2h(__fdiv_rn(oo[1], ll)) << 16);
-  pk.y = (uint32_t)f2h(__fdiv_rn(oo[2], ll)) | ((uint32_t)f2h(__fdiv_rn(oo[3], ll)) << 16);
-  *reinterpret_cast<uint2*>(outp) = pk;
   ktrace_end(a.trace);
 }
 
