@@ -299,6 +299,23 @@ int q3_generate_end(q3_model* m, int64_t* out_tokens, int64_t* n_out);
 int q3_model_profile_steps(q3_model* m, int64_t steps, float* times_us, int32_t* kinds,
                            int64_t cap);
 
+/* Prompt ingestion.  STEPS (default): every prompt token but the last runs
+ * one decode step (the reference's @prefill_all route,
+ * model/qwen3_full.mlir:1541-1570), so ingestion gives the engine's bits.
+ * BATCHED: those positions run as rows of the batched decoder's tensor-core
+ * kernels, up to 64 positions per pass (QKV, the new K/V rows, causal
+ * attention, O, FFN), writing the same K/V cache rows to within the batched
+ * path's tolerance; the last prompt token and generation then run on the
+ * model's engine.  Applies to q3_generate_begin, q3_run and q3_chat_turn. */
+#define Q3_PREFILL_STEPS 0
+#define Q3_PREFILL_BATCHED 1
+int q3_model_set_prefill(q3_model* m, int mode);
+int q3_model_prefill_mode(q3_model* m, int* mode);
+/* Batched prefill of positions pos0 .. pos0+n-1 with tokens[0..n): stores
+ * the tokens and writes the K/V rows of every layer (no vocab head).
+ * Decoding continues with q3_decode at pos0 + n. */
+int q3_model_prefill(q3_model* m, const int64_t* tokens, int64_t pos0, int64_t n);
+
 /* Engines.  FUSED (default where available): two cluster kernels per layer
  * (attention block; feed-forward block) with the O and down projections split
  * along K into 8 slices whose f32 partials are summed in slice order -- 57

@@ -1064,7 +1064,13 @@ struct q3_model {
   int trace_step = -1;
   bool chat_ready = false;
   int64_t chat_pos = 0, chat_max = 0;
+  int prefill_mode = Q3_PREFILL_STEPS;  // how prompts are ingested
+  q3_batch* pf = nullptr;               // prefill view (batched kernels on this model's cache)
 };
+
+// Prompt prefill through the batched kernels (defined with the batched decoder).
+static int model_prefill(q3_model* m, int64_t pos0, int64_t n);
+static void prefill_destroy(q3_batch* pf);
 
 // Optional instrumentation while capturing: after every kernel an event is
 // recorded and the kernel's kind appended (profiling graph only).
@@ -1338,6 +1344,7 @@ static int capture(q3_model* m, bool ingest, cudaGraphExec_t* out, int* launches
 
 static void model_free(q3_model* m) {
   if (!m) return;
+  if (m->pf) prefill_destroy(m->pf);
   if (m->g_ingest) cudaGraphExecDestroy(m->g_ingest);
   if (m->g_gen) cudaGraphExecDestroy(m->g_gen);
   if (m->g_prof) cudaGraphExecDestroy(m->g_prof);
@@ -1520,6 +1527,19 @@ extern "C" int q3_model_create(const q3_weights* w, int64_t S, void* stream, q3_
   return Q3_OK;
 }
 
+extern "C" int q3_model_set_prefill(q3_model* m, int mode) {
+  Q3_REQUIRE(m, "null model");
+  Q3_REQUIRE(mode == Q3_PREFILL_STEPS || mode == Q3_PREFILL_BATCHED, "unknown prefill mode %d", mode);
+  m->prefill_mode = mode;
+  return Q3_OK;
+}
+
+extern "C" int q3_model_prefill_mode(q3_model* m, int* mode) {
+  Q3_REQUIRE(m && mode, "null pointer");
+  *mode = m->prefill_mode;
+  return Q3_OK;
+}
+
 extern "C" int q3_model_set_engine(q3_model* m, int engine) {
   Q3_REQUIRE(m, "null model");
   Q3_REQUIRE(engine == Q3_ENGINE_GRAPH || engine == Q3_ENGINE_PERSISTENT ||
@@ -1589,14 +1609,16 @@ extern "C" int q3_model_device_error(q3_model* m, int* code) {
 }
 
 // Upload tokens at positions [pos0, pos0+n) and a fresh sequence state.
+// Tokens toks[0..n) at positions pos0.. and the step state; the first step
+// feeds position state_pos (pos0, or where a prefill stopped).
 static int seq_begin(q3_model* m, const int64_t* toks, int64_t pos0, int64_t n, int64_t n_prompt,
-                     int64_t max_gen, int64_t eos) {
+                     int64_t max_gen, int64_t eos, int64_t state_pos = -1) {
   memcpy(m->h_tokens, toks, (size_t)n * sizeof(int64_t));
   Q3_CUDA(cudaMemcpyAsync(m->tokens + pos0, m->h_tokens, (size_t)n * sizeof(int64_t),
                           cudaMemcpyHostToDevice, m->stream));
   SeqState s;
   memset(&s, 0, sizeof(s));
-  s.pos = pos0;
+  s.pos = state_pos >= 0 ? state_pos : pos0;
   s.n_prompt = n_prompt;
   s.max_gen = max_gen;
   s.eos = eos;
@@ -1696,13 +1718,20 @@ extern "C" int q3_generate_begin(q3_model* m, const int64_t* prompt, int64_t n_p
   for (int64_t i = 0; i < n_prompt; ++i)
     Q3_REQUIRE(prompt[i] >= 0 && prompt[i] < kVocab, "prompt token %lld out of range",
                (long long)prompt[i]);
-  int rc = seq_begin(m, prompt, 0, n_prompt, n_prompt, max_gen, eos);
+  // all but the last prompt token are ingested (no vocab head); the last one
+  // runs the vocab head.  Batched prefill writes the ingested positions' K/V
+  // rows in passes of up to 64 positions instead of one decode step each.
+  const bool pf = m->prefill_mode == Q3_PREFILL_BATCHED && n_prompt > 1;
+  int rc = seq_begin(m, prompt, 0, n_prompt, n_prompt, max_gen, eos, pf ? n_prompt - 1 : 0);
   if (rc) return rc;
   m->gen_n_prompt = n_prompt;
   m->gen_pos0 = 0;
   m->gen_max = max_gen;
   m->gen_active = true;
-  // ingest all but the last prompt token; the last one runs the vocab head
+  if (pf) {
+    if ((rc = model_prefill(m, 0, n_prompt - 1))) return rc;
+    return launch_graphs(m, 0, 1);
+  }
   return launch_graphs(m, n_prompt - 1, 1);
 }
 
@@ -1788,9 +1817,11 @@ extern "C" int q3_chat_turn(q3_model* m, const int64_t* toks, int64_t n, int64_t
   for (int64_t i = 0; i < n; ++i)
     Q3_REQUIRE(toks[i] >= 0 && toks[i] < kVocab, "token out of range");
   const int64_t p0 = m->chat_pos;
-  int rc = seq_begin(m, toks, p0, n, p0 + n, max_gen, eos);
+  const bool pf = m->prefill_mode == Q3_PREFILL_BATCHED && n > 1;
+  int rc = seq_begin(m, toks, p0, n, p0 + n, max_gen, eos, pf ? p0 + n - 1 : p0);
   if (rc) return rc;
-  rc = launch_graphs(m, n - 1, 1 + max_gen);
+  if (pf && (rc = model_prefill(m, p0, n - 1))) return rc;
+  rc = launch_graphs(m, pf ? 0 : n - 1, 1 + max_gen);
   if (rc) return rc;
   int64_t got = 0;
   rc = read_generated(m, p0 + n + 1, max_gen, out, &got);

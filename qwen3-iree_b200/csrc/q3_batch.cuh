@@ -428,8 +428,9 @@ struct BNormArgs {
   uint16_t* xn;          // [npad][K]
   int K;
   int B;
-  const int64_t* tokens; // [B][tok_stride]
-  int64_t tok_stride;
+  const int64_t* tokens; // row b's token at position p: tokens[b * tok_stride + p]
+  int64_t tok_stride;    // 0 when every row reads one sequence's tokens
+  int64_t tok_len;       // positions per row
   const BatchSeq* seq;
   const uint16_t* embd;
   int* err;
@@ -449,7 +450,7 @@ __global__ void __launch_bounds__(256) k_bnorm(const __grid_constant__ BNormArgs
   if (a.tokens != nullptr) {
     const int64_t pos = a.seq[b].pos;
     int64_t tok = 0;
-    if (pos < 0 || pos >= a.tok_stride) {
+    if (pos < 0 || pos >= a.tok_len) {
       if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
     } else {
       tok = a.tokens[(int64_t)b * a.tok_stride + pos];

@@ -76,8 +76,11 @@ struct BAttnArgs {
   uint16_t* kc;            // caches (for the new row)
   uint16_t* vc;
   int64_t S;               // slots per layer
+  int64_t seq_rows;        // cache rows between sequences (28 * S; 0: rows share one cache)
   int layer;
   int B;                   // sequences, <= 64
+  int prefill;             // rows hold consecutive positions of one sequence whose new K/V
+                           // rows an earlier kernel wrote: no pre-wait stream, no new row
   const int64_t* pos;      // pos[b * pos_stride]
   int pos_stride;
   uint16_t* out;           // [npad][2048]
@@ -240,6 +243,7 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
     if (lane == 0) {
       prefetch_tmap(&a.kmap);
       prefetch_tmap(&a.vmap);
+      if (a.prefill) pdl_wait();  // the rows of this pass come from the previous kernel
       const int n = hi - lo;
       int b = b_first, h = (lo - sm.pre[b]) / sm.nch[b];
       int c = lo - sm.pre[b] - h * sm.nch[b];
@@ -252,7 +256,7 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
           break;
         uint64_t* const fb = &sm.full[i % kBaFullBars];
         mbar_expect_tx(fb, 2 * kBaTileBytes);
-        const int y = (int)(((int64_t)b * kLayers + a.layer) * a.S + (int64_t)c * kAttChunk);
+        const int y = (int)((int64_t)b * a.seq_rows + (int64_t)a.layer * a.S + (int64_t)c * kAttChunk);
         tma_load_2d(gbase + st * 2 * kBaTileBytes, &a.kmap, h * kHD, y, fb);
         tma_load_2d(gbase + st * 2 * kBaTileBytes + kBaTileBytes, &a.vmap, h * kHD, y, fb);
         issued = i + 1;
@@ -292,7 +296,8 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
           !mbar_wait_own(&sm.qfree[sl], ((p / kBaQSlots) - 1) & 1, a.err,
                          kErrTimeoutEmpty | (3 << 4) | ((a.tag & 0xff) << 8), kSpinCycles))
         break;
-      const bool holds_pos = pc.s1 <= hi;  // this piece holds the (b, h)'s last chunk
+      // this piece holds the (b, h)'s last chunk: it stages and writes the new row
+      const bool holds_pos = pc.s1 <= hi && !a.prefill;
       const int64_t pos = sm.pos[pc.b];
       const float* ct = a.rope_cos + pos * 64;
       const float* sn = a.rope_sin + pos * 64;
@@ -319,7 +324,7 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
         *reinterpret_cast<uint2*>(&sm.vn[sl][4 * lane]) = v;
         __syncwarp();
         const int64_t off =
-            (((int64_t)pc.b * kLayers + a.layer) * a.S + pos) * (kNKV * kHD) + pc.h * kHD;
+            ((int64_t)pc.b * a.seq_rows + (int64_t)a.layer * a.S + pos) * (kNKV * kHD) + pc.h * kHD;
         *reinterpret_cast<uint2*>(a.kc + off + 4 * lane) =
             *reinterpret_cast<const uint2*>(&sm.kn[sl][4 * lane]);
         *reinterpret_cast<uint2*>(a.vc + off + 4 * lane) = v;
@@ -356,7 +361,8 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
         break;
       }
       const int64_t t0 = (int64_t)(lo + i - pc.s0) * kAttChunk;
-      const int tp = pos < t0 + kAttChunk ? (int)(pos - t0) : -1;  // the new key in this chunk
+      // the new key in this chunk (prefill: already in the cache)
+      const int tp = (pos < t0 + kAttChunk && !a.prefill) ? (int)(pos - t0) : -1;
       const int nvalid = (pos + 1 - t0) < kAttChunk ? (int)(pos + 1 - t0) : kAttChunk;
       const uint32_t kt = base + st * 2 * kBaTileBytes, vt = kt + kBaTileBytes;
       // q.k, lane = key
@@ -525,6 +531,52 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
       *reinterpret_cast<uint2*>(outp) = pk;
     }
   }
+  ktrace_end(a.trace);
+}
+
+// The new K (QK-RMSNorm + RoPE) and V rows of B rows of qkv at their
+// positions, one warp per kv head (prefill passes, before k_battn reads them).
+struct BKvArgs {
+  const uint16_t* qkv;     // [B][4096]
+  const uint16_t* k_norm;  // gamma [128]
+  const float* rope_cos;   // [rope_rows, 64]
+  const float* rope_sin;
+  int64_t rope_rows;
+  uint16_t* kc;
+  uint16_t* vc;
+  int64_t S;
+  int64_t seq_rows;        // cache rows between rows' sequences (0: one sequence)
+  int layer;
+  int B;
+  const int64_t* pos;      // pos[b * pos_stride]
+  int pos_stride;
+  int* err;
+  unsigned long long* trace;
+};
+
+__global__ void __launch_bounds__(32 * kNKV) k_bkv_write(const __grid_constant__ BKvArgs a) {
+  __shared__ __align__(16) uint16_t kn[kNKV][kHD];
+  const int b = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  ktrace_start(a.trace);
+  pdl_launch_dependents();
+  pdl_wait();  // qkv comes from the previous kernel
+  ktrace_release(a.trace);
+  const int64_t pos = a.pos[(int64_t)b * a.pos_stride];
+  if (pos < 0 || pos >= a.S || pos >= a.rope_rows) {
+    if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
+    return;
+  }
+  const float* ct = a.rope_cos + pos * 64;
+  const float* sn = a.rope_sin + pos * 64;
+  const uint16_t* qkv = a.qkv + (int64_t)b * 4096;
+  head_norm_rope(qkv + 2048 + h * kHD, a.k_norm, ct[lane], sn[lane], ct[lane + 32], sn[lane + 32],
+                 lane, kn[h]);
+  __syncwarp();
+  const int64_t off =
+      ((int64_t)b * a.seq_rows + (int64_t)a.layer * a.S + pos) * (kNKV * kHD) + h * kHD + 4 * lane;
+  *reinterpret_cast<uint2*>(a.kc + off) = *reinterpret_cast<const uint2*>(&kn[h][4 * lane]);
+  *reinterpret_cast<uint2*>(a.vc + off) =
+      __ldcg(reinterpret_cast<const uint2*>(qkv + 3072 + h * kHD) + lane);
   ktrace_end(a.trace);
 }
 

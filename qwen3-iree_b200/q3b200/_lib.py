@@ -101,6 +101,9 @@ SIGNATURES = {
     "q3_model_profile_steps": [P, I64, P, P, I64],
     "q3_model_set_engine": [P, I],
     "q3_model_engine": [P, ctypes.POINTER(ctypes.c_int)],
+    "q3_model_set_prefill": [P, I],
+    "q3_model_prefill_mode": [P, ctypes.POINTER(ctypes.c_int)],
+    "q3_model_prefill": [P, P, I64, I64],
     "q3_model_kernel_launches": [P, PI64],
     "q3_model_trace_steps": [P, I64, I64, P, I64, ctypes.POINTER(ctypes.c_int),
                              ctypes.POINTER(ctypes.c_int)],

@@ -48,7 +48,7 @@ class Qwen3Decoder:
     """One decoder (KV cache, activations, graphs) on the current device."""
 
     def __init__(self, weights: DeviceWeights | dict, max_seq_len: int = 1024, stream=None,
-                 engine: str | None = None):
+                 engine: str | None = None, prefill: str | None = None):
         self.weights = weights if isinstance(weights, DeviceWeights) else DeviceWeights(weights)
         self.max_seq_len = int(max_seq_len)
         h = ctypes.c_void_p()
@@ -58,6 +58,8 @@ class Qwen3Decoder:
         self.stream = lib().q3_model_stream(self.handle)
         if engine is not None:
             self.set_engine(engine)
+        if prefill is not None:
+            self.set_prefill(prefill)
 
     # -- @run (model/qwen3_full.mlir:2113-2167)
     def run(self, tokens, max_tokens: int, eos: int) -> tuple[np.ndarray, int]:
@@ -122,6 +124,25 @@ class Qwen3Decoder:
 
     def set_engine(self, name: str) -> None:
         call("q3_model_set_engine", self.handle, self.ENGINES[name])
+
+    PREFILL = {"steps": 0, "batched": 1}
+
+    def set_prefill(self, name: str) -> None:
+        """How prompts are ingested: "steps" (one decode step per token, the
+        reference's @prefill_all route) or "batched" (tensor-core passes of up
+        to 64 positions)."""
+        call("q3_model_set_prefill", self.handle, self.PREFILL[name])
+
+    @property
+    def prefill_mode(self) -> str:
+        e = ctypes.c_int(-1)
+        call("q3_model_prefill_mode", self.handle, ctypes.byref(e))
+        return {v: k for k, v in self.PREFILL.items()}[e.value]
+
+    def prefill(self, tokens, pos0: int = 0) -> None:
+        """Batched prefill: K/V rows of positions pos0 .. pos0+len(tokens)-1."""
+        t = np.ascontiguousarray(tokens, dtype=np.int64)
+        call("q3_model_prefill", self.handle, t.ctypes.data, int(pos0), t.size)
 
     @property
     def engine(self) -> str:
