@@ -446,6 +446,15 @@ int q3_batch_read_argmax(q3_batch* m, int64_t* out);
 int q3_batch_profile_steps(q3_batch* m, int64_t steps, float* times_us, int32_t* kinds,
                            int64_t cap, int64_t* n_kernels);
 int q3_batch_kernel_launches(q3_batch* m, int64_t* n);
+/* Per-CTA phase stamps of the batched projections and attention during the
+ * last of `steps` steps: out[launch][512 CTAs][8] global-timer ns (0 where a
+ * CTA or stamp did not run), kinds[launch] = Q3_KIND_*; cap >= launches *
+ * 4096.  Projections stamp start, release, weights landed, activations
+ * landed, accumulators complete, split partials stored, shares arrived, end;
+ * attention stamps start, work list ready, release, first q staged, done.
+ * For latency analysis. */
+int q3_batch_trace_phases(q3_batch* m, int64_t steps, long long* out, int32_t* kinds, int64_t cap,
+                          int64_t* n_launches);
 /* Kernel timeline of `steps` batched steps, as q3_model_trace_kernels. */
 int q3_batch_trace_kernels(q3_batch* m, int64_t steps, long long* out, int32_t* kinds,
                            int64_t cap, int64_t* n_kernels);

@@ -1082,6 +1082,8 @@ struct StepProbe {
   std::vector<int32_t>* tkinds = nullptr;
   long long* phase = nullptr;            // fused kernels' per-CTA phase stamps, per launch
   int* pslot = nullptr;
+  long long* bphase = nullptr;           // batched kernels' per-CTA phase stamps, per launch
+  std::vector<int32_t>* bkinds = nullptr;
 };
 
 // The next fused launch's phase-stamp block while capturing a phase-traced graph.

@@ -52,6 +52,17 @@ constexpr long long kBatchSpinCycles = kSpinCycles;
 __device__ __forceinline__ int bwait_code(int code, int site, int tag) {
   return code | (site << 4) | ((tag & 0xff) << 8) | (((int)blockIdx.x & 0xfff) << 16);
 }
+// Per-CTA phase stamps (global timer, ns) of the batched kernels' traced
+// launches: p[cta * kBPhases + k], written by one chosen thread.
+constexpr int kBPhases = 8;
+__device__ __forceinline__ void bphase(long long* p, int k, bool me) {
+  if (p != nullptr && me) {
+    long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    p[(int64_t)(blockIdx.y * gridDim.x + blockIdx.x) * kBPhases + k] = t;
+  }
+}
+
 #define Q3_BWAIT(bar, parity, code, site) \
   mbar_wait_own((bar), (parity), a.err, bwait_code((code), (site), a.tag), kBatchSpinCycles)
 
@@ -78,6 +89,7 @@ struct BGemmArgs {
   int* err;              // optional device error word (pipeline wait timed out)
   int tag;               // launch tag recorded with a timeout
   unsigned long long* trace;  // optional launch timing record
+  long long* phase;      // optional per-CTA phase stamps [CTAs][kBPhases] (ns)
 };
 
 // Weight stages (dequantised 64-wide K slices) between the dequantising warps
@@ -186,6 +198,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
   const int cbase = (int)blockIdx.y * nchunk;              // first 256-wide chunk of this CTA
   const int tile = blockIdx.x, n0 = tile * 128;
   ktrace_start(a.trace);
+  bphase(a.phase, 0, threadIdx.x == 0);  // start
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kBgMaxKc; ++i) mbar_init(&raw_full[i], 1);
@@ -238,12 +251,15 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       }
       pdl_wait();  // activations come from the previous kernel
       ktrace_release(a.trace);
+      bphase(a.phase, 1, true);  // release
       mbar_expect_tx(&x_full, (uint32_t)(nsub * NPAD * 128));
       for (int i = 0; i < nsub; ++i)
         tma_load_2d(gbase + (sX - base) + i * NPAD * 128, &a.xmap, (cbase * 4 + i) * 64, 0, &x_full);
       // the CTA may not exit before every copy has landed
       for (int c = 0; c < nchunk; ++c) Q3_BWAIT(&raw_full[c], 0, kErrTimeoutFull, 3);
+      bphase(a.phase, 2, true);  // weights landed (stamped after the release)
       Q3_BWAIT(&x_full, 0, kErrTimeoutFull, 4);
+      bphase(a.phase, 3, true);  // activations landed
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
@@ -297,6 +313,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
     // ------------------------------------------------ accumulators out of TMEM (warps 2-5)
     if (warp < 6) {
       const bool have = Q3_BWAIT(&acc_full, 0, kErrTimeoutFull, 10);
+      bphase(a.phase, 4, threadIdx.x == 64);  // accumulators complete
       tc_fence_after();
       const uint32_t lane_base = (32u * (uint32_t)(warp & 3)) << 16;
       if (have && splits == 1) {
@@ -360,6 +377,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
     // timing).  No CTA touches another's shared memory after its own wait.
     __syncwarp();
     cluster_sync_all();
+    bphase(a.phase, 5, threadIdx.x == 64);  // every split's partial stored
     const int total = 128 * NPAD, per = bgemm_red_per(total, splits);
     const int me = (int)cluster_rank();
     if (warp >= 2) {
@@ -376,6 +394,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
           }
       }
       const bool got = Q3_BWAIT(&red_bar, 0, kErrTimeoutFull, 11);
+      bphase(a.phase, 6, threadIdx.x == 64);  // this CTA's shares arrived
       pdl_wait();  // reads the residual stream / writes buffers of earlier kernels
       const int i0 = me * per;
       const int i1 = i0 + per < total ? i0 + per : total;
@@ -408,8 +427,13 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       if (!got) Q3_BWAIT(&red_bar, 0, kErrTimeoutFull, 12);  // pushes into this CTA landed
     }
   }
+  // role branches and per-lane polling leave warps diverged: reconverge each
+  // warp before the CTA barrier (bar.sync counts a warp when its first
+  // threads arrive)
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
+  bphase(a.phase, 7, threadIdx.x == 0);  // end
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TCOLS);
@@ -665,6 +689,7 @@ __global__ void __launch_bounds__(kBvThreads, 1) k_bvocab(const __grid_constant_
       }
     }
   }
+  __syncwarp();  // reconverge the role-diverged warps before the CTA barrier
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

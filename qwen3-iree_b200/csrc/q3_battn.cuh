@@ -37,6 +37,7 @@
 #include <cuda.h>
 
 #include "q3_attn.cuh"
+#include "q3_batch.cuh"
 #include "q3_common.cuh"
 #include "q3_tc.cuh"
 
@@ -89,6 +90,7 @@ struct BAttnArgs {
   int* err;
   int tag;
   unsigned long long* trace;  // optional launch timing record
+  long long* phase;           // optional per-CTA phase stamps [CTAs][kBPhases] (ns)
 };
 
 // One (b, h) piece of a CTA's share: chunks [u0, u1) of the flattened list,
@@ -179,6 +181,7 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
   uint8_t* const gbase = smem_raw + (base - smem_u32(smem_raw));
   const int B = a.B;
   ktrace_start(a.trace);
+  bphase(a.phase, 0, threadIdx.x == 0);  // start
 
   // ------------------------------------------------ the work list
   // positions were set by an earlier graph launch: readable before the wait
@@ -237,6 +240,7 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
   __syncthreads();
   pdl_launch_dependents();
   const int b_first = sm.b0;
+  bphase(a.phase, 1, threadIdx.x == 0);  // work list ready
 
   if (warp == kBaProducer) {
     // ------------------------------------------------ producer: K/V tiles
@@ -305,6 +309,7 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
       if (!waited) {
         pdl_wait();  // q, k, v come from the previous kernel
         waited = true;
+        bphase(a.phase, 2, lane == 0);  // release
       }
       const unsigned short* qkv =
           reinterpret_cast<const unsigned short*>(a.qkv) + (int64_t)pc.b * 4096;
@@ -340,7 +345,10 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
     const int sl = p % kBaQSlots, ws = p & 1;
     const bool qok = mbar_wait_own(&sm.qready[sl], (p / kBaQSlots) & 1, a.err,
                                    kErrTimeoutFull | (4 << 4) | ((a.tag & 0xff) << 8), kSpinCycles);
-    if (p == 0) ktrace_release(a.trace);
+    if (p == 0) {
+      ktrace_release(a.trace);
+      bphase(a.phase, 3, threadIdx.x == 0);  // first piece's q staged
+    }
     if (!qok) break;
     const int64_t pos = sm.pos[pc.b];
     const uint4* q0p = reinterpret_cast<const uint4*>(sm.q[sl][0]);
@@ -531,6 +539,7 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
       *reinterpret_cast<uint2*>(outp) = pk;
     }
   }
+  bphase(a.phase, 4, threadIdx.x == 0);  // warp 0 done
   ktrace_end(a.trace);
 }
 

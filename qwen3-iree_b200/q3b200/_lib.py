@@ -125,6 +125,7 @@ SIGNATURES = {
     "q3_batch_attention_workspace_bytes": [I64, I],
     "q3_batch_attention": [P, P, P, P, P, I64, P, P, I, I64, I, P, P, P, P],
     "q3_batch_profile_steps": [P, I64, P, P, I64, PI64],
+    "q3_batch_trace_phases": [P, I64, P, P, I64, PI64],
     "q3_batch_kernel_launches": [P, PI64],
     "q3_strerror": [I],
     "q3_last_error": [],

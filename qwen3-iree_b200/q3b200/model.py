@@ -286,15 +286,16 @@ class BatchDecoder:
         call("q3_batch_read_argmax", self.handle, out.ctypes.data)
         return out
 
-    def trace_phases(self, steps: int = 4) -> np.ndarray:
-        """Fused engine: [56 launches, 128 CTAs, phases] global-timer stamps (ns)
-        of the last of `steps` steps."""
-        cap = 56 * 128 * 16
-        out = np.zeros(cap, np.int64)
-        nl, c, p = ctypes.c_int64(), ctypes.c_int(), ctypes.c_int()
-        call("q3_model_trace_phases", self.handle, int(steps), out.ctypes.data, cap,
-             ctypes.byref(nl), ctypes.byref(c), ctypes.byref(p))
-        return out[:nl.value * c.value * p.value].reshape(nl.value, c.value, p.value)
+    def trace_phases(self, steps: int = 4):
+        """(stamps [launches, 512 CTAs, 8] global-timer ns, kinds [launches]) of
+        the batched projections and attention in the last of `steps` steps."""
+        nmax = 5 * 28
+        out = np.zeros(nmax * 512 * 8, np.int64)
+        kinds = np.zeros(nmax, np.int32)
+        n = ctypes.c_int64(0)
+        call("q3_batch_trace_phases", self.handle, int(steps), out.ctypes.data, kinds.ctypes.data,
+             out.size, ctypes.byref(n))
+        return out[:n.value * 512 * 8].reshape(n.value, 512, 8), kinds[:n.value].copy()
 
     def kernel_launches(self) -> int:
         n = ctypes.c_int64(0)
