@@ -90,6 +90,20 @@ struct BGemmArgs {
   int tag;               // launch tag recorded with a timeout
   unsigned long long* trace;  // optional launch timing record
   long long* phase;      // optional per-CTA phase stamps [CTAs][kBPhases] (ns)
+  // RMSNorm folded into the projections (model/qwen3_full.mlir:134-165),
+  // y = W (x / r_b * gamma) computed as (W f16(x * gamma)) / r_b.  A
+  // residual-producing launch (kBgResid, split) writes, per reducing CTA,
+  // the sum of squares of its f16 outputs of each row b,
+  // ssq_out[(tile * splits + rank) * 64 + b] (whole 128-row blocks per CTA),
+  // and the next projection's operand xg_out = f16(out * xg_gamma).  A
+  // normalising launch (its xmap over that operand) multiplies each reduced
+  // sum by 1 / r_b, r_b = sqrt(sum_p ssq_in[p * 64 + b] / K + eps) over
+  // p < ssq_parts in p order, before the epilogue.
+  float* ssq_out;
+  uint16_t* xg_out;       // [npad][ldy]
+  const uint16_t* xg_gamma;
+  const float* ssq_in;
+  int ssq_parts;
 };
 
 // Weight stages (dequantised 64-wide K slices) between the dequantising warps
@@ -98,10 +112,10 @@ __host__ __device__ constexpr int bgemm_substages(int naccum) { return naccum ==
 constexpr int kBgMaxKc = 2;       // chunks per CTA: all of its activations stay resident
 constexpr int kBgMaxSplits = 8;   // CTAs per tile = one portable cluster
 
-// Items of the split reduction per CTA: ceil(total / splits), rounded up to a
-// multiple of 4 so that every share starts on a 16-byte boundary.
+// Items of the split reduction per CTA: ceil(total / splits), rounded up to
+// whole 128-row blocks (item = b*128 + row: a CTA reduces whole rows b).
 __host__ __device__ constexpr int bgemm_red_per(int total, int splits) {
-  return ((total + splits - 1) / splits + 3) / 4 * 4;
+  return ((total + splits - 1) / splits + 127) / 128 * 128;
 }
 
 // Dynamic shared memory: weight stages (reused for the f32 partials), every
@@ -185,6 +199,10 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
   __shared__ __align__(8) uint64_t raw_full[kBgMaxKc], x_full, acc_full, red_bar;
   __shared__ __align__(8) uint64_t a_full[kBgSubStages], a_empty[kBgSubStages];
   __shared__ uint32_t tmem_base;
+  __shared__ float red_ss[64];               // per-warp sums of squares of the outputs
+  __shared__ float rs_b[kBMaxBatch];         // 1 / RMS of the rows (folded norm)
+  __shared__ float rs_g[2][kBMaxBatch];      // their partial sums of squares
+  const bool fold = a.ssq_in != nullptr;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nchunk = a.kc;
@@ -310,6 +328,26 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       }
       if (!ok) break;
     }
+    if (fold && warp >= 6) {
+      // 1 / r_b of every row, by the warps the accumulators do not need, while
+      // the MMAs run: row b's parts by 2 threads (32 loads issued together
+      // each), the two sums in order; read after the cluster barrier
+      pdl_wait();  // the parts come from the previous kernel
+      const int t = threadIdx.x - 192, b = t & 63, grp = t >> 6;
+      float v[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int q = grp * 32 + u;
+        v[u] = (b < NPAD && q < a.ssq_parts) ? __ldcg(a.ssq_in + q * 64 + b) : 0.0f;
+      }
+      float t32 = v[0];
+#pragma unroll
+      for (int u = 1; u < 32; ++u) t32 = __fadd_rn(t32, v[u]);
+      rs_g[grp][b] = t32;
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (t < kBMaxBatch)
+        rs_b[t] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(__fadd_rn(rs_g[0][t], rs_g[1][t]), (float)a.K), kEps)));
+    }
     // ------------------------------------------------ accumulators out of TMEM (warps 2-5)
     if (warp < 6) {
       const bool have = Q3_BWAIT(&acc_full, 0, kErrTimeoutFull, 10);
@@ -398,9 +436,12 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       pdl_wait();  // reads the residual stream / writes buffers of earlier kernels
       const int i0 = me * per;
       const int i1 = i0 + per < total ? i0 + per : total;
-      for (int i = i0 + t; got && i < i1; i += 32 * kBgDqWarps) {
+      const bool want_ss = MODE == kBgResid && a.ssq_out != nullptr;
+      for (int jj = 0; i0 + jj * 256 < i1; ++jj) {  // uniform over the 256 threads
+        const int i = i0 + jj * 256 + t;
         const int b = i >> 7, row = i & 127;
-        if (b >= a.B) continue;
+        float sq = 0.0f;
+        if (got && i < i1 && b < a.B) {
         float sum[NACC];
 #pragma unroll
         for (int acc = 0; acc < NACC; ++acc) {
@@ -412,7 +453,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
                          : "r"(sA + (uint32_t)(((sp * NACC + acc) * per + (i - i0)) * 4)));
             s0 = sp == 0 ? v : __fadd_rn(s0, v);
           }
-          sum[acc] = s0;
+          sum[acc] = fold ? __fmul_rn(s0, rs_b[b]) : s0;
         }
         const int n = n0 + row;
         uint16_t out;
@@ -423,6 +464,26 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
         else
           out = f2h(sum[0]);
         a.y[(int64_t)b * a.ldy + n] = out;
+          const float ov = h2f(out);
+          sq = __fmul_rn(ov, ov);
+          if (MODE == kBgResid && a.xg_out != nullptr)
+            a.xg_out[(int64_t)b * a.ldy + n] = f2h(__fmul_rn(ov, h2f(a.xg_gamma[n])));
+        }
+        if (want_ss) {  // a warp's 32 items lie in one row b
+          sq = warp_sum(sq);
+          if ((t & 31) == 0) red_ss[jj * 8 + (t >> 5)] = sq;
+        }
+      }
+      if (want_ss) {
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (t < kBMaxBatch) {
+          float s4 = 0.0f;
+          if (t * 128 >= i0 && t * 128 < i1) {  // row t's 4 warp sums, in order
+            const int w0 = (t * 128 - i0) >> 5;
+            s4 = __fadd_rn(__fadd_rn(red_ss[w0], red_ss[w0 + 1]), __fadd_rn(red_ss[w0 + 2], red_ss[w0 + 3]));
+          }
+          a.ssq_out[((int64_t)tile * splits + me) * 64 + t] = s4;
+        }
       }
       if (!got) Q3_BWAIT(&red_bar, 0, kErrTimeoutFull, 12);  // pushes into this CTA landed
     }
@@ -444,7 +505,9 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
 // Per-sequence RMSNorm of model/qwen3_full.mlir:134-165 into the GEMM operand
 // buffer xn [npad][K] (padding rows stay zero).  With `tokens`, the input of
 // sequence b is embedding row tokens[b * tok_stride + seq[b].pos] and is also
-// stored as the residual stream x.
+// stored as the residual stream x; with ssq_out the kernel writes each row's
+// sum of squares ssq_out[b] and xn = f16(x * gamma) instead, the operand of a
+// projection that folds the 1 / r_b in (k_bgemm_q8's ssq_in).
 struct BNormArgs {
   const uint16_t* x;     // [npad][K] residual (ignored when tokens != nullptr)
   uint16_t* x_out;       // embedding copy target (tokens != nullptr)
@@ -457,6 +520,7 @@ struct BNormArgs {
   int64_t tok_len;       // positions per row
   const BatchSeq* seq;
   const uint16_t* embd;
+  float* ssq_out;        // [64]: sum of squares of each row (rows >= B: 0)
   int* err;
   unsigned long long* trace;  // optional launch timing record
 };
@@ -487,9 +551,33 @@ __global__ void __launch_bounds__(256) k_bnorm(const __grid_constant__ BNormArgs
     for (int i = threadIdx.x; i < a.K / 8; i += 256)
       reinterpret_cast<uint4*>(a.x_out + (int64_t)b * a.K)[i] = reinterpret_cast<const uint4*>(x)[i];
   }
-  cta_rmsnorm_to_smem(x, a.gamma, a.K, xs, &rs);
-  for (int i = threadIdx.x; i < a.K / 8; i += 256)
-    reinterpret_cast<uint4*>(a.xn + (int64_t)b * a.K)[i] = reinterpret_cast<const uint4*>(xs)[i];
+  if (a.ssq_out != nullptr) {
+    // the row's sum of squares (threads' strided partials, then the 8 warps in order)
+    __shared__ float wss[8];
+    float ss = 0.0f;
+    for (int k = threadIdx.x; k < a.K; k += 256) {
+      const float v = h2f(x[k]);
+      ss = __fmaf_rn(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) wss[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = wss[0];
+      for (int w = 1; w < 8; ++w) t = __fadd_rn(t, wss[w]);
+      a.ssq_out[b] = t;
+    }
+    if (b == 0)
+      for (int r = a.B + (int)threadIdx.x; r < kBMaxBatch; r += 256) a.ssq_out[r] = 0.0f;
+  }
+  if (a.ssq_out != nullptr) {
+    for (int k = threadIdx.x; k < a.K; k += 256)
+      a.xn[(int64_t)b * a.K + k] = f2h(__fmul_rn(h2f(x[k]), h2f(a.gamma[k])));
+  } else {
+    cta_rmsnorm_to_smem(x, a.gamma, a.K, xs, &rs);
+    for (int i = threadIdx.x; i < a.K / 8; i += 256)
+      reinterpret_cast<uint4*>(a.xn + (int64_t)b * a.K)[i] = reinterpret_cast<const uint4*>(xs)[i];
+  }
   ktrace_end(a.trace);
 }
 

@@ -278,7 +278,10 @@ def test_batch_random_context_steps(gpu, bmodels):
         runs.append(np.stack([toks[b, ctx[b] + 1: ctx[b] + 7] for b in range(B)]))
     assert ((runs[0] >= 0) & (runs[0] < 151936)).all()
     assert np.array_equal(runs[0], runs[1])
-    assert bd.kernel_launches() == 2 * 6 * (28 * 7 + 2)
+    # per step: 28 x (Q|K|V, attention, O, gate|up, down), the layer-0 embedding
+    # gather, the final RMSNorm and the vocab head (the layers' RMSNorms run inside
+    # the projections)
+    assert bd.kernel_launches() == 2 * 6 * (28 * 5 + 3)
     bd.close()
 
 
