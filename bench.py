@@ -601,9 +601,35 @@ def measure_batched(q3b200, dw, d: Dist, key: str, seed: int, peak: float, warmu
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": kern[dom]["achieved_gbs"],
                          "peak": peak, "unit": "GB/s",
                          "frac": kern[dom]["achieved_gbs"] / peak,
-                         "traffic": load_traffic().get(f"b{B}_{dom}")},
+                         "traffic": batched_traffic(kern, dom),
+                         "traffic_source": "one-launch ncu captures on a context-256 small "
+                                           "case (profiles/k_bgemm_q8_b32.md, k_battn_b32.md); "
+                                           "attention's DRAM/algorithmic ratio there times "
+                                           "this launch's algorithmic bytes (its traffic grows "
+                                           "with the context it streams)"},
             "kernels": kern,
             "l2": "inputs larger than L2 (779 MB of weights + the KV caches every step)"}
+
+
+def batched_traffic(kern: dict, dom: str):
+    """DRAM bytes per launch of the dominant batched kernel: the ratio of ncu
+    DRAM bytes to algorithmic bytes in the one-launch small-case capture, times
+    this launch's algorithmic bytes (attention's traffic scales with context)."""
+    t = load_traffic()
+    ratio = {"attn": t.get("b32_attn_c256", 0) / B32_ATTN_C256_ALG if "b32_attn_c256" in t else None}
+    for k in ("qkv", "o", "gate_up", "down"):
+        if f"b32_{k}_c256" in t:
+            ratio[k] = t[f"b32_{k}_c256"] / B32_PROJ_ALG[k]
+    r = ratio.get(dom)
+    return None if r is None else r * kern[dom]["alg_bytes_per_launch"]
+
+
+# algorithmic bytes of the captured small-case launches (B=32, context 256 + 3 warm-up + 1
+# timed step of the benchmark twin at layer 4): K/V rows of every position, and the
+# projections' weights + activations
+B32_ATTN_C256_ALG = 32 * 8 * 2 * 256 * (256 + 4)  # (b, h) x K+V rows of 256 B x positions 0..259
+B32_PROJ_ALG = {"qkv": 4456448 + 32 * 1024 * 2, "o": 2228224 + 32 * 2048 * 2 + 32 * 1024 * 2,
+                "gate_up": 6684672 + 32 * 1024 * 2, "down": 3342336 + 32 * 3072 * 2 + 32 * 1024 * 2}
 
 
 def measure_gemv_stream(q3b200, dw, peak: float) -> dict:
