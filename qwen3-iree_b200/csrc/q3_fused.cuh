@@ -153,6 +153,34 @@ __device__ __forceinline__ uint64_t l2_policy_evict_normal() {
   return pol;
 }
 
+// Four warp sums (warp_sum's butterfly on each value), the shuffles of the
+// four interleaved: the same operations per value, four chains in flight.
+__device__ __forceinline__ void warp_sum4(float (&v)[4]) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], off));
+}
+
+// Four row dots of one lane's block (block b = lane, K = 1024) in the block
+// order of q8_block_dot_mlir, the four inner chains interleaved:
+// out[j] = fma(scale_j, inner_j, 0) with inner_j = the 32 products in order.
+__device__ __forceinline__ void q8_block_dot4_mlir(const Q8BlockWords (&b)[4], const uint32_t (&xr)[16],
+                                                   float (&out)[4]) {
+  float inner[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t h01, h23;
+      q8x4_to_h2(b[j].q[i], h01, h23);
+      inner[j] = fma_h2(h01, xr[2 * i], inner[j]);
+      inner[j] = fma_h2(h23, xr[2 * i + 1], inner[j]);
+    }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) out[j] = __fmaf_rn(h2f((uint16_t)b[j].scale16), inner[j], 0.0f);
+}
+
 // A K = 1024 x block (32 f16) from shared memory in the 40-half block layout.
 __device__ __forceinline__ void load_xblock(const uint16_t* xs, int b, uint32_t (&xb)[16]) {
   const uint4* p = reinterpret_cast<const uint4*>(xs + b * kXhStride);
@@ -406,11 +434,30 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   // 3) RMSNorm with attn_norm
   slice_rmsnorm(xr, xss, gam, xs);
   fphase(a.phase, 2);
-  // 4) Q|K|V dots (the block order of q8_block_dot_mlir)
+  // 4) Q|K|V dots (the block order of q8_block_dot_mlir; q8_h2regs_dot_xh's
+  //    operations for each row, the four rows' chains interleaved)
+  {
+    const uint4* xb = reinterpret_cast<const uint4*>(xs + lane * kXhStride);
+    float inner[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float d = q8_h2regs_dot_xh<1>(hq[i], sq[i], kDim / kQBlk, lane, xs);
-    if (lane == 0) loc[warp + 8 * i] = f2h(d);
+    for (int q = 0; q < 4; ++q) {
+      const uint4 xv = xb[q];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        inner[i] = fma_h2(hq[i][0][4 * q + 0], xv.x, inner[i]);
+        inner[i] = fma_h2(hq[i][0][4 * q + 1], xv.y, inner[i]);
+        inner[i] = fma_h2(hq[i][0][4 * q + 2], xv.z, inner[i]);
+        inner[i] = fma_h2(hq[i][0][4 * q + 3], xv.w, inner[i]);
+      }
+    }
+    float d[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = __fmaf_rn(sq[i][0], inner[i], 0.0f);
+    warp_sum4(d);
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) loc[warp + 8 * i] = f2h(d[i]);
+    }
   }
   __syncthreads();
   fphase(a.phase, 4);
@@ -735,16 +782,21 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   const bool wok = mbar_wait_own(&wbar, 0u, a.err, kErrTimeoutFull);
   fphase(a.phase, 3);
   {
+    // the warp's two gate and two up rows, their chains interleaved (the
+    // operations of q8_block_dot_mlir + warp_sum for each row)
     uint32_t xb[16];
     load_xblock(xs, lane, xb);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int row = 2 * warp + i;
-      const float g = warp_sum(q8_block_dot_mlir(
-          q8_load_block(smem_u32(wg) + row * kRow1K + kQBytes * lane), xb, 0.0f));
-      const float u = warp_sum(q8_block_dot_mlir(
-          q8_load_block(smem_u32(wu) + row * kRow1K + kQBytes * lane), xb, 0.0f));
-      if (lane == 0) act_loc[row] = swiglu_h(f2h(g), f2h(u));
+    const int row = 2 * warp;
+    const Q8BlockWords bw[4] = {q8_load_block(smem_u32(wg) + row * kRow1K + kQBytes * lane),
+                                q8_load_block(smem_u32(wu) + row * kRow1K + kQBytes * lane),
+                                q8_load_block(smem_u32(wg) + (row + 1) * kRow1K + kQBytes * lane),
+                                q8_load_block(smem_u32(wu) + (row + 1) * kRow1K + kQBytes * lane)};
+    float d[4];
+    q8_block_dot4_mlir(bw, xb, d);
+    warp_sum4(d);
+    if (lane == 0) {
+      act_loc[row] = swiglu_h(f2h(d[0]), f2h(d[1]));
+      act_loc[row + 1] = swiglu_h(f2h(d[2]), f2h(d[3]));
     }
   }
   __syncthreads();
