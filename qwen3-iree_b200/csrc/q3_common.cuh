@@ -251,7 +251,7 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return pol;
 }
 
-// 1-D bulk copy global -> shared (no multicast), completion on an mbarrier.
+// 1-D bulk copy global -> this CTA's shared memory, completion on an mbarrier.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {

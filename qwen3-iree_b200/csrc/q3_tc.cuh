@@ -103,7 +103,7 @@ __device__ __forceinline__ uint32_t sw128_chunk_offset(uint32_t r, uint32_t c) {
 }
 
 // ---------------------------------------------------------------- tensor TMA
-// 2-D tiled load (no multicast) of box {x.., y..} at coordinates (x, y),
+// 2-D tiled load into this CTA's shared memory of box {x.., y..} at (x, y),
 // completion on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
