@@ -158,7 +158,10 @@ int q3_decode_attention(const void* qkv, const void* q_norm, const void* k_norm,
  * library, sized for S <= 4096 positions (about 1.08 MB per device, held
  * until the process exits); larger S returns Q3_ERR_INVALID.  The first call
  * on each device looks up that array's device address (call it once before
- * any stream capture).  All calls share the one array: calls that overlap on
+ * any stream capture); the address is kept per device and belongs to the
+ * device's primary context, so a caller working in another CUDA context of
+ * the device, or after a device reset, must not use this entry point.  All
+ * calls share the one array: calls that overlap on
  * the GPU (concurrent streams, several host threads) race and must not be
  * issued.  Each call clears the counters it needs.  Results equal
  * q3_decode_attention bit for bit.  This entry point has no counterpart in
