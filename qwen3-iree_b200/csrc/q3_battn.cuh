@@ -7,10 +7,11 @@
 //
 //   * the work is the list of 32-key chunks of every (sequence b, kv head h),
 //     flattened in (b, h, chunk) order; CTA g of a persistent grid (two per
-//     SM) takes the equal share [g T / G, (g+1) T / G) of the T chunks, so
-//     every CTA streams the same number of bytes whatever the mix of
-//     positions (no tail wave).  A share cuts the list into pieces, one per
-//     (b, h) it touches.
+//     SM) takes a contiguous share of it, so every CTA streams about the same
+//     number of bytes whatever the mix of positions (no tail wave).  A share
+//     cuts the list into pieces, one per (b, h) it touches, and a piece
+//     costs about five chunks beyond its own (measured), so shares are equal
+//     in chunks + pieces rather than in chunks alone (BaShares).
 //   * a producer thread streams the share's 32-key K and V tiles (one 8 KB
 //     tensor-TMA box each, the cache seen as [B*28*S rows, 1024] f16)
 //     through a ring of stages.  Cache rows below pos were written by
@@ -87,6 +88,8 @@ struct BAttnArgs {
   uint16_t* out;           // [npad][2048]
   AttnPartial* part;       // [gridDim.x][2 slots][2 q heads]
   unsigned int* counters;  // [B][8], zero between launches
+  int piece_units;         // units a (b, h) piece adds to its share's cost (a chunk is
+                           // kBaChunkUnits; BaShares)
   int* err;
   int tag;
   unsigned long long* trace;  // optional launch timing record
@@ -103,10 +106,12 @@ struct BaPiece {
 struct BAttnSmem {
   uint64_t full[kBaFullBars], empty[kBaStages];
   uint64_t qready[kBaQSlots], qfree[kBaQSlots], wfree[2];
+  uint64_t geo;                // gfirst / glast / lofirst written (the q warp, after piece 0)
   int nch[kBaMaxBatch];        // chunks of sequence b (per kv head)
   int pre[kBaMaxBatch + 1];    // pre[b] = 8 * sum of nch below b
   long long pos[kBaMaxBatch];
-  int b0, bad;
+  int b0, bad, lo, hi;
+  int gfirst, glast, lofirst;  // CTAs of the first / last piece's (b, h), share start of gfirst
   unsigned int pcnt[2];        // warps done with the piece in state slot p % 2
   __align__(16) uint16_t q[kBaQSlots][2][kHD];
   __align__(16) uint16_t kn[kBaQSlots][kHD];
@@ -125,9 +130,79 @@ __host__ __device__ constexpr size_t battn_workspace_bytes(int grid, int B) {
   return sizeof(AttnPartial) * (size_t)grid * 4 + (size_t)B * kNKV * 4;
 }
 
-// The CTA whose share holds flattened chunk u (shares [g T / G, (g+1) T / G)).
-__device__ __forceinline__ int battn_cta_of(long long u, long long T, long long G) {
-  return (int)(((u + 1) * G + T - 1) / T - 1);
+// Shares of equal cost.  A 32-key chunk costs kBaChunkUnits; a (b, h) piece
+// adds A units ahead of its first chunk (its q staging, its partial last
+// chunk, its merges).  Chunk u starts at unit Cs(u) = kBaChunkUnits u +
+// A (8 b + h + 1) for its (b, h); CTA g of G takes the chunks whose start
+// unit lies in [g C / G, (g+1) C / G), C = kBaChunkUnits T + 8 B A, so its
+// share is contiguous.  A > 0 only while C / G >= kBaChunkUnits + A, which
+// puts a chunk start in every interval (consecutive starts are at most
+// kBaChunkUnits + A apart): no CTA between two others of a (b, h) is empty.
+constexpr long long kBaChunkUnits = 8;
+// Measured per-piece cost (B200, B=32 and 64 at contexts of 128-4096): 4-6
+// chunks; 40 units = 5 chunks.
+constexpr int kBaPieceUnits = 40;
+
+struct BaShares {
+  long long T, G, C, A;
+  __device__ void init(long long T_, long long grid, int B, long long A_) {
+    T = T_;
+    G = grid < T ? grid : T;
+    A = A_ > 0 ? A_ : 0;
+    C = kBaChunkUnits * T + (long long)kNKV * B * A;
+    if (C / G < kBaChunkUnits + A) {
+      A = 0;
+      C = kBaChunkUnits * T;
+    }
+  }
+  // start unit of (b, h)'s first chunk
+  __device__ long long unit(const BAttnSmem& sm, int b, int h) const {
+    return kBaChunkUnits * (sm.pre[b] + (long long)h * sm.nch[b]) + A * (kNKV * b + h + 1);
+  }
+};
+
+// floor(n / d) for 0 <= n < 2^53, d > 0: a double quotient, corrected.
+__device__ __forceinline__ long long battn_div(long long n, long long d) {
+  long long q = (long long)((double)n / (double)d);
+  if (q * d > n) --q;
+  else if ((q + 1) * d <= n) ++q;
+  return q;
+}
+
+// First chunk of CTA g's share; warp-collective (every lane returns it).
+__device__ long long battn_share_lo(const BaShares& s, const BAttnSmem& sm, int B, long long g,
+                                    int lane) {
+  if (g <= 0) return 0;
+  if (g >= s.G) return s.T;
+  const long long t = battn_div(g * s.C + s.G - 1, s.G);  // the share's first unit
+  // the last (b, h) whose first chunk starts at or before unit t
+  const unsigned m0 = __ballot_sync(0xffffffffu, lane < B && s.unit(sm, lane, 0) <= t);
+  const unsigned m1 = __ballot_sync(0xffffffffu, lane + 32 < B && s.unit(sm, lane + 32, 0) <= t);
+  if (m0 == 0u) return 0;  // t lies before the first chunk
+  const int b = m1 ? 63 - __clz((int)m1) : 31 - __clz((int)m0);
+  const int h = 31 - __clz((int)__ballot_sync(0xffffffffu, lane < kNKV && s.unit(sm, b, lane) <= t));
+  const long long s0 = sm.pre[b] + (long long)h * sm.nch[b];
+  const long long u = s0 + ((t - s.unit(sm, b, h) + kBaChunkUnits - 1) >> 3);  // / kBaChunkUnits
+  return u < s0 + sm.nch[b] ? u : s0 + sm.nch[b];
+}
+
+// The sequence holding flattened chunk u.
+__device__ __forceinline__ int battn_seq_of(const BAttnSmem& sm, int B, long long u) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (sm.pre[mid] <= u) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// The CTA whose share holds flattened chunk u.
+__device__ int battn_share_of(const BaShares& s, const BAttnSmem& sm, int B, long long u) {
+  const int lo = battn_seq_of(sm, B, u);
+  const int h = ((int)u - sm.pre[lo]) / sm.nch[lo];
+  const long long cs = kBaChunkUnits * u + s.A * (kNKV * lo + h + 1);
+  return (int)battn_div(cs * s.G, s.C);
 }
 
 // Walks the pieces of share [lo, hi): start with (b0, the h holding lo).
@@ -206,6 +281,7 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
     }
     mbar_init(&sm.wfree[0], 32);
     mbar_init(&sm.wfree[1], 32);
+    mbar_init(&sm.geo, 32);
     fence_mbar_init();
   }
   __syncthreads();
@@ -224,21 +300,27 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
     if (lane == 31) sm.pre[kBaMaxBatch] = tot0 + i1;
   }
   __syncthreads();
-  const long long T = sm.pre[kBaMaxBatch];
-  const long long G = (long long)gridDim.x < T ? (long long)gridDim.x : T;
+  BaShares sh;
+  sh.init(sm.pre[kBaMaxBatch], gridDim.x, B, a.piece_units);
+  const long long T = sh.T, G = sh.G;
   const int g = blockIdx.x;
   if (sm.bad || g >= G) {
     pdl_launch_dependents();
     if (sm.bad && g == 0 && threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrBadPos);
     return;
   }
-  const int lo = (int)(g * T / G), hi = (int)((g + 1) * T / G);
-  if (warp == 0) {  // the sequence holding chunk lo
-    for (int bb = lane; bb < B; bb += 32)
-      if (sm.pre[bb] <= lo && lo < sm.pre[bb + 1]) sm.b0 = bb;
+  if (warp < 2) {  // this CTA's share: warp 0 its first chunk, warp 1 its end
+    const long long gg = g + warp;
+    const int l = sh.A == 0 ? (int)battn_div(gg * T + G - 1, G)  // ceil(g T / G)
+                            : (int)battn_share_lo(sh, sm, B, gg, lane);
+    if (lane == 0) (warp == 0 ? sm.lo : sm.hi) = l;
+    if (warp == 0)  // the sequence holding the first chunk
+      for (int bb = lane; bb < B; bb += 32)
+        if (sm.pre[bb] <= l && l < sm.pre[bb + 1]) sm.b0 = bb;
   }
   __syncthreads();
   pdl_launch_dependents();
+  const int lo = sm.lo, hi = sm.hi;
   const int b_first = sm.b0;
   bphase(a.phase, 1, threadIdx.x == 0);  // work list ready
 
@@ -335,6 +417,29 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
         *reinterpret_cast<uint2*>(a.vc + off + 4 * lane) = v;
       }
       mbar_arrive(&sm.qready[sl]);
+      if (p == 0) {
+        // the CTAs of the (b, h) pairs this share cuts: its first piece's
+        // first CTA and that CTA's share start, its last piece's last CTA (the
+        // merges wait on geo; computed once piece 0's q is out)
+        const int bl = battn_seq_of(sm, B, hi - 1);
+        const int hl = (hi - 1 - sm.pre[bl]) / sm.nch[bl];
+        const int s1l = sm.pre[bl] + (hl + 1) * sm.nch[bl];
+        const int hf = (lo - sm.pre[b_first]) / sm.nch[b_first];
+        const int s0f = sm.pre[b_first] + hf * sm.nch[b_first];
+        int gf = g, gl = g;
+        if (lane == 0 && s0f < lo) gf = battn_share_of(sh, sm, B, s0f);
+        if (lane == 1 && s1l > hi) gl = battn_share_of(sh, sm, B, s1l - 1);
+        gf = __shfl_sync(0xffffffffu, gf, 0);
+        gl = __shfl_sync(0xffffffffu, gl, 1);
+        const int lof = gf == g ? lo : (int)battn_share_lo(sh, sm, B, gf, lane);
+        if (lane == 0) {
+          sm.gfirst = gf;
+          sm.glast = gl;
+          sm.lofirst = lof;
+        }
+        __syncwarp();
+        mbar_arrive(&sm.geo);
+      }
     }
     return;
   }
@@ -500,7 +605,10 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
       }
       __threadfence();
       __syncwarp();
-      const int g1 = battn_cta_of(pc.s0, T, G), g2 = battn_cta_of(pc.s1 - 1, T, G);
+      if (!mbar_wait_own(&sm.geo, 0u, a.err,
+                         kErrTimeoutFull | (7 << 4) | ((a.tag & 0xff) << 8), kSpinCycles))
+        break;
+      const int g1 = pc.s0 < lo ? sm.gfirst : g, g2 = pc.s1 > hi ? sm.glast : g;
       unsigned last = 0;
       if (lane == 0) {
         const unsigned prevc = atomicAdd(a.counters + bh, 1u);
@@ -510,7 +618,7 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
       last = __shfl_sync(0xffffffffu, last, 0);
       if (!last) continue;
       __threadfence();
-      const int lo1 = (int)(g1 * T / G);
+      const int lo1 = pc.s0 < lo ? sm.lofirst : lo;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         mm[hh] = -__int_as_float(0x7f800000);
