@@ -783,7 +783,8 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   fphase(a.phase, 3);
   {
     // the warp's two gate and two up rows, their chains interleaved (the
-    // operations of q8_block_dot_mlir + warp_sum for each row)
+    // operations of q8_block_dot_mlir + warp_sum for each row); lanes 0 and
+    // 1 apply SwiGLU to the two act values
     uint32_t xb[16];
     load_xblock(xs, lane, xb);
     const int row = 2 * warp;
@@ -794,10 +795,8 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
     float d[4];
     q8_block_dot4_mlir(bw, xb, d);
     warp_sum4(d);
-    if (lane == 0) {
-      act_loc[row] = swiglu_h(f2h(d[0]), f2h(d[1]));
-      act_loc[row + 1] = swiglu_h(f2h(d[2]), f2h(d[3]));
-    }
+    if (lane < 2)
+      act_loc[row + lane] = swiglu_h(f2h(lane == 0 ? d[0] : d[2]), f2h(lane == 0 ? d[1] : d[3]));
   }
   __syncthreads();
   fphase(a.phase, 4);
