@@ -153,6 +153,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_normal() {
   return pol;
 }
 
+// 16-byte asynchronous copy global -> shared (L2 only, like __ldcg); the
+// thread's copies are complete after cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Four warp sums (warp_sum's butterfly on each value), the shuffles of the
 // four interleaved: the same operations per value, four chains in flight.
 __device__ __forceinline__ void warp_sum4(float (&v)[4]) {
@@ -290,6 +297,8 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   __shared__ __align__(16) uint4 ssl;
   __shared__ __align__(16) uint16_t xs[kDim / kQBlk * kXhStride];
   __shared__ __align__(16) uint16_t loc[kFaRows];
+  __shared__ __align__(16) uint16_t rstage_h[kFSlice];          // warp 0's residual slice
+  __shared__ __align__(16) float rstage_p[kFParts][kFSlice];    // and its 8 partials
   __shared__ __align__(16) uint16_t qkv_h[4 * kHD];  // q head 2h | q head 2h+1 | k | v (raw)
   __shared__ __align__(16) uint16_t qs[2][kHD];
   __shared__ __align__(16) uint16_t ks[kHD];
@@ -410,31 +419,55 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
     tma_load_2d(wo, &a.wo_map, (int)(kFaOBytes / 4) * h, a.layer * kDim + kFaORows * r, &obar);
   }
   bool ok = mbar_wait_own(&cbar, 0u, a.err, kErrTimeoutFull);  // constants (long landed)
-  // 1) this rank's slice of x (cluster 0 publishes it), pushed with its sum of squares
-  if (warp == 0) {
-    uint2 xv = make_uint2(0u, 0u);
-    if (lane < 16)
-      xv = a.tokens != nullptr ? *reinterpret_cast<const uint2*>(yloc + 4 * lane)
-           : a.dpart == nullptr ? __ldcg(reinterpret_cast<const uint2*>(a.h1 + k0))
-                                : resid_plus_parts(a.h1, a.dpart, k0);
-    __syncwarp();
-    if (h == 0 && lane < 16) *reinterpret_cast<uint2*>(a.x_out + k0) = xv;
-    push_slice(xv, r, lane, yloc, xr, xss, &ssl, &xbar);
+  // 1) this rank's slice of x (cluster 0 publishes it): warp 0 starts the
+  //    slice's loads as asynchronous copies and sums them after its rows'
+  //    conversion below
+  const bool staged = a.tokens == nullptr;
+  if (warp == 0 && staged) {
+    if (lane < 8) cp_async16(rstage_h + 8 * lane, a.h1 + kFSlice * r + 8 * lane);
+    if (a.dpart != nullptr && lane < 16) {
+#pragma unroll
+      for (int c = 0; c < kFParts; ++c) cp_async16(&rstage_p[c][4 * lane], a.dpart + c * kDim + k0);
+    }
   }
-  // 2) while the slices travel: this warp's rows w, w+8 (q), w+16 (k), w+24
-  //    (v) at block `lane` converted to exact half2 registers
+  // 2) this warp's rows w, w+8 (q), w+16 (k), w+24 (v) at block `lane`
+  //    converted to exact half2 registers (warp 0's while its copies travel)
   const bool wok = mbar_wait_own(&wbar, 0u, a.err, kErrTimeoutFull);
   uint32_t hq[4][1][16];
   float sq[4][1];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     q8_row_to_h2regs<1>(smem_u32(wqkv) + (warp + 8 * i) * kRow1K, kDim / kQBlk, lane, hq[i], sq[i]);
+  // 3) warp 0: the slice x = f16(h1 + f16(sum_c dpart[c])), pushed with its
+  //    sum of squares (resid_plus_parts' operations)
+  if (warp == 0) {
+    if (staged) {
+      cp_async_wait_all();
+      __syncwarp();
+    }
+    uint2 xv = make_uint2(0u, 0u);
+    if (lane < 16) {
+      if (!staged) {
+        xv = *reinterpret_cast<const uint2*>(yloc + 4 * lane);
+      } else {
+        const uint2 rv = *reinterpret_cast<const uint2*>(rstage_h + 4 * lane);
+        if (a.dpart == nullptr) {
+          xv = rv;
+        } else {
+          xv = resid_finish_smem(rv, smem_u32(&rstage_p[0][4 * lane]), kFSlice * 4);
+        }
+      }
+    }
+    __syncwarp();
+    if (h == 0 && lane < 16) *reinterpret_cast<uint2*>(a.x_out + k0) = xv;
+    push_slice(xv, r, lane, yloc, xr, xss, &ssl, &xbar);
+  }
   fphase(a.phase, 3);
   ok = mbar_wait_own(&xbar, 0u, a.err, kErrTimeoutFull) && ok;
-  // 3) RMSNorm with attn_norm
+  // 4) RMSNorm with attn_norm
   slice_rmsnorm(xr, xss, gam, xs);
   fphase(a.phase, 2);
-  // 4) Q|K|V dots (the block order of q8_block_dot_mlir; q8_h2regs_dot_xh's
+  // 5) Q|K|V dots (the block order of q8_block_dot_mlir; q8_h2regs_dot_xh's
   //    operations for each row, the four rows' chains interleaved)
   {
     const uint4* xb = reinterpret_cast<const uint4*>(xs + lane * kXhStride);
@@ -461,7 +494,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   }
   __syncthreads();
   fphase(a.phase, 4);
-  // 4) every rank pushes its rows into every rank's copy of the head pair's
+  // 6) every rank pushes its rows into every rank's copy of the head pair's
   //    raw q (2 x 128) | k | v: q rows 16r.., k rows 8r.., v rows 8r..
   if (tid < 4 * kFC) {
     const int dst = tid >> 2, piece = tid & 3;
@@ -472,7 +505,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   }
   ok = mbar_wait_own(&qbar, 0u, a.err, kErrTimeoutFull) && ok;
   fphase(a.phase, 5);
-  // 5) QK-norm + RoPE: q heads by warps 0, 1; the k head by warp 2
+  // 7) QK-norm + RoPE: q heads by warps 0, 1; the k head by warp 2
   if (warp < 3) {
     uint16_t gv[4];
 #pragma unroll
@@ -489,7 +522,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
     a.vc[off] = qkv_h[3 * kHD + tid];
   }
 
-  // 6) this rank's chunks: warp w takes local chunks w, w+8, ... through its
+  // 8) this rank's chunks: warp w takes local chunks w, w+8, ... through its
   //    slot and folds them as it goes (att_merge order); lane = 8 q + key
   //    for the scores (dims 32q .. 32q+31 of the key), lane = 4 head dims for p.v
   bool kvok = true;
@@ -598,7 +631,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   }
   __syncthreads();
   fphase(a.phase, 9);
-  // 7) this rank's fold over its 8 warps: thread (head hh, dim d); a warp
+  // 9) this rank's fold over its 8 warps: thread (head hh, dim d); a warp
   //    without chunks holds m = -inf, l = 0, o = 0
   {
     const int hh = tid >> 7, d = tid & (kHD - 1);
@@ -629,7 +662,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
       v = *reinterpret_cast<const uint4*>(&cpart[hh].o[d0 + 4 * (piece - 1)]);
     st_async_v4(smem_u32(&fin[r][4 * piece]), (uint32_t)dst, v, smem_u32(&fbar));
   }
-  // 8) fold dims 16r .. 16r+15 over the ranks (lane q < 16 holds rank q's
+  // 10) fold dims 16r .. 16r+15 over the ranks (lane q < 16 holds rank q's
   //    weight) and push them into every rank's attention output
   if (warp == 0) {
     ok = mbar_wait_own(&fbar, 0u, a.err, kErrTimeoutFull) && ok;
@@ -654,7 +687,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   ok = mbar_wait_own(&abar, 0u, a.err, kErrTimeoutFull) && ok;
   fphase(a.phase, 12);
   const bool ook = mbar_wait_own(&obar, 0u, a.err, kErrTimeoutFull);
-  // 9) the head pair's slice of W_o: rows 64r + 8w + i, lane = 4 i + sub takes
+  // 11) the head pair's slice of W_o: rows 64r + 8w + i, lane = 4 i + sub takes
   //    blocks 2 sub, 2 sub + 1 (acc = fma(scale, inner, acc) per block), then
   //    v += shfl_xor(v, 1); v += shfl_xor(v, 2)
   {

@@ -805,22 +805,55 @@ __global__ void __launch_bounds__(kGemv1tThreads, gemv1t_min_blocks<G, MODE>())
 // per thread: y = f16(res + f16(((p0 + p1) + p2) + ... + p7)).
 constexpr int kFParts = 8;
 
-__device__ __forceinline__ uint2 resid_plus_parts(const uint16_t* res, const float* parts, int k0) {
-  const uint2 rv = __ldcg(reinterpret_cast<const uint2*>(res + k0));
-  float4 s = __ldcg(reinterpret_cast<const float4*>(parts + k0));
+// f16(res + f16(s)) of 4 elements.
+__device__ __forceinline__ uint2 resid_round(uint2 rv, float4 s) {
+  auto add = [](uint16_t r, float q) { return f2h(__fadd_rn(h2f(r), h2f(f2h(q)))); };
+  uint2 y;
+  y.x = (uint32_t)add((uint16_t)(rv.x & 0xffffu), s.x) | ((uint32_t)add((uint16_t)(rv.x >> 16), s.y) << 16);
+  y.y = (uint32_t)add((uint16_t)(rv.y & 0xffffu), s.z) | ((uint32_t)add((uint16_t)(rv.y >> 16), s.w) << 16);
+  return y;
+}
+
+// f16(res + f16(p[0] + ... + p[7])) of 4 elements, the partials summed in order.
+__device__ __forceinline__ uint2 resid_finish(uint2 rv, const float4 (&p)[kFParts]) {
+  float4 s = p[0];
 #pragma unroll
   for (int c = 1; c < kFParts; ++c) {
-    const float4 t = __ldcg(reinterpret_cast<const float4*>(parts + c * kDim + k0));
+    s.x = __fadd_rn(s.x, p[c].x);
+    s.y = __fadd_rn(s.y, p[c].y);
+    s.z = __fadd_rn(s.z, p[c].z);
+    s.w = __fadd_rn(s.w, p[c].w);
+  }
+  return resid_round(rv, s);
+}
+
+// resid_finish over partials in shared memory (partial c at p0 + c * stride
+// bytes), read one at a time.
+__device__ __forceinline__ uint2 resid_finish_smem(uint2 rv, uint32_t p0, uint32_t stride) {
+  float4 s;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(s.x), "=f"(s.y), "=f"(s.z), "=f"(s.w)
+               : "r"(p0));
+#pragma unroll 1
+  for (int c = 1; c < kFParts; ++c) {
+    float4 t;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(t.x), "=f"(t.y), "=f"(t.z), "=f"(t.w)
+                 : "r"(p0 + (uint32_t)c * stride));
     s.x = __fadd_rn(s.x, t.x);
     s.y = __fadd_rn(s.y, t.y);
     s.z = __fadd_rn(s.z, t.z);
     s.w = __fadd_rn(s.w, t.w);
   }
-  auto add = [](uint16_t r, float p) { return f2h(__fadd_rn(h2f(r), h2f(f2h(p)))); };
-  uint2 y;
-  y.x = (uint32_t)add((uint16_t)(rv.x & 0xffffu), s.x) | ((uint32_t)add((uint16_t)(rv.x >> 16), s.y) << 16);
-  y.y = (uint32_t)add((uint16_t)(rv.y & 0xffffu), s.z) | ((uint32_t)add((uint16_t)(rv.y >> 16), s.w) << 16);
-  return y;
+  return resid_round(rv, s);
+}
+
+__device__ __forceinline__ uint2 resid_plus_parts(const uint16_t* res, const float* parts, int k0) {
+  const uint2 rv = __ldcg(reinterpret_cast<const uint2*>(res + k0));
+  float4 p[kFParts];
+#pragma unroll
+  for (int c = 0; c < kFParts; ++c) p[c] = __ldcg(reinterpret_cast<const float4*>(parts + c * kDim + k0));
+  return resid_finish(rv, p);
 }
 
 // --------------------------------------------------------------------------
