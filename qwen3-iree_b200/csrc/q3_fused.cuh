@@ -412,12 +412,6 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   ktrace_release(a.trace);
   fphase(a.phase, 1);
 
-  // the W_o slice is needed last: its copy goes out after the release, so that
-  // fewer bytes are in flight while the slices below are read from L2
-  if (warp == 1 && lane == 0) {
-    mbar_expect_tx(&obar, kFaWoBytes);
-    tma_load_2d(wo, &a.wo_map, (int)(kFaOBytes / 4) * h, a.layer * kDim + kFaORows * r, &obar);
-  }
   bool ok = mbar_wait_own(&cbar, 0u, a.err, kErrTimeoutFull);  // constants (long landed)
   // 1) this rank's slice of x (cluster 0 publishes it): warp 0 starts the
   //    slice's loads as asynchronous copies and sums them after its rows'
@@ -467,6 +461,12 @@ __global__ void __launch_bounds__(kFaThreads, 1) k_fused_attn(const __grid_const
   // 4) RMSNorm with attn_norm
   slice_rmsnorm(xr, xss, gam, xs);
   fphase(a.phase, 2);
+  // the W_o slice is needed last: its copy goes out now, so that no weight
+  // bytes are in flight while the residual slices are read from L2
+  if (warp == 1 && lane == 0) {
+    mbar_expect_tx(&obar, kFaWoBytes);
+    tma_load_2d(wo, &a.wo_map, (int)(kFaOBytes / 4) * h, a.layer * kDim + kFaORows * r, &obar);
+  }
   // 5) Q|K|V dots (the block order of q8_block_dot_mlir; q8_h2regs_dot_xh's
   //    operations for each row, the four rows' chains interleaved)
   {
@@ -789,11 +789,6 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   ktrace_release(a.trace);
   fphase(a.phase, 1);
 
-  // the W_down window is needed last: its copy goes out after the release
-  if (warp == 1 && lane == 0) {
-    mbar_expect_tx(&dbar, kFbDBytes);
-    tma_load_2d(wd, &a.wd_map, (int)(dwin0 / 4), a.layer * kDim + kFbDRows * r, &dbar);
-  }
   // 1) this rank's slice of h1 = f16(x + f16(sum_h opart[h])) (cluster 0
   //    publishes it), pushed with its sum of squares
   if (warp == 0) {
@@ -810,6 +805,12 @@ __global__ void __launch_bounds__(kFbThreads, 1) k_fused_ffn(const __grid_consta
   // 2) RMSNorm with ffn_norm
   slice_rmsnorm(hr, xss, gam, xs);
   fphase(a.phase, 2);
+  // the W_down window is needed last: its copy goes out now (after the
+  // residual slices' L2 round trip)
+  if (warp == 1 && lane == 0) {
+    mbar_expect_tx(&dbar, kFbDBytes);
+    tma_load_2d(wd, &a.wd_map, (int)(dwin0 / 4), a.layer * kDim + kFbDRows * r, &dbar);
+  }
 
   // 3) gate|up rows: warp w -> act values 2w, 2w+1 of this CTA; lane = block
   const bool wok = mbar_wait_own(&wbar, 0u, a.err, kErrTimeoutFull);
