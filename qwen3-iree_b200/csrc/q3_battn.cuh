@@ -13,8 +13,11 @@
 //     costs about five chunks beyond its own (measured), so shares are equal
 //     in chunks + pieces rather than in chunks alone (BaShares).
 //   * a producer thread streams the share's 32-key K and V tiles (one 8 KB
-//     tensor-TMA box each, the cache seen as [B*28*S rows, 1024] f16)
-//     through a ring of stages.  Cache rows below pos were written by
+//     tensor-TMA box each) through a ring of stages.  The batched decoder
+//     keeps its caches head-major, [B][28][8 heads][S][128], so a piece's
+//     tiles are contiguous rows; the reference layout [B][28*S][8][128]
+//     (the batch-1 model's cache, read by the prompt prefill) is read as
+//     [rows, 1024] with a box of one head's 128 columns.  Cache rows below pos were written by
 //     earlier launches, so the stream starts before the wait on the previous
 //     kernel; only q and the new row need it.
 //   * a q warp stages, per piece, the normed and roped q of both q heads of h
@@ -67,7 +70,8 @@ constexpr int kBaQSlots = 4;                      // pieces whose q is staged ah
 constexpr int kBaMaxBatch = 64;
 
 struct BAttnArgs {
-  CUtensorMap kmap;        // K cache f16 [B*28*S rows, 1024], box {128, 32}
+  CUtensorMap kmap;        // K cache f16 [B*28*S rows, 1024] or head-major [B*28*8*S rows,
+                           // 128], box {128, 32}
   CUtensorMap vmap;        // V cache, same
   const uint16_t* qkv;     // [npad][4096] raw projections (q | k | v)
   const uint16_t* q_norm;  // gamma [128]
@@ -79,6 +83,8 @@ struct BAttnArgs {
   uint16_t* vc;
   int64_t S;               // slots per layer
   int64_t seq_rows;        // cache rows between sequences (28 * S; 0: rows share one cache)
+  int head_major;          // caches as [seq][28][8 heads][S][128] (a (b, h) piece streams
+                           // contiguous rows) instead of [seq][28 * S][8][128]
   int layer;
   int B;                   // sequences, <= 64
   int prefill;             // rows hold consecutive positions of one sequence whose new K/V
@@ -342,9 +348,12 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
           break;
         uint64_t* const fb = &sm.full[i % kBaFullBars];
         mbar_expect_tx(fb, 2 * kBaTileBytes);
-        const int y = (int)((int64_t)b * a.seq_rows + (int64_t)a.layer * a.S + (int64_t)c * kAttChunk);
-        tma_load_2d(gbase + st * 2 * kBaTileBytes, &a.kmap, h * kHD, y, fb);
-        tma_load_2d(gbase + st * 2 * kBaTileBytes + kBaTileBytes, &a.vmap, h * kHD, y, fb);
+        const int x = a.head_major ? 0 : h * kHD;
+        const int y = a.head_major
+                          ? (int)((((int64_t)b * kLayers + a.layer) * kNKV + h) * a.S + (int64_t)c * kAttChunk)
+                          : (int)((int64_t)b * a.seq_rows + (int64_t)a.layer * a.S + (int64_t)c * kAttChunk);
+        tma_load_2d(gbase + st * 2 * kBaTileBytes, &a.kmap, x, y, fb);
+        tma_load_2d(gbase + st * 2 * kBaTileBytes + kBaTileBytes, &a.vmap, x, y, fb);
         issued = i + 1;
         if (++c == sm.nch[b]) {
           c = 0;
@@ -411,7 +420,9 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
         *reinterpret_cast<uint2*>(&sm.vn[sl][4 * lane]) = v;
         __syncwarp();
         const int64_t off =
-            ((int64_t)pc.b * a.seq_rows + (int64_t)a.layer * a.S + pos) * (kNKV * kHD) + pc.h * kHD;
+            a.head_major
+                ? ((((int64_t)pc.b * kLayers + a.layer) * kNKV + pc.h) * a.S + pos) * kHD
+                : ((int64_t)pc.b * a.seq_rows + (int64_t)a.layer * a.S + pos) * (kNKV * kHD) + pc.h * kHD;
         *reinterpret_cast<uint2*>(a.kc + off + 4 * lane) =
             *reinterpret_cast<const uint2*>(&sm.kn[sl][4 * lane]);
         *reinterpret_cast<uint2*>(a.vc + off + 4 * lane) = v;
