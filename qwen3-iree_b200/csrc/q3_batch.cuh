@@ -7,12 +7,13 @@
 // Q8_0 weights (k_bgemm_q8): a producer thread brings 128 rows x 256 K of raw
 // Q8_0 bytes into shared memory with one tensor TMA (the row stride of the
 // reference layout is a multiple of 16 bytes, so a [128 x 272-byte] box
-// works) and the activations' K-slices with SWIZZLE_128B tensor TMA; four
+// works) and the activations' K-slices with SWIZZLE_128B tensor TMA; eight
 // dequantising warps turn each 64-wide K-slice into f16 weights in the
 // canonical SWIZZLE_128B layout -- w = f16(scale * q), the f16 dequant of the
 // reference's own fused-GEMV region (model/qwen3_full.mlir:564-579) -- and one
-// thread issues the MMAs.  The same four warps read the accumulators back with
-// tcgen05.ld and apply the epilogue (residual add, or SwiGLU over a gate tile
+// thread issues the MMAs.  The same warps read the accumulators back with
+// tcgen05.ld (four of them for a single-CTA tile, all eight for a split tile's
+// partial) and apply the epilogue (residual add, or SwiGLU over a gate tile
 // and its up tile held in two accumulators).
 //
 // f16 vocab head (k_bvocab): weight tiles and activations both arrive by
@@ -199,7 +200,9 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
   __shared__ __align__(8) uint64_t raw_full[kBgMaxKc], x_full, acc_full, red_bar;
   __shared__ __align__(8) uint64_t a_full[kBgSubStages], a_empty[kBgSubStages];
   __shared__ uint32_t tmem_base;
-  __shared__ float red_ss[64];               // per-warp sums of squares of the outputs
+  __shared__ float red_ss[2 * NPAD];         // per-warp sums of squares of the outputs
+  constexpr int kRPre = 8;                   // residuals of a thread staged before the shares
+  __shared__ uint16_t rstage[MODE == kBgResid ? kRPre * 256 : 1];
   __shared__ float rs_b[kBMaxBatch];         // 1 / RMS of the rows (folded norm)
   __shared__ float rs_g[2][kBMaxBatch];      // their partial sums of squares
   const bool fold = a.ssq_in != nullptr;
@@ -348,8 +351,11 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
       if (t < kBMaxBatch)
         rs_b[t] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(__fadd_rn(rs_g[0][t], rs_g[1][t]), (float)a.K), kEps)));
     }
-    // ------------------------------------------------ accumulators out of TMEM (warps 2-5)
-    if (warp < 6) {
+    // ------------------------------------------------ accumulators out of TMEM
+    // (warps 2-5 for the direct epilogue; with splits all 8 dequant warps:
+    // warp w reads TMEM lanes 32*(w%4).. of every 16-column group, warps 2-5
+    // the even groups and warps 6-9 the odd ones)
+    if (warp < 6 || splits > 1) {
       const bool have = Q3_BWAIT(&acc_full, 0, kErrTimeoutFull, 10);
       bphase(a.phase, 4, threadIdx.x == 64);  // accumulators complete
       tc_fence_after();
@@ -380,24 +386,32 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
           }
         }
       } else if (splits > 1) {
-        // partial [acc][b][row] f32 over the (now idle) raw weight stages
+        // partial [acc][b][row] f32 over the (now idle) raw weight stages:
+        // group g = TMEM columns 16g.. = (acc, b) columns acc*NPAD + 16g'..;
+        // this warp's groups are all loaded before one wait
+        constexpr int NG = NACC * NPAD / 16, NGH = (NG + 1) / 2;
+        const int half = (warp - 2) >> 2;
+        uint32_t v[NGH][16];
+        const bool all = __all_sync(0xffffffffu, have);  // TMEM loads are warp-wide
 #pragma unroll
-        for (int acc = 0; acc < NACC; ++acc) {
+        for (int k = 0; k < NGH; ++k) {
+          if (2 * k + half >= NG) continue;
+          if (all) {
+            tmem_ld16(tmem + lane_base + (uint32_t)((2 * k + half) * 16), v[k]);
+          } else {
 #pragma unroll
-          for (int col0 = 0; col0 < NPAD; col0 += 16) {
-            uint32_t v[16];
-            if (have) {
-              tmem_ld16(tmem + lane_base + acc * NPAD + col0, v);
-              tmem_wait_ld();
-            } else {
+            for (int j = 0; j < 16; ++j) v[k][j] = 0u;
+          }
+        }
+        if (all) tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = 0u;
-            }
+        for (int k = 0; k < NGH; ++k) {
+          const int g = 2 * k + half;
+          if (g < NG) {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              asm volatile("st.shared.b32 [%0], %1;" ::"r"(
-                               sR + (uint32_t)(((acc * NPAD + col0 + j) * 128 + (int)r) * 4)),
-                           "r"(v[j])
+              asm volatile("st.shared.b32 [%0], %1;" ::"r"(sR + (uint32_t)(((g * 16 + j) * 128 + (int)r) * 4)),
+                           "r"(v[k][j])
                            : "memory");
           }
         }
@@ -431,43 +445,59 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
                         smem_u32(&red_bar));
           }
       }
-      const bool got = Q3_BWAIT(&red_bar, 0, kErrTimeoutFull, 11);
-      bphase(a.phase, 6, threadIdx.x == 64);  // this CTA's shares arrived
       pdl_wait();  // reads the residual stream / writes buffers of earlier kernels
       const int i0 = me * per;
       const int i1 = i0 + per < total ? i0 + per : total;
+      // every item i0 + 256 jj + t of thread t lies in output row n (i0 and
+      // the 256-item stride are whole 128-row blocks)
+      const int n = n0 + (t & 127);
+      if (MODE == kBgResid) {
+        // the residuals of this thread's first kRPre items: the loads in
+        // flight together while the shares travel, kept for this thread
+        uint16_t rv[kRPre];
+#pragma unroll
+        for (int jj = 0; jj < kRPre; ++jj) {
+          const int i = i0 + jj * 256 + t;
+          rv[jj] = (i < i1 && (i >> 7) < a.B) ? a.r[(int64_t)(i >> 7) * a.ldy + n] : (uint16_t)0;
+        }
+#pragma unroll
+        for (int jj = 0; jj < kRPre; ++jj) rstage[jj * 256 + t] = rv[jj];
+      }
+      const bool got = Q3_BWAIT(&red_bar, 0, kErrTimeoutFull, 11);
+      bphase(a.phase, 6, threadIdx.x == 64);  // this CTA's shares arrived
       const bool want_ss = MODE == kBgResid && a.ssq_out != nullptr;
+      const float gam = MODE == kBgResid && a.xg_out != nullptr ? h2f(a.xg_gamma[n]) : 0.0f;
       for (int jj = 0; i0 + jj * 256 < i1; ++jj) {  // uniform over the 256 threads
         const int i = i0 + jj * 256 + t;
-        const int b = i >> 7, row = i & 127;
+        const int b = i >> 7;
         float sq = 0.0f;
         if (got && i < i1 && b < a.B) {
-        float sum[NACC];
+          float sum[NACC];
 #pragma unroll
-        for (int acc = 0; acc < NACC; ++acc) {
-          float s0 = 0.0f;
-          for (int sp = 0; sp < splits; ++sp) {
-            float v;
-            asm volatile("ld.shared.f32 %0, [%1];"
-                         : "=f"(v)
-                         : "r"(sA + (uint32_t)(((sp * NACC + acc) * per + (i - i0)) * 4)));
-            s0 = sp == 0 ? v : __fadd_rn(s0, v);
+          for (int acc = 0; acc < NACC; ++acc) {
+            float s0 = 0.0f;
+            for (int sp = 0; sp < splits; ++sp) {
+              float v;
+              asm volatile("ld.shared.f32 %0, [%1];"
+                           : "=f"(v)
+                           : "r"(sA + (uint32_t)(((sp * NACC + acc) * per + (i - i0)) * 4)));
+              s0 = sp == 0 ? v : __fadd_rn(s0, v);
+            }
+            sum[acc] = fold ? __fmul_rn(s0, rs_b[b]) : s0;
           }
-          sum[acc] = fold ? __fmul_rn(s0, rs_b[b]) : s0;
-        }
-        const int n = n0 + row;
-        uint16_t out;
-        if (MODE == kBgSwiglu)
-          out = swiglu_h(f2h(sum[0]), f2h(sum[NACC - 1]));
-        else if (MODE == kBgResid)
-          out = f2h(__fadd_rn(h2f(a.r[(int64_t)b * a.ldy + n]), h2f(f2h(sum[0]))));
-        else
-          out = f2h(sum[0]);
-        a.y[(int64_t)b * a.ldy + n] = out;
+          uint16_t out;
+          if (MODE == kBgSwiglu)
+            out = swiglu_h(f2h(sum[0]), f2h(sum[NACC - 1]));
+          else if (MODE == kBgResid)
+            out = f2h(__fadd_rn(h2f(jj < kRPre ? rstage[jj * 256 + t] : a.r[(int64_t)b * a.ldy + n]),
+                                h2f(f2h(sum[0]))));
+          else
+            out = f2h(sum[0]);
+          a.y[(int64_t)b * a.ldy + n] = out;
           const float ov = h2f(out);
           sq = __fmul_rn(ov, ov);
           if (MODE == kBgResid && a.xg_out != nullptr)
-            a.xg_out[(int64_t)b * a.ldy + n] = f2h(__fmul_rn(ov, h2f(a.xg_gamma[n])));
+            a.xg_out[(int64_t)b * a.ldy + n] = f2h(__fmul_rn(ov, gam));
         }
         if (want_ss) {  // a warp's 32 items lie in one row b
           sq = warp_sum(sq);
@@ -494,12 +524,15 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  bphase(a.phase, 7, threadIdx.x == 0);  // end
+  // The end stamps come from warp 1 after it frees TMEM: per-CTA stamps show
+  // warp 1 leaving this barrier only after the epilogue warps reach it, but
+  // thread 0 leaving it 1.5-7 us before them (warp 0 has nothing left to do)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TCOLS);
   }
-  ktrace_end(a.trace);
+  bphase(a.phase, 7, threadIdx.x == 32);  // end
+  ktrace_end(a.trace, 32);
 }
 
 // Per-sequence RMSNorm of model/qwen3_full.mlir:134-165 into the GEMM operand

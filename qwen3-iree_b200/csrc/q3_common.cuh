@@ -231,8 +231,8 @@ __device__ __forceinline__ void ktrace_release(unsigned long long* t) {
     atomicMax(t + 2, n);
   }
 }
-__device__ __forceinline__ void ktrace_end(unsigned long long* t) {
-  if (t != nullptr && threadIdx.x == 0) {
+__device__ __forceinline__ void ktrace_end(unsigned long long* t, unsigned tid = 0) {
+  if (t != nullptr && threadIdx.x == tid) {
     const unsigned long long n = gtimer_ns();
     atomicMax(t + 3, n);
     atomicMin(t + 5, n);
