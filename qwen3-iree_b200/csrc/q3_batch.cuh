@@ -438,11 +438,17 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
         const int i0 = dst * per;
         const int len = i0 >= total ? 0 : (total - i0 < per ? total - i0 : per);
         for (int acc = 0; acc < NACC; ++acc)
-          for (int j4 = t; j4 < len / 4; j4 += 32 * kBgDqWarps) {
-            uint4 v;
+          for (int j4 = t; j4 < len / 4; j4 += 2 * 32 * kBgDqWarps) {  // two loads, then two pushes
+            const bool two = j4 + 32 * kBgDqWarps < len / 4;
+            uint4 v, w;
             lds128(sR + (uint32_t)(((acc * total) + i0 + 4 * j4) * 4), v.x, v.y, v.z, v.w);
+            if (two)
+              lds128(sR + (uint32_t)(((acc * total) + i0 + 4 * (j4 + 32 * kBgDqWarps)) * 4), w.x, w.y, w.z, w.w);
             st_async_v4(sA + (uint32_t)(((me * NACC + acc) * per + 4 * j4) * 4), (uint32_t)dst, v,
                         smem_u32(&red_bar));
+            if (two)
+              st_async_v4(sA + (uint32_t)(((me * NACC + acc) * per + 4 * (j4 + 32 * kBgDqWarps)) * 4),
+                          (uint32_t)dst, w, smem_u32(&red_bar));
           }
       }
       pdl_wait();  // reads the residual stream / writes buffers of earlier kernels
@@ -475,14 +481,19 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemm_q8(const __grid_constan
           float sum[NACC];
 #pragma unroll
           for (int acc = 0; acc < NACC; ++acc) {
-            float s0 = 0.0f;
-            for (int sp = 0; sp < splits; ++sp) {
-              float v;
-              asm volatile("ld.shared.f32 %0, [%1];"
-                           : "=f"(v)
-                           : "r"(sA + (uint32_t)(((sp * NACC + acc) * per + (i - i0)) * 4)));
-              s0 = sp == 0 ? v : __fadd_rn(s0, v);
+            // the shares' loads issued together, then summed in split order
+            float v[kBgMaxSplits];
+#pragma unroll
+            for (int sp = 0; sp < kBgMaxSplits; ++sp) {
+              if (sp < splits)
+                asm volatile("ld.shared.f32 %0, [%1];"
+                             : "=f"(v[sp])
+                             : "r"(sA + (uint32_t)(((sp * NACC + acc) * per + (i - i0)) * 4)));
             }
+            float s0 = v[0];
+#pragma unroll
+            for (int sp = 1; sp < kBgMaxSplits; ++sp)
+              if (sp < splits) s0 = __fadd_rn(s0, v[sp]);
             sum[acc] = fold ? __fmul_rn(s0, rs_b[b]) : s0;
           }
           uint16_t out;
