@@ -852,19 +852,63 @@ __global__ void __launch_bounds__(kBvThreads, 1) k_bvocab(const __grid_constant_
   ktrace_end(a.trace);
   if (!is_last) return;
   __threadfence();
-  if (threadIdx.x < a.B) {
-    const int b = threadIdx.x;
+  // The candidates of every CTA, [c][b] for b < B, brought into the (now
+  // idle) dynamic shared memory by all threads' 16-byte cp.async at once;
+  // thread (b, g) then scans CTAs c = g mod 3 and thread b folds the three
+  // (any order: am_better is a total order).
+  const int nc = (int)gridDim.x;
+  uint8_t* const stage = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
+  const bool staged = (size_t)nc * NPAD * sizeof(ArgmaxPartial) <= bvocab_smem_bytes(NPAD) - 1024 - 256 &&
+                      (reinterpret_cast<uintptr_t>(a.part) & 15) == 0;
+  if (staged) {
+    for (int f = threadIdx.x; f < nc * NPAD; f += kBvThreads) {
+      const int c = f / NPAD, b = f - c * NPAD;
+      if (b < a.B)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(stage + (size_t)f * 16)),
+                     "l"(a.part + (int64_t)c * kBMaxBatch + b)
+                     : "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  }
+  __syncthreads();
+  constexpr int kGroups = kBvThreads / 64;
+  {
+    const int b = threadIdx.x & 63, g = threadIdx.x >> 6;
     float v = -__int_as_float(0x7f800000);
     int64_t ii = -1;
-    for (int c = 0; c < (int)gridDim.x; ++c) {
-      const ArgmaxPartial* p = a.part + (int64_t)c * kBMaxBatch + b;
-      const float pv = __ldcg(&p->v);
-      const int64_t pi = __ldcg(reinterpret_cast<const long long*>(&p->i));
-      if (am_better(pv, pi, v, ii)) {
-        v = pv;
-        ii = pi;
+    if (b < a.B) {
+      for (int c = g; c < nc; c += kGroups) {
+        float pv;
+        int64_t pi;
+        if (staged) {
+          const ArgmaxPartial* p = reinterpret_cast<const ArgmaxPartial*>(stage + (size_t)(c * NPAD + b) * 16);
+          pv = p->v;
+          pi = p->i;
+        } else {
+          const ArgmaxPartial* p = a.part + (int64_t)c * kBMaxBatch + b;
+          pv = __ldcg(&p->v);
+          pi = __ldcg(reinterpret_cast<const long long*>(&p->i));
+        }
+        if (am_better(pv, pi, v, ii)) {
+          v = pv;
+          ii = pi;
+        }
       }
+      wbv[g][b] = v;
+      wbi[g][b] = ii;
     }
+  }
+  __syncthreads();
+  if (threadIdx.x < a.B) {
+    const int b = threadIdx.x;
+    float v = wbv[0][b];
+    int64_t ii = wbi[0][b];
+#pragma unroll
+    for (int g = 1; g < kGroups; ++g)
+      if (am_better(wbv[g][b], wbi[g][b], v, ii)) {
+        v = wbv[g][b];
+        ii = wbi[g][b];
+      }
     if (a.token_out != nullptr) a.token_out[b] = ii;
     if (a.seq != nullptr) {
       BatchSeq& s = a.seq[b];
