@@ -636,14 +636,31 @@ __global__ void __launch_bounds__(kBaThreads, kBaCtasPerSm) k_battn(const __grid
         ll[hh] = 0.0f;
         oo[hh][0] = oo[hh][1] = oo[hh][2] = oo[hh][3] = 0.0f;
       }
-      for (int gg = g1; gg <= g2; ++gg) {
-        const int sg = (gg == g1 && pc.s0 > lo1) ? 1 : 0;
+      for (int gg = g1; gg <= g2; gg += 2) {
+        // two CTAs' partials loaded before either is merged (CTA order kept)
+        const bool two = gg + 1 <= g2;
+        float4 t4[2][2];
+        float pm[2][2], pl[2][2];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const AttnPartial* q = a.part + ((int64_t)gg * 2 + sg) * 2 + hh;
-          const float4 t4 = __ldcg(reinterpret_cast<const float4*>(&q->o[4 * lane]));
-          const float ob[4] = {t4.x, t4.y, t4.z, t4.w};
-          battn_merge_state(mm[hh], ll[hh], oo[hh], __ldcg(&q->m), __ldcg(&q->l), ob);
+        for (int k = 0; k < 2; ++k) {
+          if (k == 1 && !two) break;
+          const int sg = (gg + k == g1 && pc.s0 > lo1) ? 1 : 0;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const AttnPartial* q = a.part + ((int64_t)(gg + k) * 2 + sg) * 2 + hh;
+            t4[k][hh] = __ldcg(reinterpret_cast<const float4*>(&q->o[4 * lane]));
+            pm[k][hh] = __ldcg(&q->m);
+            pl[k][hh] = __ldcg(&q->l);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (k == 1 && !two) break;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const float ob[4] = {t4[k][hh].x, t4[k][hh].y, t4[k][hh].z, t4[k][hh].w};
+            battn_merge_state(mm[hh], ll[hh], oo[hh], pm[k][hh], pl[k][hh], ob);
+          }
         }
       }
     }
