@@ -1001,16 +1001,40 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
   ktrace_end(a.trace);
   if (!is_last) return;
   __threadfence();
-  // last CTA: reduce the per-CTA partials (any order: the rule is a total order)
+  // the decode state, loaded by thread 0 now (its loads in flight with the
+  // partials'; only this thread changes it during the launch)
+  int64_t s_pos = 0, s_prompt = 0, s_gen = 0, s_max = 0, s_eos = 0;
+  if (threadIdx.x == 0 && a.seq != nullptr) {
+    const volatile SeqState* vs = a.seq;
+    s_pos = vs->pos;
+    s_prompt = vs->n_prompt;
+    s_gen = vs->n_gen;
+    s_max = vs->max_gen;
+    s_eos = vs->eos;
+  }
+  // last CTA: reduce the per-CTA partials (any order: the rule is a total
+  // order); a thread's two partials are loaded before either is compared
   float bv = -__int_as_float(0x7f800000);
   int64_t bi = -1;
-  for (int c = threadIdx.x; c < (int)gridDim.x; c += blockDim.x) {
+  const int nc = (int)gridDim.x, nt = (int)blockDim.x;
+  for (int c = threadIdx.x; c < nc; c += 2 * nt) {
     const volatile ArgmaxPartial* p = a.partial + c;
     const float v = p->v;
     const int64_t ii = p->i;
+    const bool two = c + nt < nc;
+    float v2 = -__int_as_float(0x7f800000);
+    int64_t i2 = -1;
+    if (two) {
+      v2 = p[nt].v;
+      i2 = p[nt].i;
+    }
     if (am_better(v, ii, bv, bi)) {
       bv = v;
       bi = ii;
+    }
+    if (two && am_better(v2, i2, bv, bi)) {
+      bv = v2;
+      bi = i2;
     }
   }
 #pragma unroll
@@ -1036,7 +1060,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
     if (a.token_out != nullptr) *a.token_out = bi;
     if (a.seq != nullptr) {
       SeqState* st = a.seq;
-      const int64_t pos = st->pos;
+      const int64_t pos = s_pos;
       if (pos < 0 || pos >= a.S) {  // a corrupted state: report it, write nothing
         if (a.err) atomicCAS(a.err, 0, kErrBadPos);
         st->stop = 1;
@@ -1044,11 +1068,12 @@ __global__ void __launch_bounds__(kGemvThreads) k_vocab_argmax(const __grid_cons
         return;
       }
       a.tokens[pos + 1] = bi;
-      if (pos >= st->n_prompt) {
-        st->n_gen += 1;
+      if (pos >= s_prompt) {
+        const int64_t n_gen = s_gen + 1;
+        st->n_gen = n_gen;
         // @generate (model/qwen3_full.mlir:1412-1530): groups of 4; the loop
         // ends when the last token of a group is eos, or max_gen is reached.
-        if (st->n_gen >= st->max_gen || ((st->n_gen % 4) == 0 && bi == st->eos)) st->stop = 1;
+        if (n_gen >= s_max || ((n_gen % 4) == 0 && bi == s_eos)) st->stop = 1;
       }
       st->pos = pos + 1;
     }
