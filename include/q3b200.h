@@ -400,7 +400,9 @@ int q3_bgemm_q8(const void* w, int64_t w_rows, int64_t row0, const void* x, void
                 const void* r, int B, int N, int K, int mode, int ksplit, void* stream);
 /* Batched vocab GEMV + argmax (model/qwen3_full.mlir:1456-1509 per row):
  * logits[b][N] (optional, f16) and tokens[b] = first index of the largest f16
- * logit of xn[b] (xn already normalised).  Workspace zero-filled once. */
+ * logit of xn[b] (xn already normalised).  Workspace zero-filled once,
+ * 8-byte aligned (16-byte alignment lets the last CTA copy the per-CTA
+ * candidates with cp.async; otherwise it loads them directly). */
 size_t q3_bvocab_workspace_bytes(void);
 int q3_bvocab_argmax(const void* w, int N, const void* xn, int B, void* logits, int64_t* tokens,
                      void* ws, void* stream);

@@ -148,6 +148,36 @@ def test_bvocab_ties_pick_lowest_index(gpu):
     assert (dt.download() == 3).all()
 
 
+def test_bvocab_workspace_alignment(gpu):
+    """A 16-byte-aligned workspace lets the last CTA stage the per-CTA
+    candidates in shared memory; an 8-byte-aligned one takes the direct-load
+    path.  Both must give the same logits and tokens, call after call; a
+    workspace below 8-byte alignment is refused before any launch."""
+    L = gpu.lib()
+    N, B = 128 * 512, 32
+    rng = np.random.default_rng(9)
+    W = (rng.standard_normal((N, 1024)) * 0.02).astype(np.float16)
+    xn = rng.standard_normal((B, 1024)).astype(np.float16)
+    dW, dx = _up(gpu, W), _up(gpu, xn)
+    ws = gpu.DeviceArray((L.q3_bvocab_workspace_bytes() + 16,), np.uint8, zero=True)
+    assert ws.ptr % 16 == 0
+    dl, dt = gpu.DeviceArray((B, N), np.float16), gpu.DeviceArray((B,), np.int64)
+    out = {}
+    for off in (0, 8, 0, 8):
+        dt.fill_bytes(0xEE)
+        assert L.q3_bvocab_argmax(dW.ptr, N, dx.ptr, B, dl.ptr, dt.ptr, ws.ptr + off, None) == 0, \
+            L.q3_last_error()
+        gpu.synchronize(None)
+        logits, tok = dl.download(), dt.download()
+        if off in out:
+            assert np.array_equal(out[off][1], tok)
+        out[off] = (logits, tok)
+    assert np.array_equal(out[0][0].view(np.uint16), out[8][0].view(np.uint16))
+    assert np.array_equal(out[0][1], out[8][1])
+    assert np.array_equal(out[0][1], np.argmax(out[0][0].astype(np.float32), axis=1))
+    assert L.q3_bvocab_argmax(dW.ptr, N, dx.ptr, B, dl.ptr, dt.ptr, ws.ptr + 4, None) == 1
+
+
 def test_batch_attention_vs_oracle(gpu, O):
     """The batched attention kernel against the oracle's attention, one
     sequence per position class: single chunk, chunk boundaries, one and
