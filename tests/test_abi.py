@@ -81,6 +81,8 @@ def test_argument_errors_are_statuses(q3):
     assert L.q3_run(None, p, 1, 1, 0, p, None) == 1
     assert L.q3_gemv_q8_layers(p, 16, p, p, 8, 256, 0, None) == 1
     assert L.q3_quantize_q8_0(p, 33, p) == 1
+    assert L.q3_bvocab_argmax(p, 128, p, 1, None, p, p + 4, None) == 1  # workspace below 8 bytes
+    assert b"8-byte aligned" in L.q3_last_error()
     assert L.q3_strerror(3).startswith(b"kernel reported")
 
 
